@@ -1,0 +1,1 @@
+"""CPU oracle for the attention hot path: test infrastructure only (see oracle.py)."""

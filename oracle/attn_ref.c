@@ -1,0 +1,522 @@
+/*
+ * attn_ref.c -- CPU restatement of the reference engine's attention hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY (see attn_ref.h): the parity oracle and the timed
+ * CPU baseline, never part of the product path.
+ *
+ * Every function cites the reference file:line it restates. Compile with
+ * -ffp-contract=off: JavaScript evaluates a*b+c as two rounded f64 operations.
+ */
+#include "attn_ref.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#if defined(__FP_FAST_FMA) && !defined(B2A_ALLOW_FMA)
+/* Not an error by itself (the macro only says fma() is fast), but this file
+ * must be built with -ffp-contract=off; the Makefile does that. */
+#endif
+
+static inline uint32_t f32_bits(float x) { uint32_t u; memcpy(&u, &x, 4); return u; }
+static inline float bits_f32(uint32_t u) { float x; memcpy(&x, &u, 4); return x; }
+
+/* ---------------------------------------------------------------- dtype ---- */
+
+/* src/core/dtype.js:17-20 -- bf16 is the top half of an f32. */
+float or_bf16_to_f32(uint16_t bits) { return bits_f32((uint32_t)bits << 16); }
+
+/* src/core/dtype.js:23-35 -- round to nearest even; NaN kept NaN with a quiet bit. */
+uint16_t or_f32_to_bf16(float x) {
+  uint32_t u = f32_bits(x);
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu) != 0) {
+    return (uint16_t)(((u >> 16) | 0x0040u) & 0xffffu);
+  }
+  uint32_t lsb = (u >> 16) & 1u;
+  return (uint16_t)(((uint64_t)u + 0x7fffu + lsb) >> 16);
+}
+
+/* src/core/dtype.js:55-78 */
+float or_f16_to_f32(uint16_t bits) {
+  uint32_t sign = ((uint32_t)bits & 0x8000u) << 16;
+  uint32_t exp = (bits >> 10) & 0x1fu;
+  uint32_t mant = bits & 0x3ffu;
+  uint32_t out;
+  if (exp == 0x1f) {
+    out = sign | 0x7f800000u | (mant << 13);
+  } else if (exp == 0) {
+    if (mant == 0) {
+      out = sign;
+    } else {
+      int e = -1;
+      uint32_t m = mant;
+      do { m <<= 1; e++; } while ((m & 0x400u) == 0);
+      out = sign | ((uint32_t)(127 - 15 - e) << 23) | ((m & 0x3ffu) << 13);
+    }
+  } else {
+    out = sign | ((exp - 15 + 127) << 23) | (mant << 13);
+  }
+  return bits_f32(out);
+}
+
+/* src/core/dtype.js:81-113 -- RNE, overflow to inf, gradual underflow. */
+uint16_t or_f32_to_f16(float x) {
+  uint32_t u = f32_bits(x);
+  uint32_t sign = (u >> 16) & 0x8000u;
+  int exp = (int)((u >> 23) & 0xffu);
+  uint32_t mant = u & 0x7fffffu;
+  if (exp == 0xff) {
+    return (uint16_t)(sign | 0x7c00u | (mant != 0 ? ((mant >> 13) | 0x200u) : 0u));
+  }
+  int e = exp - 127 + 15;
+  if (e >= 0x1f) return (uint16_t)(sign | 0x7c00u);
+  if (e <= 0) {
+    if (e < -10) return (uint16_t)sign;
+    uint32_t m = mant | 0x800000u;
+    int shift = 14 - e;
+    uint32_t half = 1u << (shift - 1);
+    uint32_t lsb = (m >> shift) & 1u;
+    return (uint16_t)(sign | ((m + half - 1 + lsb) >> shift));
+  }
+  uint32_t lsb = (mant >> 13) & 1u;
+  uint32_t rounded = mant + 0x0fffu + lsb;
+  return (uint16_t)(sign | (((uint32_t)e << 10) + (rounded >> 13)));
+}
+
+void or_f32_to_f16_array(const float* src, uint16_t* dst, size_t n) {
+  for (size_t i = 0; i < n; i++) dst[i] = or_f32_to_f16(src[i]);
+}
+void or_f16_to_f32_array(const uint16_t* src, float* dst, size_t n) {
+  for (size_t i = 0; i < n; i++) dst[i] = or_f16_to_f32(src[i]);
+}
+void or_f32_to_bf16_array(const float* src, uint16_t* dst, size_t n) {
+  for (size_t i = 0; i < n; i++) dst[i] = or_f32_to_bf16(src[i]);
+}
+void or_bf16_to_f32_array(const uint16_t* src, float* dst, size_t n) {
+  for (size_t i = 0; i < n; i++) dst[i] = or_bf16_to_f32(src[i]);
+}
+
+/* ------------------------------------------------------------------ ops ---- */
+
+/* src/core/ops.js:66-78. max over f32, exp in f64 stored to f32, the sum of
+ * the unrounded f64 exps, then x = f32(x * (1/sum)). */
+void or_softmax_inplace(float* x, int n) {
+  float max = -INFINITY;
+  for (int i = 0; i < n; i++) if (x[i] > max) max = x[i];
+  double sum = 0.0;
+  for (int i = 0; i < n; i++) {
+    double e = exp((double)x[i] - (double)max);
+    x[i] = (float)e;
+    sum += e;
+  }
+  double inv = 1.0 / sum;
+  for (int i = 0; i < n; i++) x[i] = (float)((double)x[i] * inv);
+}
+
+/* src/core/ops.js:99-104 -- inv_freq[j] = theta^(-2j/headDim). */
+void or_rope_frequencies(int head_dim, double theta, double* inv_freq) {
+  int half = head_dim >> 1;
+  for (int j = 0; j < half; j++) inv_freq[j] = pow(theta, (double)(-2 * j) / (double)head_dim);
+}
+
+/* src/core/ops.js:123-136 -- f32 tables computed in f64. */
+void or_rope_tables(int head_dim, double theta, int positions, float* cos_out, float* sin_out) {
+  int half = head_dim >> 1;
+  double* inv = (double*)malloc(sizeof(double) * (size_t)(half > 0 ? half : 1));
+  or_rope_frequencies(head_dim, theta, inv);
+  for (int p = 0; p < positions; p++) {
+    for (int j = 0; j < half; j++) {
+      double angle = (double)p * inv[j];
+      cos_out[(size_t)p * half + j] = (float)cos(angle);
+      sin_out[(size_t)p * half + j] = (float)sin(angle);
+    }
+  }
+  free(inv);
+}
+
+/* The f64 angles of ops.js:147-152 (angle = position * invFreq[j]) tabulated
+ * without the f32 rounding of ropeTables: exactly the cos/sin ropeInPlace
+ * evaluates for that position. */
+void or_rope_tables_f64(int head_dim, double theta, int positions, double* cos_out, double* sin_out) {
+  int half = head_dim >> 1;
+  double* inv = (double*)malloc(sizeof(double) * (size_t)(half > 0 ? half : 1));
+  or_rope_frequencies(head_dim, theta, inv);
+  for (int p = 0; p < positions; p++) {
+    for (int j = 0; j < half; j++) {
+      double angle = (double)p * inv[j];
+      cos_out[(size_t)p * half + j] = cos(angle);
+      sin_out[(size_t)p * half + j] = sin(angle);
+    }
+  }
+  free(inv);
+}
+
+/* src/core/ops.js:147-158 -- half-split rotation in f64, stored to f32. */
+void or_rope_inplace(float* vec, int offset, int head_dim, int position, const double* inv_freq) {
+  int half = head_dim >> 1;
+  for (int j = 0; j < half; j++) {
+    double angle = (double)position * inv_freq[j];
+    double c = cos(angle);
+    double s = sin(angle);
+    double lo = vec[offset + j];
+    double hi = vec[offset + j + half];
+    vec[offset + j] = (float)(lo * c - hi * s);
+    vec[offset + j + half] = (float)(hi * c + lo * s);
+  }
+}
+
+/* ------------------------------------------------------------ attention ---- */
+
+/* src/core/attention.js:74-76 -- the blocked mapping. */
+int or_kv_head_for(int query_head, int num_heads, int num_kv_heads) {
+  return query_head / (num_heads / num_kv_heads);
+}
+
+/* src/core/attention.js:32-66. f64 dot of f32 operands, score stored to f32,
+ * softmax (ops.js:66-78), then out = f32(out + f64(p * v)) in key order. */
+void or_grouped_attention(const float* q, const float* keys, const float* values,
+                          float* out, float* scores, int seq, int past,
+                          int num_heads, int num_kv_heads, int head_dim) {
+  int group = num_heads / num_kv_heads;
+  int q_dim = num_heads * head_dim;
+  int kv_dim = num_kv_heads * head_dim;
+  double scale = 1.0 / sqrt((double)head_dim);
+  memset(out, 0, sizeof(float) * (size_t)seq * q_dim);
+  for (int h = 0; h < num_heads; h++) {
+    int kv_base = (h / group) * head_dim;
+    for (int t = 0; t < seq; t++) {
+      int q_base = t * q_dim + h * head_dim;
+      int up_to = past + t;
+      for (int s = 0; s <= up_to; s++) {
+        size_t k_base = (size_t)s * kv_dim + kv_base;
+        double dot = 0.0;
+        for (int i = 0; i < head_dim; i++) dot += (double)q[q_base + i] * (double)keys[k_base + i];
+        scores[s] = (float)(dot * scale);
+      }
+      or_softmax_inplace(scores, up_to + 1);
+      int out_base = t * q_dim + h * head_dim;
+      for (int s = 0; s <= up_to; s++) {
+        double w = scores[s];
+        size_t v_base = (size_t)s * kv_dim + kv_base;
+        for (int i = 0; i < head_dim; i++) {
+          out[out_base + i] = (float)((double)out[out_base + i] + w * (double)values[v_base + i]);
+        }
+      }
+    }
+  }
+}
+
+/* test/attention.test.js:15-58 -- repeat each KV head groupSize times, then
+ * plain multi-head attention. */
+void or_expanded_attention(const float* q, const float* keys, const float* values,
+                           float* out, int seq, int past,
+                           int num_heads, int num_kv_heads, int head_dim) {
+  int group = num_heads / num_kv_heads;
+  int q_dim = num_heads * head_dim;
+  int kv_dim = num_kv_heads * head_dim;
+  int total = past + seq;
+  float* wk = (float*)malloc(sizeof(float) * (size_t)total * q_dim);
+  float* wv = (float*)malloc(sizeof(float) * (size_t)total * q_dim);
+  float* scores = (float*)malloc(sizeof(float) * (size_t)(total > 0 ? total : 1));
+  for (int s = 0; s < total; s++) {
+    for (int h = 0; h < num_heads; h++) {
+      size_t from = (size_t)s * kv_dim + (size_t)(h / group) * head_dim;
+      size_t to = (size_t)s * q_dim + (size_t)h * head_dim;
+      for (int i = 0; i < head_dim; i++) { wk[to + i] = keys[from + i]; wv[to + i] = values[from + i]; }
+    }
+  }
+  memset(out, 0, sizeof(float) * (size_t)seq * q_dim);
+  double scale = 1.0 / sqrt((double)head_dim);
+  for (int h = 0; h < num_heads; h++) {
+    for (int t = 0; t < seq; t++) {
+      int up_to = past + t;
+      int q_base = t * q_dim + h * head_dim;
+      for (int s = 0; s <= up_to; s++) {
+        double dot = 0.0;
+        size_t k_base = (size_t)s * q_dim + (size_t)h * head_dim;
+        for (int i = 0; i < head_dim; i++) dot += (double)q[q_base + i] * (double)wk[k_base + i];
+        scores[s] = (float)(dot * scale);
+      }
+      or_softmax_inplace(scores, up_to + 1);
+      int out_base = t * q_dim + h * head_dim;
+      for (int s = 0; s <= up_to; s++) {
+        size_t v_base = (size_t)s * q_dim + (size_t)h * head_dim;
+        for (int i = 0; i < head_dim; i++) {
+          out[out_base + i] = (float)((double)out[out_base + i] + (double)scores[s] * (double)wv[v_base + i]);
+        }
+      }
+    }
+  }
+  free(wk); free(wv); free(scores);
+}
+
+/* ------------------------------------------------------------- KV cache ---- */
+
+struct or_kvcache {
+  int num_layers, kv_dim, capacity, length;
+  float** keys;
+  float** values;
+};
+
+/* src/cpu/cache.js:23-35 */
+or_kvcache* or_kvcache_new(int num_layers, int kv_dim, int capacity, char* err, size_t errlen) {
+  if (capacity < 1) {
+    if (err) snprintf(err, errlen, "cache capacity must be a positive integer, got %d", capacity);
+    return NULL;
+  }
+  or_kvcache* c = (or_kvcache*)calloc(1, sizeof(or_kvcache));
+  c->num_layers = num_layers;
+  c->kv_dim = kv_dim;
+  c->capacity = capacity;
+  c->keys = (float**)calloc((size_t)num_layers, sizeof(float*));
+  c->values = (float**)calloc((size_t)num_layers, sizeof(float*));
+  for (int l = 0; l < num_layers; l++) {
+    c->keys[l] = (float*)calloc((size_t)capacity * kv_dim, sizeof(float));
+    c->values[l] = (float*)calloc((size_t)capacity * kv_dim, sizeof(float));
+  }
+  return c;
+}
+
+void or_kvcache_free(or_kvcache* c) {
+  if (!c) return;
+  for (int l = 0; l < c->num_layers; l++) { free(c->keys[l]); free(c->values[l]); }
+  free(c->keys); free(c->values); free(c);
+}
+
+int or_kvcache_length(const or_kvcache* c) { return c->length; }
+int or_kvcache_capacity(const or_kvcache* c) { return c->capacity; }
+
+/* src/cpu/cache.js:41-43 */
+size_t or_kvcache_byte_length(const or_kvcache* c) {
+  return (size_t)c->num_layers * c->capacity * c->kv_dim * 4 * 2;
+}
+
+/* src/cpu/cache.js:52-60 */
+int or_kvcache_allocate(or_kvcache* c, int count, char* err, size_t errlen) {
+  if (c->length + count > c->capacity) {
+    if (err) snprintf(err, errlen, "cache holds %d of %d positions; cannot add %d more",
+                      c->length, c->capacity, count);
+    return -1;
+  }
+  return c->length;
+}
+
+/* src/cpu/cache.js:63-67 */
+void or_kvcache_write_at(or_kvcache* c, int layer, int at, const float* keys,
+                         const float* values, int count) {
+  memcpy(c->keys[layer] + (size_t)at * c->kv_dim, keys, sizeof(float) * (size_t)count * c->kv_dim);
+  memcpy(c->values[layer] + (size_t)at * c->kv_dim, values, sizeof(float) * (size_t)count * c->kv_dim);
+}
+
+/* src/cpu/cache.js:75-81 -- views; n is the caller's horizon (may exceed length). */
+const float* or_kvcache_keys_up_to(const or_kvcache* c, int layer, int n) { (void)n; return c->keys[layer]; }
+const float* or_kvcache_values_up_to(const or_kvcache* c, int layer, int n) { (void)n; return c->values[layer]; }
+
+/* src/cpu/cache.js:84-86 */
+void or_kvcache_commit(or_kvcache* c, int count) { c->length += count; }
+
+/* src/cpu/cache.js:97-115 -- [kvHeads, length, headDim]. */
+void or_kvcache_present(const or_kvcache* c, int layer, int num_kv_heads, int head_dim,
+                        float* key_out, float* value_out) {
+  int n = c->length;
+  const float* k = c->keys[layer];
+  const float* v = c->values[layer];
+  for (int h = 0; h < num_kv_heads; h++) {
+    for (int t = 0; t < n; t++) {
+      size_t from = (size_t)t * c->kv_dim + (size_t)h * head_dim;
+      size_t to = ((size_t)h * n + t) * head_dim;
+      for (int i = 0; i < head_dim; i++) { key_out[to + i] = k[from + i]; value_out[to + i] = v[from + i]; }
+    }
+  }
+}
+
+/* src/cpu/cache.js:118 */
+void or_kvcache_reset(or_kvcache* c) { c->length = 0; }
+
+/* src/cpu/model.js:103-123 -- rope at absolute position past+t, append, attend. */
+void or_layer_attention(or_kvcache* c, int layer, float* q, float* k, const float* v,
+                        float* out, int seq, int num_heads, int num_kv_heads, int head_dim,
+                        const double* inv_freq) {
+  int past = c->length;
+  int q_dim = num_heads * head_dim;
+  int kv_dim = num_kv_heads * head_dim;
+  for (int t = 0; t < seq; t++) {
+    int position = past + t;
+    for (int h = 0; h < num_heads; h++) or_rope_inplace(q, t * q_dim + h * head_dim, head_dim, position, inv_freq);
+    for (int h = 0; h < num_kv_heads; h++) or_rope_inplace(k, t * kv_dim + h * head_dim, head_dim, position, inv_freq);
+  }
+  or_kvcache_write_at(c, layer, past, k, v, seq);
+  float* scores = (float*)malloc(sizeof(float) * (size_t)(past + seq));
+  or_grouped_attention(q, c->keys[layer], c->values[layer], out, scores, seq, past,
+                       num_heads, num_kv_heads, head_dim);
+  free(scores);
+}
+
+/* ------------------------------------------------------- decode helpers ---- */
+
+/* attention.js:42-63 for seq=1, past=len, reading a head-major cache. */
+void or_decode_head_major(const float* q, const float* kcache, const float* vcache,
+                          int cap, int len, int num_heads, int num_kv_heads,
+                          int head_dim, float* out) {
+  int group = num_heads / num_kv_heads;
+  double scale = 1.0 / sqrt((double)head_dim);
+  float* scores = (float*)malloc(sizeof(float) * (size_t)(len + 1));
+  for (int h = 0; h < num_heads; h++) {
+    int g = h / group;
+    const float* kh = kcache + (size_t)g * cap * head_dim;
+    const float* vh = vcache + (size_t)g * cap * head_dim;
+    const float* qh = q + (size_t)h * head_dim;
+    for (int s = 0; s <= len; s++) {
+      double dot = 0.0;
+      for (int i = 0; i < head_dim; i++) dot += (double)qh[i] * (double)kh[(size_t)s * head_dim + i];
+      scores[s] = (float)(dot * scale);
+    }
+    or_softmax_inplace(scores, len + 1);
+    float* oh = out + (size_t)h * head_dim;
+    for (int i = 0; i < head_dim; i++) oh[i] = 0.0f;
+    for (int s = 0; s <= len; s++) {
+      double w = scores[s];
+      for (int i = 0; i < head_dim; i++) oh[i] = (float)((double)oh[i] + w * (double)vh[(size_t)s * head_dim + i]);
+    }
+  }
+  free(scores);
+}
+
+/* One chunk of the split-KV decomposition of attention.js:49-62: the softmax of
+ * ops.js:66-78 with its normalisation deferred. Natural-log units. */
+void or_decode_partial(const float* qh, const float* kh, const float* vh,
+                       int p0, int p1, int head_dim, float* m, float* l, float* o) {
+  double scale = 1.0 / sqrt((double)head_dim);
+  int n = p1 - p0;
+  float* scores = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+  float mx = -INFINITY;
+  for (int s = 0; s < n; s++) {
+    double dot = 0.0;
+    for (int i = 0; i < head_dim; i++) dot += (double)qh[i] * (double)kh[(size_t)(p0 + s) * head_dim + i];
+    scores[s] = (float)(dot * scale);
+    if (scores[s] > mx) mx = scores[s];
+  }
+  double sum = 0.0;
+  double* acc = (double*)calloc((size_t)head_dim, sizeof(double));
+  for (int s = 0; s < n; s++) {
+    double e = exp((double)scores[s] - (double)mx);
+    sum += e;
+    for (int i = 0; i < head_dim; i++) acc[i] += e * (double)vh[(size_t)(p0 + s) * head_dim + i];
+  }
+  *m = mx;
+  *l = (float)sum;
+  for (int i = 0; i < head_dim; i++) o[i] = (float)acc[i];
+  free(acc);
+  free(scores);
+}
+
+/* m* = max m_g; l* = sum e^(m_g-m*) l_g; out = sum e^(m_g-m*) o_g / l*, in
+ * ascending g so every caller gets the same bits. Empty partials (l == 0)
+ * contribute nothing. */
+void or_lse_combine(const float* m, const float* l, const float* o, int g,
+                    int head_dim, float* out) {
+  double mx = -INFINITY;
+  for (int i = 0; i < g; i++) if (l[i] > 0.0f && m[i] > mx) mx = m[i];
+  double lsum = 0.0;
+  double* acc = (double*)calloc((size_t)head_dim, sizeof(double));
+  for (int i = 0; i < g; i++) {
+    if (!(l[i] > 0.0f)) continue;
+    double w = exp((double)m[i] - mx);
+    lsum += w * (double)l[i];
+    for (int d = 0; d < head_dim; d++) acc[d] += w * (double)o[(size_t)i * head_dim + d];
+  }
+  for (int d = 0; d < head_dim; d++) out[d] = (float)(acc[d] / lsum);
+  free(acc);
+}
+
+/* ----------------------------------------------------------- generators ---- */
+
+/* test/attention.test.js:60-69 */
+void or_random_array(float* out, size_t n, uint32_t seed) {
+  uint32_t state = seed;
+  for (size_t i = 0; i < n; i++) {
+    state = state * 1664525u + 1013904223u;
+    out[i] = (float)(((double)state / 4294967295.0) * 2.0 - 1.0);
+  }
+}
+
+static inline uint64_t splitmix64(uint64_t* s) {
+  uint64_t z = (*s += 0x9e3779b97f4a7c15ull);
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+/* splitmix64 uniforms (53-bit) into Box-Muller pairs. */
+void or_normal_array(float* out, size_t n, uint64_t seed) {
+  uint64_t s = seed;
+  const double two_pi = 6.283185307179586;
+  for (size_t i = 0; i < n; i += 2) {
+    double u1 = ((double)(splitmix64(&s) >> 11) + 1.0) * (1.0 / 9007199254740992.0); /* (0,1] */
+    double u2 = (double)(splitmix64(&s) >> 11) * (1.0 / 9007199254740992.0);         /* [0,1) */
+    double r = sqrt(-2.0 * log(u1));
+    out[i] = (float)(r * cos(two_pi * u2));
+    if (i + 1 < n) out[i + 1] = (float)(r * sin(two_pi * u2));
+  }
+}
+
+/* ------------------------------------------------- CPU baseline (batched) -- */
+
+static float g_f16_table[65536];
+static int g_f16_table_ready = 0;
+
+static void f16_table_init(void) {
+  if (g_f16_table_ready) return;
+  for (uint32_t h = 0; h < 65536; h++) g_f16_table[h] = or_f16_to_f32((uint16_t)h);
+  g_f16_table_ready = 1;
+}
+
+int or_batched_decode_f16(const float* q, size_t q_stride, const uint16_t* kcache,
+                          const uint16_t* vcache, size_t seq_stride, const int32_t* len,
+                          int batch, int cap, int num_heads, int num_kv_heads, int head_dim,
+                          float* out, size_t out_stride, int threads) {
+  f16_table_init();
+  int used = 1;
+#ifdef _OPENMP
+  if (threads <= 0) threads = omp_get_num_procs();
+  used = threads;
+#else
+  (void)threads;
+#endif
+  int group = num_heads / num_kv_heads;
+  double scale = 1.0 / sqrt((double)head_dim);
+  long pairs = (long)batch * num_heads;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+#endif
+  for (long bh = 0; bh < pairs; bh++) {
+    int b = (int)(bh / num_heads);
+    int h = (int)(bh % num_heads);
+    int g = h / group;
+    int n = len[b] + 1;
+    const uint16_t* kh = kcache + (size_t)b * seq_stride + (size_t)g * cap * head_dim;
+    const uint16_t* vh = vcache + (size_t)b * seq_stride + (size_t)g * cap * head_dim;
+    const float* qh = q + (size_t)b * q_stride + (size_t)h * head_dim;
+    float* scores = (float*)malloc(sizeof(float) * (size_t)n);
+    for (int s = 0; s < n; s++) {
+      double dot = 0.0;
+      const uint16_t* kr = kh + (size_t)s * head_dim;
+      for (int i = 0; i < head_dim; i++) dot += (double)qh[i] * (double)g_f16_table[kr[i]];
+      scores[s] = (float)(dot * scale);
+    }
+    or_softmax_inplace(scores, n);
+    float* oh = out + (size_t)b * out_stride + (size_t)h * head_dim;
+    for (int i = 0; i < head_dim; i++) oh[i] = 0.0f;
+    for (int s = 0; s < n; s++) {
+      double w = scores[s];
+      const uint16_t* vr = vh + (size_t)s * head_dim;
+      for (int i = 0; i < head_dim; i++) oh[i] = (float)((double)oh[i] + w * (double)g_f16_table[vr[i]]);
+    }
+    free(scores);
+  }
+  return used;
+}
