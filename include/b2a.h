@@ -1,0 +1,194 @@
+/*
+ * b2a.h -- C ABI of the B200 attention hot path (libb2a.so).
+ *
+ * Replaces the attention / KV-cache operator surface of abho7/llm-inference-webgpu:
+ *   CPU  groupedAttention   src/core/attention.js:32-66
+ *        kvHeadFor          src/core/attention.js:74-76
+ *        ropeFrequencies    src/core/ops.js:99-104
+ *        ropeTables         src/core/ops.js:123-136
+ *        ropeInPlace        src/core/ops.js:147-158
+ *        KVCache            src/cpu/cache.js:18-119
+ *   GPU  GpuKVCache         src/gpu/model.js:69-84
+ *        rope-q, rope-k, KV append, ATTENTION dispatch sequence
+ *                           src/gpu/model.js:323-346 (kernels ROPE src/gpu/kernels.js:360-389,
+ *                           ATTENTION src/gpu/kernels.js:404-499)
+ *
+ * Conventions
+ *   - Every call returns a b2a_status; b2a_last_error() holds the message of
+ *     the calling thread's last failure. No call aborts, traps or throws.
+ *   - Plain pointers and sizes only. `flags` says where the data pointers of a
+ *     compute call live: B2A_HOST (default: staged through pinned buffers; the
+ *     call returns after the results are back on the host, like the reference's
+ *     readback, src/gpu/device.js:253-270) or B2A_DEVICE (zero-copy device
+ *     pointers; the call only enqueues work on the context's stream).
+ *   - A context is not re-entrant (src/gpu/model.js:231): a call made while
+ *     another call on the same context is running returns B2A_EBUSY.
+ *   - Tensor layouts: q [tokens][num_heads][head_dim]; new keys/values
+ *     [tokens][num_kv_heads][head_dim] (== the reference's [seq, kvDim] rows);
+ *     the device KV cache is head-major, per sequence and layer
+ *     [kv_head][position][head_dim] (== KVCache.present(), src/cpu/cache.js:97-115).
+ *   - Query head h reads KV head h / (num_heads / num_kv_heads) (blocked map).
+ *   - RoPE is the half-split rotation at ABSOLUTE positions (src/cpu/model.js:103-113),
+ *     evaluated in f64 from an f64 cos/sin table built on the host, stored to
+ *     f32, then rounded to the cache dtype; cache bytes are bit-exact against
+ *     the reference's f32 CPU path rounded the same way.
+ */
+#ifndef B2A_H
+#define B2A_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2A_ABI_VERSION 1
+
+typedef enum b2a_status {
+  B2A_OK = 0,
+  B2A_EINVAL = 1,     /* bad argument (shape, dtype, null pointer)                  */
+  B2A_ERANGE = 2,     /* capacity / position range: the reference's RangeError      */
+  B2A_EBUSY = 3,      /* context already running a call (src/gpu/model.js:231)      */
+  B2A_ECUDA = 4,      /* CUDA runtime error (message in b2a_last_error)             */
+  B2A_ENCCL = 5,      /* collective error                                           */
+  B2A_ETIMEDOUT = 6,  /* a bounded device-side wait gave up                         */
+  B2A_ENODEV = 7      /* no usable CUDA device                                      */
+} b2a_status;
+
+typedef enum b2a_dtype { B2A_F32 = 0, B2A_F16 = 1, B2A_BF16 = 2 } b2a_dtype;
+
+enum { B2A_HOST = 0, B2A_DEVICE = 1 };
+
+typedef struct b2a_ctx b2a_ctx;
+typedef struct b2a_rope b2a_rope;
+typedef struct b2a_kvcache b2a_kvcache;
+
+/* ---- errors and version ------------------------------------------------- */
+const char* b2a_last_error(void);
+const char* b2a_status_name(b2a_status s);
+int b2a_abi_version(void);
+
+/* ---- context: one device, one stream (the reference's GpuContext, src/gpu/device.js:21) */
+b2a_status b2a_init(int device, b2a_ctx** out);
+b2a_status b2a_destroy(b2a_ctx* ctx);
+/* Run subsequent work on an external cudaStream_t (NULL: the context's own). */
+b2a_status b2a_set_stream(b2a_ctx* ctx, void* cuda_stream);
+b2a_status b2a_synchronize(b2a_ctx* ctx);
+
+/* ---- host-side helpers (no device work) ---------------------------------- */
+/* kvHeadFor, src/core/attention.js:74-76. Returns -1 for an invalid grouping. */
+int b2a_kv_head_for(int query_head, int num_heads, int num_kv_heads);
+/* ropeFrequencies, src/core/ops.js:99-104: inv_freq[head_dim/2] in f64. */
+b2a_status b2a_rope_frequencies(int head_dim, double theta, double* inv_freq);
+/* ropeTables, src/core/ops.js:123-136: f32 cos/sin [positions][head_dim/2]. */
+b2a_status b2a_rope_tables(int head_dim, double theta, int positions, float* cos_out, float* sin_out);
+
+/* ---- device RoPE table (the model's ropeTable, src/gpu/model.js:200-205) -- */
+/* f64 cos/sin for positions 0..max_positions-1, kept on the device. */
+b2a_status b2a_rope_create(b2a_ctx* ctx, int head_dim, double theta, int max_positions, b2a_rope** out);
+b2a_status b2a_rope_destroy(b2a_rope* rope);
+
+/* ---- KV cache (KVCache src/cpu/cache.js:18-119; GpuKVCache src/gpu/model.js:69-84) */
+/* One device pool for keys and one for values, laid out
+ * [batch][num_layers][num_kv_heads][capacity][head_dim] in `dtype`, zero-filled.
+ * Each of the `batch` sequences has its own length. capacity < 1 fails with
+ * B2A_ERANGE "cache capacity must be a positive integer, got N" (cache.js:24-26). */
+b2a_status b2a_kvcache_create(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim,
+                              int capacity, int batch, b2a_dtype dtype, b2a_kvcache** out);
+b2a_status b2a_kvcache_destroy(b2a_kvcache* cache);
+/* allocate(count), cache.js:52-60: returns where `count` new positions of
+ * sequence `seq_idx` start, or B2A_ERANGE "cache holds L of C positions;
+ * cannot add K more" without changing anything. */
+b2a_status b2a_kvcache_allocate(b2a_kvcache* cache, int seq_idx, int count, int* at);
+/* commit(count), cache.js:84-86. seq_idx -1 commits every sequence. */
+b2a_status b2a_kvcache_commit(b2a_kvcache* cache, int seq_idx, int count);
+/* length, cache.js:38. */
+b2a_status b2a_kvcache_length(const b2a_kvcache* cache, int seq_idx, int* length);
+/* Set every sequence's length at once (a cache filled by other means, e.g. a
+ * benchmark or a restore). Each length must be within [0, capacity]. */
+b2a_status b2a_kvcache_set_lengths(b2a_kvcache* cache, const int32_t* lengths);
+/* reset(), cache.js:118. seq_idx -1 resets every sequence. */
+b2a_status b2a_kvcache_reset(b2a_kvcache* cache, int seq_idx);
+/* byteLength, cache.js:41-43 (in the cache's own dtype). */
+b2a_status b2a_kvcache_byte_length(const b2a_kvcache* cache, size_t* bytes);
+/* Device pools and element strides, for zero-copy callers:
+ * strides[0..3] = elements between sequences, layers, kv heads, positions. */
+b2a_status b2a_kvcache_pools(const b2a_kvcache* cache, void** keys, void** values, int64_t strides[4]);
+/* writeAt(layer, at, keys, values, count), cache.js:63-67: raw store (no RoPE)
+ * of `count` position-major rows [count][num_kv_heads*head_dim] in src_dtype,
+ * rounded to the cache dtype. Positions at..at+count-1 must be < capacity. */
+b2a_status b2a_kvcache_write_at(b2a_ctx* ctx, b2a_kvcache* cache, int layer, int seq_idx, int at,
+                                const void* keys, const void* values, b2a_dtype src_dtype,
+                                int count, int flags);
+/* keysUpTo/valuesUpTo/present, cache.js:75-115: the first n positions of a
+ * layer in present() layout [num_kv_heads][n][head_dim], raw cache dtype. */
+b2a_status b2a_kvcache_read(b2a_ctx* ctx, const b2a_kvcache* cache, int layer, int seq_idx, int n,
+                            void* keys_out, void* values_out, int flags);
+
+/* ---- fused RoPE(K) + round + append (src/cpu/model.js:103-116; src/gpu/model.js:327-338) */
+/* For sequence seq_idx with length L: rotate each KV head of k[t] at absolute
+ * position L+t, round to the cache dtype and store it, and store v[t], at
+ * cache position L+t, t < count. Length is unchanged until commit. */
+b2a_status b2a_append_rope(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope, int layer,
+                           int seq_idx, const void* k, const void* v, b2a_dtype src_dtype,
+                           int count, int flags);
+
+/* ---- single-token decode over every sequence of the cache ------------------
+ * groupedAttention with seq=1, past=L_b (attention.js:32-66), preceded by the
+ * rope-q / rope-k / append steps (src/gpu/model.js:327-338), fused.
+ * For each sequence b (length L_b) and each layer in [layer_begin, layer_begin+num_layers):
+ *   q rotated at position L_b; if k_new/v_new are given, k_new rotated at L_b
+ *   and stored with v_new at cache position L_b; attention over positions 0..L_b.
+ * q [batch][num_layers][num_heads][head_dim] (in_dtype);
+ * k_new, v_new [batch][num_layers][num_kv_heads][head_dim] (in_dtype) or NULL
+ *   (then position L_b must already hold the new key/value);
+ * out [batch][num_layers][num_heads][head_dim] (out_dtype).
+ * Lengths are not advanced (commit after the last layer, as the reference does). */
+b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
+                                int layer_begin, int num_layers, int num_heads,
+                                const void* q, const void* k_new, const void* v_new,
+                                b2a_dtype in_dtype, void* out, b2a_dtype out_dtype, int flags);
+
+/* ---- causal prefill of one sequence ----------------------------------------
+ * groupedAttention with seq=count, past=L (attention.js:32-66) for sequence
+ * seq_idx, with RoPE on q and k at absolute positions L..L+count-1 and the K/V
+ * append (src/cpu/model.js:103-123) fused in.
+ * q [count][num_heads][head_dim]; k, v [count][num_kv_heads][head_dim] (in_dtype);
+ * out [count][num_heads][head_dim] (out_dtype). */
+b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
+                                 int layer, int seq_idx, int num_heads,
+                                 const void* q, const void* k, const void* v, b2a_dtype in_dtype,
+                                 int count, void* out, b2a_dtype out_dtype, int flags);
+
+/* ---- the literal drop-in for groupedAttention (src/core/attention.js:32) ---
+ * Same arguments and layouts as the JS: q [seq][num_heads*head_dim], keys and
+ * values [past+seq][num_kv_heads*head_dim], out [seq][num_heads*head_dim], all
+ * f32; q is already rotated and keys hold the rotated cache. `scores` is the
+ * reference's scratch and is not used (may be NULL). head_dim <= 256. */
+b2a_status b2a_grouped_attention(b2a_ctx* ctx, const float* q, const float* keys, const float* values,
+                                 float* out, float* scores, int seq, int past, int num_heads,
+                                 int num_kv_heads, int head_dim, int flags);
+
+/* ---- split-KV decode across devices (one process per GPU) -------------------
+ * Partial attention of one new token per sequence over the positions this
+ * rank's cache holds: local positions [0, L_b) plus, when k_new/v_new are
+ * given, the new token appended at local position L_b. q and k_new are rotated
+ * at ABSOLUTE position q_positions[b] (host or device per flags).
+ * partial [batch][num_heads][head_dim + 4] f32: the unnormalised output
+ * sum_s 2^(t_s - m) v_s in [0, head_dim), then m (base-2 units of the scaled
+ * score t = score*log2(e)) at head_dim and l = sum_s 2^(t_s - m) at head_dim+1.
+ * An empty range gives l = 0, m = -inf. */
+b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
+                                        int layer, int num_heads, const void* q,
+                                        const void* k_new, const void* v_new, b2a_dtype in_dtype,
+                                        const int32_t* q_positions, float* partial, int flags);
+/* Log-sum-exp combine of `num_parts` partials laid out [num_parts][batch][num_heads][head_dim+4]
+ * in ascending part order, into out [batch][num_heads][head_dim] (out_dtype). */
+b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch,
+                           int num_heads, int head_dim, void* out, b2a_dtype out_dtype, int flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2A_H */

@@ -1,0 +1,12 @@
+"""b2a: the Qwen2.5 grouped-query attention hot path of abho7/llm-inference-webgpu,
+rebuilt as CUDA kernels for B200 (sm_100a) behind a C ABI (include/b2a.h).
+
+This package is the host-side mirror of the reference's attention / KV-cache
+operator API (src/core/attention.js, src/core/ops.js, src/cpu/cache.js,
+src/gpu/model.js) over libb2a.so. There is no CPU fallback: without the built
+library, or without a CUDA device, calls raise.
+"""
+from ._lib import B2AError, BusyError, RangeError, load, lib_path  # noqa: F401
+from .attention import (appendRope, attentionDecode, attentionPrefill, decodePartial,  # noqa: F401
+                        default_context, groupedAttention, kvHeadFor, lseCombine, ropeFrequencies, ropeTables)
+from .runtime import CacheConfig, Context, GpuKVCache, RopeTable  # noqa: F401

@@ -1,0 +1,131 @@
+"""The attention operator API, mirroring the reference's names and arguments:
+
+  groupedAttention(q, keys, values, out, scores, {seq, past, numHeads, numKVHeads, headDim})
+                                    src/core/attention.js:32-66
+  kvHeadFor(queryHead, numHeads, numKVHeads)      src/core/attention.js:74-76
+  ropeFrequencies(headDim, theta)                 src/core/ops.js:99-104
+  ropeTables(headDim, theta, positions)           src/core/ops.js:123-136
+
+plus the fused device operators that replace the GPU backend's rope-q / rope-k /
+KV append / ATTENTION sequence (src/gpu/model.js:323-346): appendRope,
+attentionDecode, attentionPrefill, decodePartial and lseCombine. Every one runs
+the CUDA kernels in libb2a.so.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import DTYPES, check, load
+from .runtime import Context, GpuKVCache, RopeTable, _arg, _same_dtype, _where
+
+_default_ctx: Context | None = None
+
+
+def default_context() -> Context:
+    global _default_ctx
+    if _default_ctx is None:
+        _default_ctx = Context(0)
+    return _default_ctx
+
+
+def kvHeadFor(queryHead: int, numHeads: int, numKVHeads: int) -> int:
+    r = load().b2a_kv_head_for(queryHead, numHeads, numKVHeads)
+    if r < 0:
+        raise ValueError(f"query head {queryHead} does not map onto {numKVHeads} KV heads of {numHeads}")
+    return r
+
+
+def ropeFrequencies(headDim: int, theta: float) -> np.ndarray:
+    inv = np.empty(headDim // 2, np.float64)
+    check(load().b2a_rope_frequencies(headDim, float(theta), inv.ctypes.data_as(ctypes.POINTER(ctypes.c_double))))
+    return inv
+
+
+def ropeTables(headDim: int, theta: float, positions: int) -> dict:
+    half = headDim >> 1
+    c = np.empty(positions * half, np.float32)
+    s = np.empty(positions * half, np.float32)
+    fp = ctypes.POINTER(ctypes.c_float)
+    check(load().b2a_rope_tables(headDim, float(theta), positions, c.ctypes.data_as(fp), s.ctypes.data_as(fp)))
+    return {"cos": c, "sin": s, "half": half}
+
+
+def groupedAttention(q, keys, values, out, scores=None, shape: dict | None = None, ctx: Context | None = None,
+                     **kw):
+    """src/core/attention.js:32-66 on the GPU. q [seq, numHeads*headDim] (already rotated),
+    keys/values [past+seq, numKVHeads*headDim], out overwritten and returned. f32."""
+    sh = dict(shape or {}, **kw)
+    ctx = ctx or default_context()
+    qa, ka, va, oa = _arg(q), _arg(keys), _arg(values), _arg(out, writable=True)
+    if {a.dtype for a in (qa, ka, va, oa)} != {"f32"}:
+        raise ValueError("groupedAttention takes f32 arrays, as the reference does")
+    check(load().b2a_grouped_attention(ctx.handle, qa.ptr, ka.ptr, va.ptr, oa.ptr, None, sh["seq"], sh["past"],
+                                       sh["numHeads"], sh["numKVHeads"], sh["headDim"], _where(qa, ka, va, oa)))
+    return out
+
+
+def appendRope(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, k, v, count: int, seq: int = 0,
+               dtype: str | None = None) -> None:
+    """RoPE on every KV head of k at absolute positions L..L+count-1 (L = the sequence's
+    length), rounded to the cache dtype, and stored with v (src/cpu/model.js:103-116)."""
+    ka, va = _arg(k, dtype), _arg(v, dtype)
+    check(load().b2a_append_rope(ctx.handle, cache.handle, rope.handle, layer, seq, ka.ptr, va.ptr,
+                                 DTYPES[_same_dtype(ka, va)], count, _where(ka, va)))
+
+
+def attentionDecode(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, out,
+                    numHeads: int, numLayers: int = 1, dtype: str | None = None,
+                    out_dtype: str | None = None) -> None:
+    """One new token for every sequence of the cache, over layers [layer, layer+numLayers).
+    q [batch, numLayers, numHeads, headDim]; k_new/v_new [batch, numLayers, numKVHeads, headDim]
+    or None; out [batch, numLayers, numHeads, headDim]."""
+    qa, ka, va = _arg(q, dtype), _arg(k_new, dtype), _arg(v_new, dtype)
+    oa = _arg(out, out_dtype or dtype, writable=True)
+    in_dt = _same_dtype(qa, ka, va)
+    check(load().b2a_attention_decode(ctx.handle, cache.handle, rope.handle, layer, numLayers, numHeads, qa.ptr,
+                                      ka.ptr if ka else None, va.ptr if va else None, DTYPES[in_dt], oa.ptr,
+                                      DTYPES[oa.dtype], _where(qa, ka, va, oa)))
+
+
+def attentionPrefill(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k, v, out, count: int,
+                     numHeads: int, seq: int = 0, dtype: str | None = None, out_dtype: str | None = None) -> None:
+    """Causal attention of `count` new tokens of one sequence over past+count positions,
+    with RoPE(q), RoPE(k) and the K/V append fused (src/cpu/model.js:103-123)."""
+    qa, ka, va = _arg(q, dtype), _arg(k, dtype), _arg(v, dtype)
+    oa = _arg(out, out_dtype or dtype, writable=True)
+    in_dt = _same_dtype(qa, ka, va)
+    check(load().b2a_attention_prefill(ctx.handle, cache.handle, rope.handle, layer, seq, numHeads, qa.ptr, ka.ptr,
+                                       va.ptr, DTYPES[in_dt], count, oa.ptr, DTYPES[oa.dtype], _where(qa, ka, va, oa)))
+
+
+def decodePartial(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, q_positions,
+                  partial, numHeads: int, dtype: str | None = None) -> None:
+    """Split-KV partial over this cache's positions (see b2a_attention_decode_partial).
+    partial [batch, numHeads, headDim+4] f32."""
+    qa, ka, va, pa = _arg(q, dtype), _arg(k_new, dtype), _arg(v_new, dtype), _arg(partial, writable=True)
+    in_dt = _same_dtype(qa, ka, va)
+    where = _where(qa, ka, va, pa)
+    if where == _lib.B2A_HOST:
+        pos = np.ascontiguousarray(q_positions, dtype=np.int32)
+        pos_ptr, keep = pos.ctypes.data, pos
+    else:
+        import torch
+        pos = q_positions if isinstance(q_positions, torch.Tensor) else torch.as_tensor(
+            np.asarray(q_positions, np.int32), device=f"cuda:{ctx.device}")
+        pos = pos.to(torch.int32).contiguous()
+        pos_ptr, keep = pos.data_ptr(), pos
+    check(load().b2a_attention_decode_partial(ctx.handle, cache.handle, rope.handle, layer, numHeads, qa.ptr,
+                                              ka.ptr if ka else None, va.ptr if va else None, DTYPES[in_dt],
+                                              pos_ptr, pa.ptr, where))
+    del keep
+
+
+def lseCombine(ctx: Context, partials, numParts: int, batch: int, numHeads: int, headDim: int, out,
+               out_dtype: str | None = None) -> None:
+    """Merge [numParts, batch, numHeads, headDim+4] partials in ascending part order."""
+    pa, oa = _arg(partials), _arg(out, out_dtype, writable=True)
+    check(load().b2a_lse_combine(ctx.handle, pa.ptr, numParts, batch, numHeads, headDim, oa.ptr, DTYPES[oa.dtype],
+                                 _where(pa, oa)))

@@ -1,0 +1,889 @@
+// The C ABI of libb2a.so (include/b2a.h): argument validation with the
+// reference's error messages, host<->device staging, planning and launches.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "b2a_internal.cuh"
+
+namespace {
+thread_local char g_err[1024] = "";
+}
+
+namespace b2a {
+
+b2a_status fail(b2a_status s, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return s;
+}
+
+b2a_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(B2A_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+}  // namespace b2a
+
+using namespace b2a;
+
+namespace {
+
+#define B2A_CUDA(call, what)                      \
+  do {                                            \
+    cudaError_t e_ = (call);                      \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+// Holds the context for one call: rejects re-entry (src/gpu/model.js:231) and
+// makes the context's device current on this thread.
+class CallGuard {
+ public:
+  explicit CallGuard(b2a_ctx* ctx) : ctx_(ctx) {
+    int expected = 0;
+    ok_ = ctx_ != nullptr && ctx_->busy.compare_exchange_strong(expected, 1);
+    if (ok_) cudaSetDevice(ctx_->device);
+  }
+  ~CallGuard() {
+    if (ok_) ctx_->busy.store(0);
+  }
+  bool ok() const { return ok_; }
+  b2a_status busy_status() const {
+    if (ctx_ == nullptr) return fail(B2A_EINVAL, "null context");
+    return fail(B2A_EBUSY, "a call is already running on this context; wait for it first");
+  }
+
+ private:
+  b2a_ctx* ctx_;
+  bool ok_ = false;
+};
+
+b2a_status ensure_buffer(void** buf, size_t* cap, size_t need, const char* what) {
+  if (need <= *cap) return B2A_OK;
+  if (*buf != nullptr) {
+    cudaError_t e = cudaFree(*buf);   // implicitly waits for work that may still use it
+    *buf = nullptr;
+    *cap = 0;
+    if (e != cudaSuccess) return cuda_fail(e, what);
+  }
+  size_t bytes = need + need / 4 + 4096;
+  B2A_CUDA(cudaMalloc(buf, bytes), what);
+  *cap = bytes;
+  return B2A_OK;
+}
+
+bool valid_dtype(int d) { return d == B2A_F32 || d == B2A_F16 || d == B2A_BF16; }
+
+// Carves device staging for host-pointer calls: each `add` reserves an
+// aligned slice of ctx->d_stage.
+struct Stage {
+  size_t offsets[8];
+  size_t sizes[8];
+  int n = 0;
+  size_t total = 0;
+  int add(size_t bytes) {
+    offsets[n] = total;
+    sizes[n] = bytes;
+    total += (bytes + 255) / 256 * 256;
+    return n++;
+  }
+  void* ptr(b2a_ctx* ctx, int i) const { return static_cast<char*>(ctx->d_stage) + offsets[i]; }
+};
+
+b2a_status h2d(b2a_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  if (bytes == 0) return B2A_OK;
+  B2A_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream), "copying inputs to the device");
+  return B2A_OK;
+}
+
+b2a_status d2h_sync(b2a_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  if (bytes) {
+    B2A_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "copying results to the host");
+  }
+  B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the results");
+  return B2A_OK;
+}
+
+b2a_status check_cache_shape(const b2a_kvcache* c, const b2a_rope* rope, int num_heads) {
+  if (c == nullptr || rope == nullptr) return fail(B2A_EINVAL, "null cache or rope table");
+  if (num_heads <= 0 || num_heads % c->kv_heads != 0) {
+    return fail(B2A_EINVAL,
+                "num_attention_heads %d is not divisible by num_key_value_heads %d, so the query heads "
+                "cannot be grouped evenly over the key/value heads",
+                num_heads, c->kv_heads);
+  }
+  if (rope->head_dim != c->head_dim) {
+    return fail(B2A_EINVAL, "rope table head_dim %d differs from the cache's %d", rope->head_dim, c->head_dim);
+  }
+  if (c->head_dim != 64) return fail(B2A_EINVAL, "cache attention kernels are built for head_dim 64, got %d",
+                                     c->head_dim);
+  if (num_heads / c->kv_heads > 8) return fail(B2A_EINVAL, "at most 8 query heads per KV head, got %d",
+                                               num_heads / c->kv_heads);
+  return B2A_OK;
+}
+
+AttnParams base_params(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope) {
+  AttnParams p{};
+  p.kc = c->d_k;
+  p.vc = c->d_v;
+  p.kc_w = c->d_k;
+  p.vc_w = c->d_v;
+  p.s_seq = c->s_seq;
+  p.s_layer = c->s_layer;
+  p.s_head = c->s_head;
+  p.cache_dtype = static_cast<int>(c->dtype);
+  p.len = c->d_len;
+  p.kv_heads = c->kv_heads;
+  p.head_dim = c->head_dim;
+  p.rope_cos = rope->d_cos;
+  p.rope_sin = rope->d_sin;
+  p.rope_max = rope->max_positions;
+  p.err = ctx->d_err;
+  return p;
+}
+
+// Splits every query row's keys into chunks, runs the attention kernel into
+// the context's scratch, and merges the chunks into `out` (mode 0) or into a
+// merged partial (mode 1). max_keys: the longest row's key count.
+b2a_status run_split_kv(b2a_ctx* ctx, AttnParams& p, int max_keys, void* out, int out_dtype, int mode) {
+  const int64_t rows = static_cast<int64_t>(p.batch) * p.num_layers * p.tokens * p.heads;
+  if (rows == 0) return B2A_OK;
+  const bool mma = attn_mma_supported(p);
+  p.chunk = 256;
+  if (mma) {
+    // Enough chunks for several waves over the SMs, but no chunk under 256 positions.
+    const int64_t groups = static_cast<int64_t>(p.batch) * p.num_layers * p.tokens * p.kv_heads;
+    int64_t want = 4LL * ctx->sm_count;
+    int64_t per = groups > 0 ? (want + groups - 1) / groups : 1;
+    int chunk = static_cast<int>((max_keys + per - 1) / per);
+    chunk = (chunk + 255) / 256 * 256;
+    if (chunk < 256) chunk = 256;
+    p.chunk = chunk;
+  }
+  p.nchunks = max_keys > 0 ? (max_keys + p.chunk - 1) / p.chunk : 1;
+  const size_t need = static_cast<size_t>(rows) * p.nchunks * (p.head_dim + 4) * sizeof(float);
+  b2a_status s = ensure_buffer(&ctx->d_scratch, &ctx->d_scratch_bytes, need, "allocating split-KV scratch");
+  if (s != B2A_OK) return s;
+  p.partial = static_cast<float*>(ctx->d_scratch);
+  cudaError_t e = mma ? launch_attn_mma(p, ctx->sm_count, ctx->stream) : launch_attn_simt(p, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching the attention kernel");
+  CombineParams cp{};
+  cp.partial = p.partial;
+  cp.rows = rows;
+  cp.nchunks = p.nchunks;
+  cp.head_dim = p.head_dim;
+  cp.part_stride_rows = 0;
+  cp.out = out;
+  cp.out_dtype = out_dtype;
+  cp.mode = mode;
+  e = launch_combine(cp, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching the split-KV combine");
+  return B2A_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b2a_last_error(void) { return g_err; }
+
+const char* b2a_status_name(b2a_status s) {
+  switch (s) {
+    case B2A_OK: return "B2A_OK";
+    case B2A_EINVAL: return "B2A_EINVAL";
+    case B2A_ERANGE: return "B2A_ERANGE";
+    case B2A_EBUSY: return "B2A_EBUSY";
+    case B2A_ECUDA: return "B2A_ECUDA";
+    case B2A_ENCCL: return "B2A_ENCCL";
+    case B2A_ETIMEDOUT: return "B2A_ETIMEDOUT";
+    case B2A_ENODEV: return "B2A_ENODEV";
+  }
+  return "B2A_UNKNOWN";
+}
+
+int b2a_abi_version(void) { return B2A_ABI_VERSION; }
+
+// ---------------------------------------------------------------- context --
+
+b2a_status b2a_init(int device, b2a_ctx** out) {
+  if (out == nullptr) return fail(B2A_EINVAL, "null output pointer");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    return fail(B2A_ENODEV, "no CUDA device available (%s)", e != cudaSuccess ? cudaGetErrorString(e) : "0 devices");
+  }
+  if (device < 0 || device >= count) return fail(B2A_ENODEV, "device %d out of range (%d devices)", device, count);
+  B2A_CUDA(cudaSetDevice(device), "selecting the device");
+  cudaDeviceProp prop;
+  B2A_CUDA(cudaGetDeviceProperties(&prop, device), "querying the device");
+  if (prop.major != 10) {
+    return fail(B2A_ENODEV, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, prop.major,
+                prop.minor);
+  }
+  b2a_ctx* ctx = new (std::nothrow) b2a_ctx();
+  if (ctx == nullptr) return fail(B2A_EINVAL, "out of host memory");
+  ctx->device = device;
+  ctx->sm_count = prop.multiProcessorCount;
+  e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(e, "creating the stream");
+  }
+  ctx->stream = ctx->own_stream;
+  e = cudaMalloc(&ctx->d_err, 64);
+  if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, 64);
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return cuda_fail(e, "allocating the error word");
+  }
+  *out = ctx;
+  return B2A_OK;
+}
+
+b2a_status b2a_destroy(b2a_ctx* ctx) {
+  if (ctx == nullptr) return B2A_OK;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->d_stage) cudaFree(ctx->d_stage);
+  if (ctx->d_scratch) cudaFree(ctx->d_scratch);
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->d_positions) cudaFree(ctx->d_positions);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+  return B2A_OK;
+}
+
+b2a_status b2a_set_stream(b2a_ctx* ctx, void* cuda_stream) {
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  ctx->stream = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : ctx->own_stream;
+  return B2A_OK;
+}
+
+b2a_status b2a_synchronize(b2a_ctx* ctx) {
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  B2A_CUDA(cudaStreamSynchronize(ctx->stream), "synchronizing the stream");
+  return B2A_OK;
+}
+
+// ------------------------------------------------------------ host helpers --
+
+int b2a_kv_head_for(int query_head, int num_heads, int num_kv_heads) {
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return -1;
+  if (query_head < 0 || query_head >= num_heads) return -1;
+  return query_head / (num_heads / num_kv_heads);
+}
+
+b2a_status b2a_rope_frequencies(int head_dim, double theta, double* inv_freq) {
+  if (head_dim <= 0 || head_dim % 2 != 0 || inv_freq == nullptr) {
+    return fail(B2A_EINVAL, "head_dim must be a positive even number, got %d", head_dim);
+  }
+  const int half = head_dim >> 1;
+  for (int j = 0; j < half; j++) inv_freq[j] = std::pow(theta, static_cast<double>(-2 * j) / head_dim);
+  return B2A_OK;
+}
+
+b2a_status b2a_rope_tables(int head_dim, double theta, int positions, float* cos_out, float* sin_out) {
+  if (positions < 0 || cos_out == nullptr || sin_out == nullptr) return fail(B2A_EINVAL, "bad rope table arguments");
+  double inv[512];
+  if (head_dim > 1024) return fail(B2A_EINVAL, "head_dim %d too large", head_dim);
+  b2a_status s = b2a_rope_frequencies(head_dim, theta, inv);
+  if (s != B2A_OK) return s;
+  const int half = head_dim >> 1;
+  for (int p = 0; p < positions; p++) {
+    for (int j = 0; j < half; j++) {
+      const double angle = static_cast<double>(p) * inv[j];
+      cos_out[static_cast<size_t>(p) * half + j] = static_cast<float>(std::cos(angle));
+      sin_out[static_cast<size_t>(p) * half + j] = static_cast<float>(std::sin(angle));
+    }
+  }
+  return B2A_OK;
+}
+
+// -------------------------------------------------------------- rope table --
+
+b2a_status b2a_rope_create(b2a_ctx* ctx, int head_dim, double theta, int max_positions, b2a_rope** out) {
+  if (out == nullptr) return fail(B2A_EINVAL, "null output pointer");
+  *out = nullptr;
+  if (head_dim <= 0 || head_dim % 2 != 0 || head_dim > 1024) {
+    return fail(B2A_EINVAL, "head_dim must be a positive even number <= 1024, got %d", head_dim);
+  }
+  if (max_positions < 1) return fail(B2A_ERANGE, "rope table needs at least one position, got %d", max_positions);
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const int half = head_dim >> 1;
+  double inv[512];
+  b2a_rope_frequencies(head_dim, theta, inv);
+  const size_t n = static_cast<size_t>(max_positions) * half;
+  double* hc = nullptr;
+  double* hs = nullptr;
+  B2A_CUDA(cudaMallocHost(&hc, n * sizeof(double)), "allocating the host rope table");
+  cudaError_t e = cudaMallocHost(&hs, n * sizeof(double));
+  if (e != cudaSuccess) {
+    cudaFreeHost(hc);
+    return cuda_fail(e, "allocating the host rope table");
+  }
+  // The angle ropeInPlace evaluates (src/core/ops.js:150-152), in f64.
+  for (int p = 0; p < max_positions; p++) {
+    for (int j = 0; j < half; j++) {
+      const double angle = static_cast<double>(p) * inv[j];
+      hc[static_cast<size_t>(p) * half + j] = std::cos(angle);
+      hs[static_cast<size_t>(p) * half + j] = std::sin(angle);
+    }
+  }
+  b2a_rope* r = new (std::nothrow) b2a_rope();
+  r->ctx = ctx;
+  r->device = ctx->device;
+  r->head_dim = head_dim;
+  r->theta = theta;
+  r->max_positions = max_positions;
+  e = cudaMalloc(&r->d_cos, n * sizeof(double));
+  if (e == cudaSuccess) e = cudaMalloc(&r->d_sin, n * sizeof(double));
+  if (e == cudaSuccess) e = cudaMemcpyAsync(r->d_cos, hc, n * sizeof(double), cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(r->d_sin, hs, n * sizeof(double), cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaFreeHost(hc);
+  cudaFreeHost(hs);
+  if (e != cudaSuccess) {
+    if (r->d_cos) cudaFree(r->d_cos);
+    if (r->d_sin) cudaFree(r->d_sin);
+    delete r;
+    return cuda_fail(e, "uploading the rope table");
+  }
+  *out = r;
+  return B2A_OK;
+}
+
+// Destruction touches only the object's own device memory (cudaFree waits for
+// work still using it), so it is safe after the context is gone.
+b2a_status b2a_rope_destroy(b2a_rope* rope) {
+  if (rope == nullptr) return B2A_OK;
+  cudaSetDevice(rope->device);
+  cudaFree(rope->d_cos);
+  cudaFree(rope->d_sin);
+  delete rope;
+  return B2A_OK;
+}
+
+// ---------------------------------------------------------------- KV cache --
+
+b2a_status b2a_kvcache_create(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim, int capacity, int batch,
+                              b2a_dtype dtype, b2a_kvcache** out) {
+  if (out == nullptr) return fail(B2A_EINVAL, "null output pointer");
+  *out = nullptr;
+  // src/cpu/cache.js:24-26
+  if (capacity < 1) return fail(B2A_ERANGE, "cache capacity must be a positive integer, got %d", capacity);
+  if (num_layers < 1 || num_kv_heads < 1 || head_dim < 2 || head_dim % 8 != 0 || batch < 1) {
+    return fail(B2A_EINVAL, "bad cache shape: layers %d, kv heads %d, head_dim %d, batch %d", num_layers,
+                num_kv_heads, head_dim, batch);
+  }
+  if (!valid_dtype(dtype)) return fail(B2A_EINVAL, "unknown dtype %d", static_cast<int>(dtype));
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  b2a_kvcache* c = new (std::nothrow) b2a_kvcache();
+  c->ctx = ctx;
+  c->device = ctx->device;
+  c->layers = num_layers;
+  c->kv_heads = num_kv_heads;
+  c->head_dim = head_dim;
+  c->capacity = capacity;
+  c->batch = batch;
+  c->dtype = dtype;
+  c->s_head = static_cast<int64_t>(capacity) * head_dim;
+  c->s_layer = c->s_head * num_kv_heads;
+  c->s_seq = c->s_layer * num_layers;
+  c->len.assign(batch, 0);
+  const size_t bytes = static_cast<size_t>(c->s_seq) * batch * dtype_size(dtype);
+  cudaError_t e = cudaMalloc(&c->d_k, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_v, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_len, sizeof(int32_t) * batch);
+  if (e == cudaSuccess) e = cudaMemsetAsync(c->d_k, 0, bytes, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(c->d_v, 0, bytes, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(c->d_len, 0, sizeof(int32_t) * batch, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    if (c->d_k) cudaFree(c->d_k);
+    if (c->d_v) cudaFree(c->d_v);
+    if (c->d_len) cudaFree(c->d_len);
+    delete c;
+    return cuda_fail(e, "allocating the KV cache");
+  }
+  *out = c;
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_destroy(b2a_kvcache* c) {
+  if (c == nullptr) return B2A_OK;
+  cudaSetDevice(c->device);
+  cudaFree(c->d_k);
+  cudaFree(c->d_v);
+  cudaFree(c->d_len);
+  delete c;
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_allocate(b2a_kvcache* c, int seq_idx, int count, int* at) {
+  if (c == nullptr || at == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (seq_idx < 0 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range [0, %d)", seq_idx, c->batch);
+  if (count < 0) return fail(B2A_EINVAL, "count must be non-negative, got %d", count);
+  const int len = c->len[seq_idx];
+  // src/cpu/cache.js:53-58
+  if (static_cast<int64_t>(len) + count > c->capacity) {
+    return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", len, c->capacity, count);
+  }
+  *at = len;
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_commit(b2a_kvcache* c, int seq_idx, int count) {
+  if (c == nullptr) return fail(B2A_EINVAL, "null cache");
+  if (seq_idx < -1 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range", seq_idx);
+  for (int b = 0; b < c->batch; b++) {
+    if (seq_idx >= 0 && b != seq_idx) continue;
+    if (static_cast<int64_t>(c->len[b]) + count > c->capacity || c->len[b] + count < 0) {
+      return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", c->len[b], c->capacity, count);
+    }
+  }
+  CallGuard g(c->ctx);
+  if (!g.ok()) return g.busy_status();
+  for (int b = 0; b < c->batch; b++) {
+    if (seq_idx >= 0 && b != seq_idx) continue;
+    c->len[b] += count;
+  }
+  cudaError_t e = launch_lengths_update(c->d_len, seq_idx, c->batch, count, 0, c->ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "updating the device lengths");
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_length(const b2a_kvcache* c, int seq_idx, int* length) {
+  if (c == nullptr || length == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (seq_idx < 0 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range [0, %d)", seq_idx, c->batch);
+  *length = c->len[seq_idx];
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_set_lengths(b2a_kvcache* c, const int32_t* lengths) {
+  if (c == nullptr || lengths == nullptr) return fail(B2A_EINVAL, "null argument");
+  for (int b = 0; b < c->batch; b++) {
+    if (lengths[b] < 0 || lengths[b] > c->capacity) {
+      return fail(B2A_ERANGE, "length %d of sequence %d outside [0, %d]", lengths[b], b, c->capacity);
+    }
+  }
+  CallGuard g(c->ctx);
+  if (!g.ok()) return g.busy_status();
+  for (int b = 0; b < c->batch; b++) c->len[b] = lengths[b];
+  B2A_CUDA(cudaMemcpyAsync(c->d_len, c->len.data(), sizeof(int32_t) * c->batch, cudaMemcpyHostToDevice,
+                           c->ctx->stream),
+           "uploading lengths");
+  B2A_CUDA(cudaStreamSynchronize(c->ctx->stream), "uploading lengths");
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_reset(b2a_kvcache* c, int seq_idx) {
+  if (c == nullptr) return fail(B2A_EINVAL, "null cache");
+  if (seq_idx < -1 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range", seq_idx);
+  CallGuard g(c->ctx);
+  if (!g.ok()) return g.busy_status();
+  for (int b = 0; b < c->batch; b++) {
+    if (seq_idx >= 0 && b != seq_idx) continue;
+    c->len[b] = 0;
+  }
+  cudaError_t e = launch_lengths_update(c->d_len, seq_idx, c->batch, 0, 1, c->ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "resetting the device lengths");
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_byte_length(const b2a_kvcache* c, size_t* bytes) {
+  if (c == nullptr || bytes == nullptr) return fail(B2A_EINVAL, "null argument");
+  *bytes = static_cast<size_t>(c->s_seq) * c->batch * dtype_size(c->dtype) * 2;
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_pools(const b2a_kvcache* c, void** keys, void** values, int64_t strides[4]) {
+  if (c == nullptr) return fail(B2A_EINVAL, "null cache");
+  if (keys) *keys = c->d_k;
+  if (values) *values = c->d_v;
+  if (strides) {
+    strides[0] = c->s_seq;
+    strides[1] = c->s_layer;
+    strides[2] = c->s_head;
+    strides[3] = c->head_dim;
+  }
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_write_at(b2a_ctx* ctx, b2a_kvcache* c, int layer, int seq_idx, int at, const void* keys,
+                                const void* values, b2a_dtype src_dtype, int count, int flags) {
+  if (c == nullptr || keys == nullptr || values == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (!valid_dtype(src_dtype)) return fail(B2A_EINVAL, "unknown dtype %d", static_cast<int>(src_dtype));
+  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  if (seq_idx < 0 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range [0, %d)", seq_idx, c->batch);
+  if (count < 0 || at < 0 || static_cast<int64_t>(at) + count > c->capacity) {
+    return fail(B2A_ERANGE, "positions %d..%d outside the %d-position cache", at, at + count - 1, c->capacity);
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const size_t bytes = static_cast<size_t>(count) * c->kv_heads * c->head_dim * dtype_size(src_dtype);
+  const void* dk = keys;
+  const void* dv = values;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int ik = st.add(bytes), iv = st.add(bytes);
+    b2a_status s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging");
+    if (s != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, ik), keys, bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iv), values, bytes)) != B2A_OK) return s;
+    dk = st.ptr(ctx, ik);
+    dv = st.ptr(ctx, iv);
+  }
+  cudaError_t e = launch_write_at(c, layer, seq_idx, at, dk, dv, static_cast<int>(src_dtype), count, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching writeAt");
+  if (flags == B2A_HOST) return d2h_sync(ctx, nullptr, nullptr, 0);
+  return B2A_OK;
+}
+
+b2a_status b2a_kvcache_read(b2a_ctx* ctx, const b2a_kvcache* c, int layer, int seq_idx, int n, void* keys_out,
+                            void* values_out, int flags) {
+  if (c == nullptr || keys_out == nullptr || values_out == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  if (seq_idx < 0 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range [0, %d)", seq_idx, c->batch);
+  if (n < 0 || n > c->capacity) return fail(B2A_ERANGE, "cannot read %d positions of a %d-position cache", n, c->capacity);
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const size_t es = dtype_size(c->dtype);
+  const size_t head_bytes = static_cast<size_t>(n) * c->head_dim * es;
+  const cudaMemcpyKind kind = flags == B2A_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+  for (int h = 0; h < c->kv_heads; h++) {
+    const size_t off = (static_cast<size_t>(seq_idx) * c->s_seq + static_cast<size_t>(layer) * c->s_layer +
+                        static_cast<size_t>(h) * c->s_head) * es;
+    B2A_CUDA(cudaMemcpyAsync(static_cast<char*>(keys_out) + h * head_bytes, static_cast<const char*>(c->d_k) + off,
+                             head_bytes, kind, ctx->stream), "reading keys");
+    B2A_CUDA(cudaMemcpyAsync(static_cast<char*>(values_out) + h * head_bytes,
+                             static_cast<const char*>(c->d_v) + off, head_bytes, kind, ctx->stream), "reading values");
+  }
+  if (flags == B2A_HOST) B2A_CUDA(cudaStreamSynchronize(ctx->stream), "reading the cache");
+  return B2A_OK;
+}
+
+// ------------------------------------------------------------- append/rope --
+
+b2a_status b2a_append_rope(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx, const void* k,
+                           const void* v, b2a_dtype src_dtype, int count, int flags) {
+  if (c == nullptr || rope == nullptr || k == nullptr || v == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (!valid_dtype(src_dtype)) return fail(B2A_EINVAL, "unknown dtype %d", static_cast<int>(src_dtype));
+  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  if (seq_idx < 0 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range [0, %d)", seq_idx, c->batch);
+  if (rope->head_dim != c->head_dim) return fail(B2A_EINVAL, "rope table head_dim differs from the cache's");
+  if (count < 0) return fail(B2A_EINVAL, "count must be non-negative");
+  const int past = c->len[seq_idx];
+  if (static_cast<int64_t>(past) + count > c->capacity) {
+    return fail(B2A_ERANGE, "cache holds %d of %d; cannot add %d", past, c->capacity, count);
+  }
+  if (static_cast<int64_t>(past) + count > rope->max_positions) {
+    return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", past + count, rope->max_positions);
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const size_t bytes = static_cast<size_t>(count) * c->kv_heads * c->head_dim * dtype_size(src_dtype);
+  AttnParams p = base_params(ctx, c, rope);
+  p.layer_begin = layer;
+  p.in_dtype = static_cast<int>(src_dtype);
+  p.k_new = k;
+  p.v_new = v;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int ik = st.add(bytes), iv = st.add(bytes);
+    b2a_status s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging");
+    if (s != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, ik), k, bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iv), v, bytes)) != B2A_OK) return s;
+    p.k_new = st.ptr(ctx, ik);
+    p.v_new = st.ptr(ctx, iv);
+  }
+  cudaError_t e = launch_rope_append(p, seq_idx, count, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching the rope append");
+  if (flags == B2A_HOST) return d2h_sync(ctx, nullptr, nullptr, 0);
+  return B2A_OK;
+}
+
+// ------------------------------------------------------------------ decode --
+
+b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer_begin, int num_layers,
+                                int num_heads, const void* q, const void* k_new, const void* v_new,
+                                b2a_dtype in_dtype, void* out, b2a_dtype out_dtype, int flags) {
+  b2a_status s = check_cache_shape(c, rope, num_heads);
+  if (s != B2A_OK) return s;
+  if (q == nullptr || out == nullptr) return fail(B2A_EINVAL, "null q or out");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(B2A_EINVAL, "give both new keys and values, or neither");
+  if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  if (layer_begin < 0 || num_layers < 1 || layer_begin + num_layers > c->layers) {
+    return fail(B2A_EINVAL, "layers [%d, %d) outside the cache's %d", layer_begin, layer_begin + num_layers, c->layers);
+  }
+  int max_keys = 0;
+  for (int b = 0; b < c->batch; b++) {
+    const int past = c->len[b];
+    // src/gpu/model.js:249-254
+    if (past + 1 > c->capacity) {
+      return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add 1 more", past, c->capacity);
+    }
+    if (past + 1 > rope->max_positions) {
+      return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", past + 1, rope->max_positions);
+    }
+    if (past + 1 > max_keys) max_keys = past + 1;
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  AttnParams p = base_params(ctx, c, rope);
+  p.seq_begin = 0;
+  p.batch = c->batch;
+  p.num_layers = num_layers;
+  p.layer_begin = layer_begin;
+  p.tokens = 1;
+  p.heads = num_heads;
+  p.group = num_heads / c->kv_heads;
+  p.in_dtype = static_cast<int>(in_dtype);
+  p.q = q;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.horizon_extra = 1;
+  const size_t ies = dtype_size(in_dtype);
+  const size_t q_bytes = static_cast<size_t>(c->batch) * num_layers * num_heads * c->head_dim * ies;
+  const size_t kv_bytes = static_cast<size_t>(c->batch) * num_layers * c->kv_heads * c->head_dim * ies;
+  const size_t out_bytes = static_cast<size_t>(c->batch) * num_layers * num_heads * c->head_dim * dtype_size(out_dtype);
+  void* dout = out;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int iq = st.add(q_bytes), ik = st.add(k_new ? kv_bytes : 0), iv = st.add(k_new ? kv_bytes : 0),
+        io = st.add(out_bytes);
+    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
+    p.q = st.ptr(ctx, iq);
+    if (k_new) {
+      if ((s = h2d(ctx, st.ptr(ctx, ik), k_new, kv_bytes)) != B2A_OK) return s;
+      if ((s = h2d(ctx, st.ptr(ctx, iv), v_new, kv_bytes)) != B2A_OK) return s;
+      p.k_new = st.ptr(ctx, ik);
+      p.v_new = st.ptr(ctx, iv);
+    }
+    dout = st.ptr(ctx, io);
+  }
+  if ((s = run_split_kv(ctx, p, max_keys, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
+  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
+  return B2A_OK;
+}
+
+// ----------------------------------------------------------------- prefill --
+
+b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx,
+                                 int num_heads, const void* q, const void* k, const void* v, b2a_dtype in_dtype,
+                                 int count, void* out, b2a_dtype out_dtype, int flags) {
+  b2a_status s = check_cache_shape(c, rope, num_heads);
+  if (s != B2A_OK) return s;
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  if (seq_idx < 0 || seq_idx >= c->batch) return fail(B2A_EINVAL, "sequence %d out of range [0, %d)", seq_idx, c->batch);
+  if (count < 1) return fail(B2A_EINVAL, "forward: need at least one token");
+  const int past = c->len[seq_idx];
+  if (static_cast<int64_t>(past) + count > c->capacity) {
+    return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", past, c->capacity, count);
+  }
+  if (static_cast<int64_t>(past) + count > rope->max_positions) {
+    return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", past + count, rope->max_positions);
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const size_t ies = dtype_size(in_dtype);
+  const size_t q_bytes = static_cast<size_t>(count) * num_heads * c->head_dim * ies;
+  const size_t kv_bytes = static_cast<size_t>(count) * c->kv_heads * c->head_dim * ies;
+  const size_t out_bytes = static_cast<size_t>(count) * num_heads * c->head_dim * dtype_size(out_dtype);
+  AttnParams p = base_params(ctx, c, rope);
+  p.seq_begin = seq_idx;
+  p.batch = 1;
+  p.num_layers = 1;
+  p.layer_begin = layer;
+  p.tokens = count;
+  p.heads = num_heads;
+  p.group = num_heads / c->kv_heads;
+  p.in_dtype = static_cast<int>(in_dtype);
+  p.q = q;
+  p.k_new = k;
+  p.v_new = v;
+  p.horizon_extra = 1;
+  void* dout = out;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int iq = st.add(q_bytes), ik = st.add(kv_bytes), iv = st.add(kv_bytes), io = st.add(out_bytes);
+    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, ik), k, kv_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iv), v, kv_bytes)) != B2A_OK) return s;
+    p.q = st.ptr(ctx, iq);
+    p.k_new = st.ptr(ctx, ik);
+    p.v_new = st.ptr(ctx, iv);
+    dout = st.ptr(ctx, io);
+  }
+  // RoPE(K) + append first (src/cpu/model.js:116 writes before attending), then
+  // causal attention over past+count with RoPE(Q) fused into the Q load.
+  cudaError_t e = launch_rope_append(p, seq_idx, count, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching the rope append");
+  p.k_new = nullptr;
+  p.v_new = nullptr;
+  if ((s = run_split_kv(ctx, p, past + count, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
+  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
+  return B2A_OK;
+}
+
+// ----------------------------------------------------- groupedAttention drop-in --
+
+b2a_status b2a_grouped_attention(b2a_ctx* ctx, const float* q, const float* keys, const float* values, float* out,
+                                 float* scores, int seq, int past, int num_heads, int num_kv_heads, int head_dim,
+                                 int flags) {
+  (void)scores;
+  if (q == nullptr || keys == nullptr || values == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (seq < 0 || past < 0 || num_heads < 1 || num_kv_heads < 1 || num_heads % num_kv_heads != 0) {
+    return fail(B2A_EINVAL, "bad attention shape: seq %d, past %d, heads %d/%d", seq, past, num_heads, num_kv_heads);
+  }
+  if (head_dim < 1 || head_dim > 256) return fail(B2A_EINVAL, "head_dim must be in [1, 256], got %d", head_dim);
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  if (seq == 0) return B2A_OK;
+  const size_t q_bytes = static_cast<size_t>(seq) * num_heads * head_dim * 4;
+  const size_t kv_bytes = static_cast<size_t>(past + seq) * num_kv_heads * head_dim * 4;
+  const float* dq = q;
+  const float* dk = keys;
+  const float* dv = values;
+  float* dout = out;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int iq = st.add(q_bytes), ik = st.add(kv_bytes), iv = st.add(kv_bytes), io = st.add(q_bytes);
+    b2a_status s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging");
+    if (s != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, ik), keys, kv_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iv), values, kv_bytes)) != B2A_OK) return s;
+    dq = static_cast<const float*>(st.ptr(ctx, iq));
+    dk = static_cast<const float*>(st.ptr(ctx, ik));
+    dv = static_cast<const float*>(st.ptr(ctx, iv));
+    dout = static_cast<float*>(st.ptr(ctx, io));
+  }
+  cudaError_t e = launch_grouped_generic(dq, dk, dv, dout, seq, past, num_heads, num_kv_heads, head_dim, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching groupedAttention");
+  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, q_bytes);
+  return B2A_OK;
+}
+
+// --------------------------------------------------------- split-KV partials --
+
+b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_heads,
+                                        const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
+                                        const int32_t* q_positions, float* partial, int flags) {
+  b2a_status s = check_cache_shape(c, rope, num_heads);
+  if (s != B2A_OK) return s;
+  if (q == nullptr || partial == nullptr || q_positions == nullptr) return fail(B2A_EINVAL, "null argument");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(B2A_EINVAL, "give both new keys and values, or neither");
+  if (!valid_dtype(in_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  const int extra = k_new ? 1 : 0;
+  int max_keys = 0;
+  for (int b = 0; b < c->batch; b++) {
+    if (c->len[b] + extra > c->capacity) {
+      return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", c->len[b], c->capacity, extra);
+    }
+    if (c->len[b] + extra > max_keys) max_keys = c->len[b] + extra;
+  }
+  if (flags == B2A_HOST) {
+    for (int b = 0; b < c->batch; b++) {
+      if (q_positions[b] < 0 || q_positions[b] >= rope->max_positions) {
+        return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", q_positions[b] + 1, rope->max_positions);
+      }
+    }
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  AttnParams p = base_params(ctx, c, rope);
+  p.seq_begin = 0;
+  p.batch = c->batch;
+  p.num_layers = 1;
+  p.layer_begin = layer;
+  p.tokens = 1;
+  p.heads = num_heads;
+  p.group = num_heads / c->kv_heads;
+  p.in_dtype = static_cast<int>(in_dtype);
+  p.q = q;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.q_pos = q_positions;
+  p.horizon_extra = extra;
+  const size_t ies = dtype_size(in_dtype);
+  const size_t q_bytes = static_cast<size_t>(c->batch) * num_heads * c->head_dim * ies;
+  const size_t kv_bytes = static_cast<size_t>(c->batch) * c->kv_heads * c->head_dim * ies;
+  const size_t part_bytes = static_cast<size_t>(c->batch) * num_heads * (c->head_dim + 4) * 4;
+  float* dpart = partial;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int iq = st.add(q_bytes), ik = st.add(k_new ? kv_bytes : 0), iv = st.add(k_new ? kv_bytes : 0),
+        ip = st.add(part_bytes), ipos = st.add(sizeof(int32_t) * c->batch);
+    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
+    p.q = st.ptr(ctx, iq);
+    if (k_new) {
+      if ((s = h2d(ctx, st.ptr(ctx, ik), k_new, kv_bytes)) != B2A_OK) return s;
+      if ((s = h2d(ctx, st.ptr(ctx, iv), v_new, kv_bytes)) != B2A_OK) return s;
+      p.k_new = st.ptr(ctx, ik);
+      p.v_new = st.ptr(ctx, iv);
+    }
+    if ((s = h2d(ctx, st.ptr(ctx, ipos), q_positions, sizeof(int32_t) * c->batch)) != B2A_OK) return s;
+    p.q_pos = static_cast<const int32_t*>(st.ptr(ctx, ipos));
+    dpart = static_cast<float*>(st.ptr(ctx, ip));
+  }
+  if ((s = run_split_kv(ctx, p, max_keys, dpart, B2A_F32, 1)) != B2A_OK) return s;
+  if (flags == B2A_HOST) return d2h_sync(ctx, partial, dpart, part_bytes);
+  return B2A_OK;
+}
+
+b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch, int num_heads, int head_dim,
+                           void* out, b2a_dtype out_dtype, int flags) {
+  if (partials == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (num_parts < 1 || batch < 0 || num_heads < 1 || head_dim < 1 || head_dim > 128) {
+    return fail(B2A_EINVAL, "bad combine shape: parts %d, batch %d, heads %d, head_dim %d", num_parts, batch,
+                num_heads, head_dim);
+  }
+  if (!valid_dtype(out_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const int64_t rows = static_cast<int64_t>(batch) * num_heads;
+  const size_t in_bytes = static_cast<size_t>(num_parts) * rows * (head_dim + 4) * 4;
+  const size_t out_bytes = static_cast<size_t>(rows) * head_dim * dtype_size(out_dtype);
+  const float* dpart = partials;
+  void* dout = out;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int ip = st.add(in_bytes), io = st.add(out_bytes);
+    b2a_status s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging");
+    if (s != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, ip), partials, in_bytes)) != B2A_OK) return s;
+    dpart = static_cast<const float*>(st.ptr(ctx, ip));
+    dout = st.ptr(ctx, io);
+  }
+  CombineParams cp{};
+  cp.partial = dpart;
+  cp.rows = rows;
+  cp.nchunks = num_parts;
+  cp.head_dim = head_dim;
+  cp.part_stride_rows = static_cast<int>(rows);
+  cp.out = dout;
+  cp.out_dtype = static_cast<int>(out_dtype);
+  cp.mode = 0;
+  cudaError_t e = launch_combine(cp, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching the combine");
+  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
+  return B2A_OK;
+}
+
+}  // extern "C"

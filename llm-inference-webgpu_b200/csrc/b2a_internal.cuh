@@ -1,0 +1,110 @@
+// Internal declarations shared by the C ABI (api.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include <atomic>
+#include <cstdint>
+#include <vector>
+
+#include "b2a.h"
+
+struct b2a_ctx {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;        // where work is enqueued
+  std::atomic<int> busy{0};
+  // device staging for host-pointer calls, grown on demand
+  void* d_stage = nullptr;
+  size_t d_stage_bytes = 0;
+  // split-KV partials, grown on demand
+  void* d_scratch = nullptr;
+  size_t d_scratch_bytes = 0;
+  int32_t* d_err = nullptr;             // device error word (bounded waits, bounds checks)
+  int32_t* d_positions = nullptr;       // staging for host q_positions
+  int d_positions_cap = 0;
+};
+
+struct b2a_rope {
+  b2a_ctx* ctx = nullptr;   // creating context; not used after creation
+  int device = 0;
+  int head_dim = 0;
+  double theta = 0;
+  int max_positions = 0;
+  double* d_cos = nullptr;  // [max_positions][head_dim/2]
+  double* d_sin = nullptr;
+};
+
+struct b2a_kvcache {
+  b2a_ctx* ctx = nullptr;   // owning context: must outlive the cache for data calls
+  int device = 0;
+  int layers = 0, kv_heads = 0, head_dim = 0, capacity = 0, batch = 0;
+  b2a_dtype dtype = B2A_F16;
+  void* d_k = nullptr;
+  void* d_v = nullptr;
+  int32_t* d_len = nullptr;     // device mirror of len, updated in stream order
+  std::vector<int32_t> len;     // committed length per sequence (host truth)
+  int64_t s_seq = 0, s_layer = 0, s_head = 0;  // element strides; position stride = head_dim
+};
+
+namespace b2a {
+
+// ---- errors ----------------------------------------------------------------
+b2a_status fail(b2a_status s, const char* fmt, ...);
+b2a_status cuda_fail(cudaError_t e, const char* what);
+inline size_t dtype_size(b2a_dtype d) { return d == B2A_F32 ? 4 : 2; }
+
+// ---- kernel parameter blocks -------------------------------------------------
+// Attention over a head-major cache: rows of queries (b, layer, t, head).
+struct AttnParams {
+  const void* kc;
+  const void* vc;
+  void* kc_w;                 // same pools, writable (fused append)
+  void* vc_w;
+  int64_t s_seq, s_layer, s_head;
+  int cache_dtype;
+  const int32_t* len;         // [cache batch] past length per sequence (device)
+  int seq_begin;              // first cache sequence of this call
+  int batch, num_layers, layer_begin, tokens, heads, kv_heads, group, head_dim;
+  const void* q;              // [batch][num_layers][tokens][heads][D]
+  const void* k_new;          // [batch][num_layers][tokens][kv_heads][D] or null
+  const void* v_new;
+  int in_dtype;
+  const int32_t* q_pos;       // absolute rope position per sequence (partials) or null
+  int horizon_extra;          // decode/prefill: 1 (slot L+t inclusive); partial: (k_new?1:0)
+  const double* rope_cos;
+  const double* rope_sin;
+  int rope_max;
+  float* partial;             // [rows][nchunks][D+4]
+  int chunk;                  // positions per chunk (multiple of 64)
+  int nchunks;                // chunks per row (max over rows)
+  int32_t* err;
+};
+
+struct CombineParams {
+  const float* partial;       // chunked: [rows][nchunks][D+4]; cross-rank: [nchunks][rows][D+4]
+  int64_t rows;
+  int nchunks, head_dim;
+  int part_stride_rows;       // 0: chunked layout; else rows between parts (cross-rank layout)
+  void* out;                  // mode 0: [rows][D] in out_dtype; mode 1: merged partial [rows][D+4] f32
+  int out_dtype;
+  int mode;
+};
+
+cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st);
+cudaError_t launch_write_at(const b2a_kvcache* c, int layer, int seq_idx, int at, const void* k,
+                            const void* v, int src_dtype, int count, cudaStream_t st);
+cudaError_t launch_read(const b2a_kvcache* c, int layer, int seq_idx, int n, void* k_out, void* v_out,
+                        cudaStream_t st);
+cudaError_t launch_lengths_update(int32_t* d_len, int idx, int batch, int count, int mode, cudaStream_t st);
+cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t st);
+bool attn_mma_supported(const AttnParams& p);
+cudaError_t launch_attn_mma(const AttnParams& p, int sm_count, cudaStream_t st);
+cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
+cudaError_t launch_grouped_generic(const float* q, const float* k, const float* v, float* out, int seq,
+                                   int past, int heads, int kv_heads, int head_dim, cudaStream_t st);
+
+}  // namespace b2a

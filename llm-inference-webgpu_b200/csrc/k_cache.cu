@@ -1,0 +1,91 @@
+// KV-cache kernels: fused RoPE(K) + round + append, raw writeAt, and the
+// device mirror of the per-sequence lengths.
+#include "b2a_internal.cuh"
+#include "k_util.cuh"
+
+namespace b2a {
+
+// src/cpu/model.js:103-116 (rope-k at absolute position past+t, then
+// kv.writeAt), src/gpu/model.js:327-338 (ROPE on k, two copies). One thread
+// per rotation pair (t, kv head, j); the same thread stores both halves of V.
+__global__ void k_rope_append(AttnParams p, int seq_idx, int count) {
+  const int half = p.head_dim >> 1;
+  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * half;
+  const int past = p.len[seq_idx];
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(i % half);
+    const int g = static_cast<int>((i / half) % p.kv_heads);
+    const int t = static_cast<int>(i / (static_cast<int64_t>(half) * p.kv_heads));
+    const int pos = past + t;
+    const int64_t src = (static_cast<int64_t>(t) * p.kv_heads + g) * p.head_dim;
+    const int64_t dst = seq_idx * p.s_seq + static_cast<int64_t>(p.layer_begin) * p.s_layer +
+                        g * p.s_head + static_cast<int64_t>(pos) * p.head_dim;
+    const double c = p.rope_cos[static_cast<int64_t>(pos) * half + j];
+    const double s = p.rope_sin[static_cast<int64_t>(pos) * half + j];
+    float lo, hi;
+    rope_pair_f64(ld_as_f32(p.k_new, src + j, p.in_dtype), ld_as_f32(p.k_new, src + j + half, p.in_dtype), c,
+                  s, lo, hi);
+    st_from_f32(p.kc_w, dst + j, p.cache_dtype, lo);
+    st_from_f32(p.kc_w, dst + j + half, p.cache_dtype, hi);
+    convert_elem(p.v_new, src + j, p.in_dtype, p.vc_w, dst + j, p.cache_dtype);
+    convert_elem(p.v_new, src + j + half, p.in_dtype, p.vc_w, dst + j + half, p.cache_dtype);
+  }
+}
+
+cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st) {
+  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * (p.head_dim / 2);
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  const int blocks = static_cast<int>((n + threads - 1) / threads < 4096 ? (n + threads - 1) / threads : 4096);
+  k_rope_append<<<blocks, threads, 0, st>>>(p, seq_idx, count);
+  return cudaGetLastError();
+}
+
+// src/cpu/cache.js:63-67: rows [count][kv_heads*head_dim] stored as given
+// (rounded to the cache dtype) at positions at..at+count-1, head-major.
+__global__ void k_write_at(void* kc, void* vc, int64_t base, int64_t s_head, const void* k, const void* v,
+                           int src_dt, int cache_dt, int count, int kv_heads, int head_dim, int at) {
+  const int64_t n = static_cast<int64_t>(count) * kv_heads * head_dim;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int d = static_cast<int>(i % head_dim);
+    const int g = static_cast<int>((i / head_dim) % kv_heads);
+    const int t = static_cast<int>(i / (static_cast<int64_t>(head_dim) * kv_heads));
+    const int64_t dst = base + g * s_head + static_cast<int64_t>(at + t) * head_dim + d;
+    convert_elem(k, i, src_dt, kc, dst, cache_dt);
+    convert_elem(v, i, src_dt, vc, dst, cache_dt);
+  }
+}
+
+cudaError_t launch_write_at(const b2a_kvcache* c, int layer, int seq_idx, int at, const void* k, const void* v,
+                            int src_dtype, int count, cudaStream_t st) {
+  const int64_t n = static_cast<int64_t>(count) * c->kv_heads * c->head_dim;
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  const int blocks = static_cast<int>((n + threads - 1) / threads < 4096 ? (n + threads - 1) / threads : 4096);
+  const int64_t base = seq_idx * c->s_seq + static_cast<int64_t>(layer) * c->s_layer;
+  k_write_at<<<blocks, threads, 0, st>>>(c->d_k, c->d_v, base, c->s_head, k, v, src_dtype,
+                                         static_cast<int>(c->dtype), count, c->kv_heads, c->head_dim, at);
+  return cudaGetLastError();
+}
+
+// mode 0: len[idx] += count (idx < 0: every sequence); mode 1: len[idx] = 0
+// (idx < 0: every sequence). Keeps the device lengths in stream order with the
+// host's bookkeeping.
+__global__ void k_lengths_update(int32_t* len, int idx, int batch, int count, int mode) {
+  for (int b = threadIdx.x + blockIdx.x * blockDim.x; b < batch; b += blockDim.x * gridDim.x) {
+    if (idx >= 0 && b != idx) continue;
+    if (mode == 0) len[b] += count;
+    else len[b] = 0;
+  }
+}
+
+cudaError_t launch_lengths_update(int32_t* d_len, int idx, int batch, int count, int mode, cudaStream_t st) {
+  const int threads = 256;
+  const int blocks = (batch + threads - 1) / threads;
+  k_lengths_update<<<blocks > 0 ? blocks : 1, threads, 0, st>>>(d_len, idx, batch, count, mode);
+  return cudaGetLastError();
+}
+
+}  // namespace b2a

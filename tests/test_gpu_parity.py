@@ -1,0 +1,307 @@
+"""GPU parity: the CUDA kernels (through the C ABI) against the CPU oracle on
+the same seeded inputs. Every case restates a reference test or a BASELINE
+configuration; see tests/helpers.py for the tolerance."""
+import numpy as np
+import pytest
+
+import b2a
+from helpers import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+H, KVH, D, THETA = 14, 2, 64, 1e6
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = b2a.Context(0)
+    yield c
+    c.close()
+
+
+@pytest.fixture(scope="module")
+def rope(ctx):
+    return b2a.RopeTable(ctx, D, THETA, 40000)
+
+
+def cfg(layers=1):
+    return b2a.CacheConfig(numLayers=layers, numKVHeads=KVH, headDim=D, numHeads=H)
+
+
+# ---------------------------------------------------------------- drop-in --
+
+@pytest.mark.parametrize("name,shape,seeds", [
+    ("attn_kernels_html", (3, 5, 14, 2, 64), (31, 32, 33)),
+    ("attn_prefill_s5_p0", (5, 0, 14, 2, 64), (1, 2, 3)),
+    ("attn_decode_s1_p11", (1, 11, 14, 2, 64), (99, 100, 101)),
+    ("attn_mixed_s3_p7", (3, 7, 14, 2, 64), (4242, 4243, 4244)),
+    ("attn_mha_4_4", (4, 2, 4, 4, 8), (1, 2, 3)),
+    ("attn_mqa_6_1", (4, 3, 6, 1, 8), (1, 2, 3)),
+])
+def test_grouped_attention_dropin_matches_golden(ctx, oracle, golden, name, shape, seeds):
+    seq, past, nh, nkv, hd = shape
+    total = past + seq
+    q = oracle.random_array(seq * nh * hd, seeds[0])
+    k = oracle.random_array(total * nkv * hd, seeds[1])
+    v = oracle.random_array(total * nkv * hd, seeds[2])
+    out = np.empty(seq * nh * hd, np.float32)
+    b2a.groupedAttention(q, k, v, out, None, dict(seq=seq, past=past, numHeads=nh, numKVHeads=nkv, headDim=hd),
+                         ctx=ctx)
+    c = assert_parity(out, golden[name], "f32", name)
+    # web/kernels.html:351-385 holds the WGSL kernel to 1e-5 relative; so do we.
+    assert c["rel"] <= 1e-5, c
+
+
+def test_dropin_first_position_returns_value(ctx, oracle):
+    nh, nkv, hd = 4, 2, 8
+    q = oracle.random_array(nh * hd, 21)
+    k = oracle.random_array(nkv * hd, 22)
+    v = oracle.random_array(nkv * hd, 23)
+    out = np.empty(nh * hd, np.float32)
+    b2a.groupedAttention(q, k, v, out, None, seq=1, past=0, numHeads=nh, numKVHeads=nkv, headDim=hd, ctx=ctx)
+    for h in range(nh):
+        g = b2a.kvHeadFor(h, nh, nkv)
+        assert np.array_equal(out[h * hd:(h + 1) * hd], v[g * hd:(g + 1) * hd])
+
+
+def test_dropin_is_causal(ctx, oracle):
+    seq, nh, nkv, hd = 4, 4, 2, 8
+    q_dim, kv_dim = nh * hd, nkv * hd
+    q = oracle.random_array(seq * q_dim, 7)
+    k = oracle.random_array(seq * kv_dim, 8)
+    v = oracle.random_array(seq * kv_dim, 9)
+    shape = dict(seq=seq, past=0, numHeads=nh, numKVHeads=nkv, headDim=hd)
+    before = np.empty(seq * q_dim, np.float32)
+    b2a.groupedAttention(q, k, v, before, None, shape, ctx=ctx)
+    k2, v2 = k.copy(), v.copy()
+    k2[(seq - 1) * kv_dim:] += np.float32(3.5)
+    v2[(seq - 1) * kv_dim:] -= np.float32(2.25)
+    after = np.empty(seq * q_dim, np.float32)
+    b2a.groupedAttention(q, k2, v2, after, None, shape, ctx=ctx)
+    assert np.array_equal(after[:(seq - 1) * q_dim], before[:(seq - 1) * q_dim])
+    assert not np.array_equal(after[(seq - 1) * q_dim:], before[(seq - 1) * q_dim:])
+
+
+def test_dropin_long_context(ctx, oracle):
+    """More keys than one 1024-position chunk: exercises the online rescale."""
+    seq, past = 2, 3000
+    q = oracle.normal_array(seq * H * D, 41)
+    k = oracle.normal_array((past + seq) * KVH * D, 42)
+    v = oracle.normal_array((past + seq) * KVH * D, 43)
+    out = np.empty(seq * H * D, np.float32)
+    b2a.groupedAttention(q, k, v, out, None, seq=seq, past=past, numHeads=H, numKVHeads=KVH, headDim=D, ctx=ctx)
+    ref = oracle.grouped_attention(q, k, v, seq, past, H, KVH, D)
+    assert_parity(out, ref, "f32", "long context")
+
+
+# ------------------------------------------------------------------- cache --
+
+def test_cache_bookkeeping_matches_reference(ctx):
+    c = b2a.GpuKVCache(ctx, b2a.CacheConfig(2, 2, 8), 3, dtype="f32")
+    assert c.length == 0 and c.capacity == 3
+    assert c.allocate(3) == 0
+    c.commit(3)
+    with pytest.raises(b2a.RangeError, match="holds 3 of 3 positions"):
+        c.allocate(1)
+    assert c.length == 3
+    c.reset()
+    assert c.length == 0 and c.allocate(3) == 0
+    with pytest.raises(b2a.RangeError, match="positive integer"):
+        b2a.GpuKVCache(ctx, b2a.CacheConfig(2, 2, 8), 0)
+
+
+def test_cache_present_transpose(ctx):
+    # test/cache.test.js:136-150 with kvDim = 2 heads x head width 8 (kernel minimum), same pattern
+    c = b2a.GpuKVCache(ctx, b2a.CacheConfig(2, 2, 8), 2, dtype="f32")
+    at = c.allocate(2)
+    keys = np.arange(32, dtype=np.float32)
+    c.writeAt(0, at, keys, keys, 2)
+    c.commit(2)
+    k = c.present(0)["key"]
+    assert list(k.reshape(-1)) == [*range(0, 8), *range(16, 24), *range(8, 16), *range(24, 32)]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_append_rope_is_bit_exact(ctx, rope, oracle, dtype):
+    """RoPE(K) at absolute positions, rounded to the cache dtype: the stored bytes
+    equal the oracle's ropeInPlace (src/core/ops.js:147-158) rounded the same way."""
+    layers, cap, past, count = 2, 300, 37, 50
+    c = b2a.GpuKVCache(ctx, cfg(layers), cap, dtype=dtype)
+    c.setLengths([past])
+    k = oracle.normal_array(count * KVH * D, 51) * np.float32(3)
+    v = oracle.normal_array(count * KVH * D, 52)
+    b2a.appendRope(ctx, c, rope, 1, k, v, count)
+    got_k, got_v = c.read(1, past + count)
+    ref_k = oracle.rope_rows(k.reshape(count, KVH * D), range(past, past + count), D, THETA)
+    ref_k = oracle.to_bits(ref_k.reshape(count, KVH, D).transpose(1, 0, 2), dtype)
+    ref_v = oracle.to_bits(v.reshape(count, KVH, D).transpose(1, 0, 2), dtype)
+    assert np.array_equal(got_k[:, past:], ref_k)
+    assert np.array_equal(got_v[:, past:], ref_v)
+    assert not np.any(got_k[:, :past])   # untouched, zero-filled
+
+
+# ----------------------------------------------------------- config 1 decode --
+
+def _fill_cache(ctx, c, oracle, lengths, layers, dtype, seed):
+    """Positions 0..L-1 of every sequence/layer: N(0,1) keys and values, stored as
+    already-rotated cache contents (the cache holds post-RoPE keys)."""
+    hk, hv = {}, {}
+    for b, L in enumerate(lengths):
+        for layer in range(layers):
+            kk = oracle.normal_array(L * KVH * D, seed + 1000 * b + 10 * layer)
+            vv = oracle.normal_array(L * KVH * D, seed + 1000 * b + 10 * layer + 1)
+            c.writeAt(layer, 0, kk, vv, L, seq=b)
+            hk[b, layer] = oracle.round_to(kk, dtype).reshape(L, KVH, D).transpose(1, 0, 2)
+            hv[b, layer] = oracle.round_to(vv, dtype).reshape(L, KVH, D).transpose(1, 0, 2)
+    c.setLengths(lengths)
+    return hk, hv
+
+
+def _oracle_decode(oracle, q, kn, vn, hk, hv, L, dtype):
+    """src/cpu/model.js:103-123 for one token at position L over a cache holding
+    hk/hv (head-major, already rounded). Returns (out [H*D], new K row, new V row)."""
+    qr = oracle.rope_rows(q.reshape(1, H * D), [L], D, THETA).reshape(-1)
+    kr = oracle.rope_rows(kn.reshape(1, KVH * D), [L], D, THETA).reshape(KVH, D)
+    kr = oracle.round_to(kr, dtype)
+    vr = oracle.round_to(vn.reshape(KVH, D), dtype)
+    kc = np.concatenate([hk, kr[:, None, :]], axis=1)
+    vc = np.concatenate([hv, vr[:, None, :]], axis=1)
+    out = oracle.decode_head_major(qr, np.ascontiguousarray(kc), np.ascontiguousarray(vc), L + 1, L, H, KVH, D)
+    return out, kr, vr
+
+
+def test_config1_decode_f32(ctx, rope, oracle):
+    """batch 1, 14/2 heads, D 64, cache positions 0..127, new token at 128, f32."""
+    L = 128
+    c = b2a.GpuKVCache(ctx, cfg(1), 256, dtype="f32")
+    hk, hv = _fill_cache(ctx, c, oracle, [L], 1, "f32", 100)
+    q = oracle.normal_array(H * D, 1)
+    kn = oracle.normal_array(KVH * D, 2)
+    vn = oracle.normal_array(KVH * D, 3)
+    out = np.empty((1, 1, H, D), np.float32)
+    b2a.attentionDecode(ctx, c, rope, 0, q.reshape(1, 1, H, D), kn.reshape(1, 1, KVH, D), vn.reshape(1, 1, KVH, D),
+                        out, H)
+    ref, kr, vr = _oracle_decode(oracle, q, kn, vn, hk[0, 0], hv[0, 0], L, "f32")
+    assert_parity(out, ref, "f32", "config 1")
+    gk, gv = c.read(0, L + 1)
+    assert np.array_equal(gk[:, L], oracle.to_bits(kr, "f32"))
+    assert np.array_equal(gv[:, L], oracle.to_bits(vr, "f32"))
+    assert c.length == L   # not advanced until commit
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_batched_decode_multilayer(ctx, rope, oracle, dtype):
+    """BASELINE config 3, scaled down: independent sequences of different lengths,
+    several layers in one call, RoPE at each sequence's own position."""
+    rng = np.random.default_rng(7)
+    batch, layers = 6, 3
+    lengths = [int(x) for x in rng.integers(1, 1500, size=batch)]
+    lengths[0] = 1
+    lengths[1] = 256
+    c = b2a.GpuKVCache(ctx, cfg(layers), 1600, batch=batch, dtype=dtype)
+    hk, hv = _fill_cache(ctx, c, oracle, lengths, layers, dtype, 300)
+    q = oracle.round_to(oracle.normal_array(batch * layers * H * D, 5), dtype).reshape(batch, layers, H, D)
+    kn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 6), dtype).reshape(batch, layers, KVH, D)
+    vn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 7), dtype).reshape(batch, layers, KVH, D)
+    out = np.empty((batch, layers, H, D), np.float32)
+    b2a.attentionDecode(ctx, c, rope, 0, oracle.to_bits(q, dtype), oracle.to_bits(kn, dtype),
+                        oracle.to_bits(vn, dtype), out, H, numLayers=layers, dtype=dtype)
+    for b in range(batch):
+        for layer in range(layers):
+            ref, kr, vr = _oracle_decode(oracle, q[b, layer], kn[b, layer], vn[b, layer], hk[b, layer],
+                                         hv[b, layer], lengths[b], dtype)
+            assert_parity(out[b, layer].reshape(-1), ref, "f32", f"seq {b} layer {layer}")
+            gk, gv = c.read(layer, lengths[b] + 1, seq=b)
+            assert np.array_equal(gk[:, lengths[b]], oracle.to_bits(kr, dtype))
+            assert np.array_equal(gv[:, lengths[b]], oracle.to_bits(vr, dtype))
+
+
+# ---------------------------------------------------------- config 2 prefill --
+
+@pytest.mark.parametrize("S", [8, 64, 512])
+def test_config2_prefill_bf16(ctx, rope, oracle, S):
+    """causal prefill, bf16 Q/K/V N(0,1), RoPE at 0..S-1, bf16 out."""
+    q = oracle.round_to(oracle.normal_array(S * H * D, 11), "bf16")
+    k = oracle.round_to(oracle.normal_array(S * KVH * D, 12), "bf16")
+    v = oracle.round_to(oracle.normal_array(S * KVH * D, 13), "bf16")
+    c = b2a.GpuKVCache(ctx, cfg(1), S, dtype="bf16")
+    out = np.empty(S * H * D, np.uint16)
+    b2a.attentionPrefill(ctx, c, rope, 0, oracle.to_bits(q, "bf16"), oracle.to_bits(k, "bf16"),
+                         oracle.to_bits(v, "bf16"), out, S, H, dtype="bf16")
+    # the oracle on the same inputs; its cache is f32, so K is rounded to bf16
+    # in the cache the way the kernel stores it, before attention reads it
+    qr = oracle.rope_rows(q.reshape(S, H * D), range(S), D, THETA).reshape(-1)
+    kr = oracle.round_to(oracle.rope_rows(k.reshape(S, KVH * D), range(S), D, THETA), "bf16").reshape(-1)
+    ref = oracle.grouped_attention(qr, kr, v, S, 0, H, KVH, D)
+    got = oracle.from_bits(out, "bf16")
+    assert_parity(got, ref, "bf16", f"prefill S={S}")
+    gk, _ = c.read(0, S)
+    assert np.array_equal(gk, oracle.to_bits(kr.reshape(S, KVH, D).transpose(1, 0, 2), "bf16"))
+
+
+@pytest.mark.parametrize("splits", [[40], [1] * 12 + [28], [17, 1, 22]])
+def test_incremental_equals_full_recompute(ctx, rope, oracle, splits):
+    """validate/phase2.js:83-121 on synthetic projections: prefill in one call,
+    in chunks, or token by token gives the same cache bits and outputs within
+    the tolerance."""
+    n = sum(splits)
+    q = oracle.normal_array(n * H * D, 61).reshape(n, H * D)
+    k = oracle.normal_array(n * KVH * D, 62).reshape(n, KVH * D)
+    v = oracle.normal_array(n * KVH * D, 63).reshape(n, KVH * D)
+    c = b2a.GpuKVCache(ctx, cfg(1), n, dtype="f32")
+    outs = []
+    t0 = 0
+    for s in splits:
+        c.allocate(s)
+        o = np.empty(s * H * D, np.float32)
+        if s == 1:
+            b2a.attentionDecode(ctx, c, rope, 0, q[t0].reshape(1, 1, H, D), k[t0].reshape(1, 1, KVH, D),
+                                v[t0].reshape(1, 1, KVH, D), o.reshape(1, 1, H, D), H)
+        else:
+            b2a.attentionPrefill(ctx, c, rope, 0, q[t0:t0 + s], k[t0:t0 + s], v[t0:t0 + s], o, s, H)
+        outs.append(o)
+        c.commit(s)
+        t0 += s
+    got = np.concatenate(outs)
+    oc = oracle.OracleKVCache(1, KVH * D, n)
+    oc.allocate(n)
+    ref, _, kr = oc.layer_attention(0, q, k, v, n, H, KVH, D, THETA)
+    assert_parity(got, ref, "f32", f"splits {splits}")
+    gk, gv = c.read(0, n)
+    assert np.array_equal(gk, kr.reshape(n, KVH, D).transpose(1, 0, 2))
+    assert np.array_equal(gv, v.reshape(n, KVH, D).transpose(1, 0, 2))
+
+
+# ------------------------------------------------------- split-KV partials --
+
+def test_split_kv_partials_combine_to_full_decode(ctx, rope, oracle):
+    """BASELINE config 5, scaled down: the KV sequence split into parts held by
+    separate caches (as separate ranks would), partials combined in order."""
+    batch, L, parts = 3, 2500, 3
+    dtype = "f16"
+    chunk = (L + parts - 1) // parts
+    kfull = [oracle.round_to(oracle.normal_array(L * KVH * D, 900 + b), dtype).reshape(L, KVH, D) for b in range(batch)]
+    vfull = [oracle.round_to(oracle.normal_array(L * KVH * D, 950 + b), dtype).reshape(L, KVH, D) for b in range(batch)]
+    q = oracle.round_to(oracle.normal_array(batch * H * D, 31), dtype).reshape(batch, H, D)
+    kn = oracle.round_to(oracle.normal_array(batch * KVH * D, 32), dtype).reshape(batch, KVH, D)
+    vn = oracle.round_to(oracle.normal_array(batch * KVH * D, 33), dtype).reshape(batch, KVH, D)
+    pos = np.full(batch, L, np.int32)
+    partials = np.empty((parts, batch, H, D + 4), np.float32)
+    for r in range(parts):
+        lo, hi = r * chunk, min(L, (r + 1) * chunk)
+        last = r == parts - 1
+        c = b2a.GpuKVCache(ctx, cfg(1), (hi - lo) + 1, batch=batch, dtype=dtype)
+        for b in range(batch):
+            c.writeAt(0, 0, oracle.to_bits(kfull[b][lo:hi], dtype), oracle.to_bits(vfull[b][lo:hi], dtype),
+                      hi - lo, seq=b, dtype=dtype)
+        c.setLengths([hi - lo] * batch)
+        b2a.decodePartial(ctx, c, rope, 0, oracle.to_bits(q, dtype),
+                          oracle.to_bits(kn, dtype) if last else None, oracle.to_bits(vn, dtype) if last else None,
+                          pos, partials[r], H, dtype=dtype)
+    out = np.empty((batch, H, D), np.float32)
+    b2a.lseCombine(ctx, partials, parts, batch, H, D, out)
+    for b in range(batch):
+        ref, _, _ = _oracle_decode(oracle, q[b], kn[b], vn[b], np.ascontiguousarray(kfull[b].transpose(1, 0, 2)),
+                                   np.ascontiguousarray(vfull[b].transpose(1, 0, 2)), L, dtype)
+        assert_parity(out[b].reshape(-1), ref, "f32", f"split seq {b}")
+
