@@ -1,0 +1,469 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline line (one JSON line on rank 0): decode-attention HBM GB/s on BASELINE
+config 3 -- 64 independent sequences per GPU, 24 layers, 14 query / 2 KV heads,
+head_dim 64, f16 head-major KV cache with lengths drawn U{256..4096}, one new
+token per sequence with RoPE and the KV append fused. A step is one decode of
+all 24 layers for every sequence (one C-ABI call). `value` is whole-job
+throughput over all ranks with inputs resident in HBM; `e2e` is the same metric
+through the host-pointer C-ABI path (pinned host inputs copied in and outputs
+read back inside the timed region). Per GPU the work is fixed (weak scaling);
+sequences are independent, so no collective touches the data path.
+
+The `prefill` object reports BASELINE config 2 (causal prefill, bf16) in
+TFLOPS with its own roofline. `cpu_baseline` times the CPU restatement of the
+reference's attention (oracle/, f64 accumulation as the reference's JS does)
+on a bounded sample of the same workload on this host's cores.
+
+--impl reference times the reference's CPU path restated in C (the reference is
+JavaScript and no JS runtime exists on this machine) on the same workload and
+prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "llm-inference-webgpu_b200")
+for _p in (ROOT, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+H, KVH, D, THETA = 14, 2, 64, 1e6
+SEQS, LAYERS, LMIN, LMAX = 64, 24, 256, 4096
+CAP = 4160                       # >= LMAX + 1, a multiple of 64
+METRIC = "decode-attn HBM GB/s"
+
+
+# ----------------------------------------------------------------- helpers --
+
+def peaks() -> dict:
+    p = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            m = json.load(f)
+        for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained"):
+            if k in m:
+                p[k] = float(m[k])
+        p["source"] = "measured"
+    return p
+
+
+def ncu_traffic(kernel: str, workload: str):
+    """dram read+write bytes per launch from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 3 and not line.startswith("#") and parts[0] == kernel and parts[1] == workload:
+                return float(parts[2])
+    return None
+
+
+def config3_lengths(rank: int) -> np.ndarray:
+    rng = np.random.default_rng(1234 + rank)
+    return rng.integers(LMIN, LMAX + 1, size=SEQS).astype(np.int32)
+
+
+def config3_bytes(lengths: np.ndarray, cache_es: int = 2, in_es: int = 2, out_es: int = 4) -> dict:
+    """Algorithmic bytes of one config-3 step (all layers, all sequences)."""
+    kv_read = int(LAYERS * KVH * D * cache_es * 2 * int((lengths.astype(np.int64) + 1).sum()))
+    q = SEQS * LAYERS * H * D * in_es
+    kv_new = 2 * SEQS * LAYERS * KVH * D * in_es
+    append = 2 * SEQS * LAYERS * KVH * D * cache_es
+    out = SEQS * LAYERS * H * D * out_es
+    return {"kv_read": kv_read, "q": q, "kv_new": kv_new, "append": append, "out": out,
+            "attention_kernel": kv_read + q + kv_new + append, "step": kv_read + q + kv_new + append + out}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float) -> dict:
+        rows = [s for t, s in self.samples if t0 <= t <= t1] or [s for _, s in self.samples]
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            f = [x.strip() for x in r.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_id_for(torch, dev: int) -> str:
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return vis.split(",")[dev]
+        return str(dev)
+
+
+class _CAI:
+    """__cuda_array_interface__ over a device pointer, so torch can view the cache pools."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+# ---------------------------------------------------------- CPU baselines --
+
+def cpu_decode_sample(lengths: np.ndarray, target_s: float, threads: int = 0):
+    """The reference's attention (restated in C, f64 accumulation) over config-3
+    sequences, one layer's worth of data reused for `n` layers. Returns
+    (GB/s, threads, description)."""
+    from oracle import oracle as o
+    rng = np.random.default_rng(99)
+    cap = int(lengths.max()) + 1
+    seq_stride = KVH * cap * D
+    kb = rng.standard_normal(SEQS * seq_stride, dtype=np.float32).astype(np.float16).view(np.uint16)
+    vb = rng.standard_normal(SEQS * seq_stride, dtype=np.float32).astype(np.float16).view(np.uint16)
+    q = rng.standard_normal(SEQS * H * D, dtype=np.float32)
+    b = config3_bytes(lengths)
+    per_layer = b["step"] / LAYERS
+    t0 = time.perf_counter()
+    _, used = o.batched_decode_f16(q, H * D, kb, vb, seq_stride, lengths, SEQS, cap, H, KVH, D, H * D, threads)
+    t1 = time.perf_counter() - t0
+    n = max(1, min(LAYERS, int(target_s / max(t1, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        o.batched_decode_f16(q, H * D, kb, vb, seq_stride, lengths, SEQS, cap, H, KVH, D, H * D, threads)
+    dt = time.perf_counter() - t0
+    return per_layer * n / dt / 1e9, used, (f"{SEQS} sequences x {n} layer(s) of config 3 "
+                                           f"({n * per_layer / 1e9:.3f} GB), {dt:.2f} s")
+
+
+# ------------------------------------------------------------------ ours ----
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import b2a
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    stream = torch.cuda.Stream(device=dev)
+    ctx = b2a.Context(local)
+    ctx.set_stream(stream)
+    lengths = config3_lengths(rank)
+    nb = config3_bytes(lengths)
+    with torch.cuda.stream(stream):
+        cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(LAYERS, KVH, D, H), CAP, batch=SEQS, dtype="f16")
+        rope = b2a.RopeTable(ctx, D, THETA, 32769)
+        kp, vp, strides = cache.pools()
+        shape = (SEQS, LAYERS, KVH, CAP, D)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(4321 + rank)
+        torch.as_tensor(_CAI(kp, shape, "<f2"), device=dev).normal_(generator=gen)
+        torch.as_tensor(_CAI(vp, shape, "<f2"), device=dev).normal_(generator=gen)
+        cache.setLengths(lengths)
+        q = torch.randn(SEQS, LAYERS, H, D, device=dev, generator=gen).half()
+        kn = torch.randn(SEQS, LAYERS, KVH, D, device=dev, generator=gen).half()
+        vn = torch.randn(SEQS, LAYERS, KVH, D, device=dev, generator=gen).half()
+        out = torch.empty(SEQS, LAYERS, H, D, device=dev, dtype=torch.float32)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        b2a.attentionDecode(ctx, cache, rope, 0, q, kn, vn, out, H, numLayers=LAYERS)
+
+    clocks = ClockSampler(gpu_id_for(torch, local)) if rank == 0 else None
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_wall0 = time.time()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t_wall1 = time.time()
+    ms = e0.elapsed_time(e1)
+    if clocks:
+        time.sleep(0.2)
+        clocks.stop()
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * nb["step"] * args.steps / (ms_max / 1e3) / 1e9
+
+    # per-kernel device time (events around each launch on the launching stream)
+    ktimes_steps = max(3, min(args.steps, 50))
+    ctx.enable_timing(True)
+    for _ in range(ktimes_steps):
+        step()
+    kt = ctx.read_timing()
+    ctx.enable_timing(False)
+    attn_name = "attention_mma" if "attention_mma" in kt else "attention_simt"
+    attn_ms = kt[attn_name][1] / kt[attn_name][0]
+    launches_per_step = sum(v[0] for v in kt.values()) / ktimes_steps
+
+    # end to end through the host-pointer C ABI: pinned inputs in, output back
+    qh, knh, vnh = q.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    outh = torch.empty(out.shape, dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 200))
+    for _ in range(max(1, min(args.warmup, 5))):
+        b2a.attentionDecode(ctx, cache, rope, 0, qh, knh, vnh, outh, H, numLayers=LAYERS)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        b2a.attentionDecode(ctx, cache, rope, 0, qh, knh, vnh, outh, H, numLayers=LAYERS)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * nb["step"] * e2e_steps / (e2e_ms / 1e3) / 1e9
+
+    pk = peaks()
+    achieved = nb["attention_kernel"] / (attn_ms / 1e3) / 1e9
+    traffic = ncu_traffic(attn_name, "config3")
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config3-batched-decode", "sequences_per_gpu": SEQS, "layers": LAYERS,
+                   "heads": "14q/2kv", "head_dim": D, "kv_len": f"U{{{LMIN}..{LMAX}}} seeded per rank",
+                   "cache_dtype": "f16", "q_dtype": "f16", "out_dtype": "f32", "rope_theta": THETA,
+                   "bytes_per_step_per_gpu": nb["step"], "parallelism": f"dp{world} (sequences)",
+                   "l2": "inputs larger than L2 (KV read per step per GPU %.2f GB)" % (nb["kv_read"] / 1e9)},
+        "roofline": {"bound": "hbm", "kernel": attn_name, "achieved": round(achieved, 1),
+                     "peak": pk["hbm_gbs"], "peak_source": pk["source"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": nb["attention_kernel"],
+                     "launch_ms": round(attn_ms, 4)},
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": nb["q"] + nb["kv_new"],
+                "d2h_bytes_per_step": nb["out"], "ms_per_step": round(e2e_ms / e2e_steps, 4),
+                "path": "b2a_attention_decode with B2A_HOST pointers (pinned)"},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "kernels": {k: {"launches": v[0], "avg_ms": round(v[1] / v[0], 4)} for k, v in kt.items()},
+    }
+    if clocks:
+        line["clocks"] = clocks.summary(t_wall0, t_wall1)
+
+    if world == 1 and not args.no_prefill:
+        line["prefill"] = bench_prefill(torch, b2a, ctx, stream, dev, pk, args)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, used, sample = cpu_decode_sample(lengths, target_s=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": used, "kind": "port",
+                                "sample": sample}
+    barrier()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    cache.close()
+    rope.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
+    """causal prefill, bf16 Q/K/V, RoPE at 0..S-1, fused append, bf16 out."""
+    res = {"metric": "prefill-attn TFLOPS", "unit": "TFLOPS", "dtype": "bf16", "sweep": {}}
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)   # > L2, rewritten between steps
+    for S in args.prefill_seqs:
+        with torch.cuda.stream(stream):
+            cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(1, KVH, D, H), S, batch=1, dtype="bf16")
+            rope = b2a.RopeTable(ctx, D, THETA, S)
+            q = torch.randn(S, H, D, device=dev).bfloat16()
+            k = torch.randn(S, KVH, D, device=dev).bfloat16()
+            v = torch.randn(S, KVH, D, device=dev).bfloat16()
+            o = torch.empty(S, H, D, device=dev, dtype=torch.bfloat16)
+        flops = 4 * D * H * S * (S + 1) / 2
+        steps = max(3, min(50, int(2e9 / max(flops, 1))))
+        for _ in range(3):
+            b2a.attentionPrefill(ctx, cache, rope, 0, q, k, v, o, S, H)
+        total = 0.0
+        ctx.enable_timing(True)
+        for _ in range(steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            b2a.attentionPrefill(ctx, cache, rope, 0, q, k, v, o, S, H)
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            total += a.elapsed_time(b)
+        kt = ctx.read_timing()
+        ctx.enable_timing(False)
+        attn = "prefill_tc" if "prefill_tc" in kt else ("attention_simt" if "attention_simt" in kt else None)
+        kms = kt[attn][1] / kt[attn][0] if attn else None
+        res["sweep"][str(S)] = {"ms": round(total / steps, 4), "tflops": round(flops / (total / steps / 1e3) / 1e12, 3),
+                                "kernel": attn, "kernel_ms": round(kms, 4) if kms else None,
+                                "kernel_tflops": round(flops / (kms / 1e3) / 1e12, 3) if kms else None,
+                                "launches_per_step": sum(x[0] for x in kt.values()) / steps}
+        cache.close()
+        rope.close()
+    main = res["sweep"].get("512") or next(iter(res["sweep"].values()))
+    res["value"] = main["tflops"]
+    res["config"] = {"workload": "config2-causal-prefill", "seq": 512, "heads": "14q/2kv", "head_dim": D,
+                     "flops": "4*D*H*S(S+1)/2", "l2": "flushed (256 MiB write) between timed steps"}
+    best_s = max(res["sweep"], key=lambda s: res["sweep"][s]["kernel_tflops"] or 0)
+    bk = res["sweep"][best_s]
+    if bk["kernel_tflops"]:
+        res["roofline"] = {"bound": "tensor", "kernel": bk["kernel"], "seq": int(best_s),
+                           "achieved": bk["kernel_tflops"], "peak": pk["bf16_tflops"], "peak_source": pk["source"],
+                           "unit": "TFLOP/s", "frac": round(bk["kernel_tflops"] / pk["bf16_tflops"], 4),
+                           "traffic": ncu_traffic(bk["kernel"], f"prefill{best_s}")}
+    return res
+
+
+# -------------------------------------------------------------- reference ---
+
+def run_reference(args) -> None:
+    """The reference's CPU attention path (restated in C: no JS runtime exists here),
+    all host threads, rank 0 only, same metric and workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle import oracle as o
+    o.build()
+    lengths = config3_lengths(0)
+    # each step: a bounded sample of config 3 sized so the whole run ends in ~2 minutes
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rng = np.random.default_rng(99)
+    cap = int(lengths.max()) + 1
+    seq_stride = KVH * cap * D
+    kb = rng.standard_normal(SEQS * seq_stride, dtype=np.float32).astype(np.float16).view(np.uint16)
+    vb = rng.standard_normal(SEQS * seq_stride, dtype=np.float32).astype(np.float16).view(np.uint16)
+    q = rng.standard_normal(SEQS * H * D, dtype=np.float32)
+    per_seq = config3_bytes(lengths)["step"] / LAYERS / SEQS
+    t0 = time.perf_counter()
+    _, used = o.batched_decode_f16(q, H * D, kb, vb, seq_stride, lengths, SEQS, cap, H, KVH, D, H * D, 0)
+    t_layer = time.perf_counter() - t0
+    nseq = max(1, min(SEQS, int(SEQS * budget / max(t_layer, 1e-6))))
+    sel = np.arange(nseq)
+    sample_bytes = per_seq * nseq
+    for _ in range(args.warmup):
+        o.batched_decode_f16(q, H * D, kb, vb, seq_stride, lengths[sel], nseq, cap, H, KVH, D, H * D, 0)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        o.batched_decode_f16(q, H * D, kb, vb, seq_stride, lengths[sel], nseq, cap, H, KVH, D, H * D, 0)
+    dt = time.perf_counter() - t0
+    value = sample_bytes * args.steps / dt / 1e9
+    sample = f"{nseq} of {SEQS} sequences x 1 layer of config 3 per step ({sample_bytes / 1e6:.1f} MB)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config3-batched-decode", "sequences_per_gpu": SEQS, "layers": LAYERS,
+                   "heads": "14q/2kv", "head_dim": D, "kv_len": f"U{{{LMIN}..{LMAX}}} seeded per rank",
+                   "cache_dtype": "f16"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": used, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference is JavaScript (src/core/attention.js); no JS runtime exists on this machine, "
+                 "so its CPU path runs as the C restatement in oracle/ with f64 accumulation, all host threads"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -76,6 +76,19 @@ b2a_status b2a_destroy(b2a_ctx* ctx);
 b2a_status b2a_set_stream(b2a_ctx* ctx, void* cuda_stream);
 b2a_status b2a_synchronize(b2a_ctx* ctx);
 
+/* ---- per-kernel device timing (GpuContext.timed, src/gpu/device.js:301-338) --
+ * While enabled, every kernel the context launches is bracketed by CUDA events
+ * on its stream. b2a_timing_read waits for the stream, then reports per kernel
+ * kind the launch count and summed device milliseconds since the last read,
+ * and clears them. */
+typedef struct b2a_kernel_time {
+  char name[32];
+  int launches;
+  double total_ms;
+} b2a_kernel_time;
+b2a_status b2a_timing_enable(b2a_ctx* ctx, int enable);
+b2a_status b2a_timing_read(b2a_ctx* ctx, b2a_kernel_time* out, int max_entries, int* n_entries);
+
 /* ---- host-side helpers (no device work) ---------------------------------- */
 /* kvHeadFor, src/core/attention.js:74-76. Returns -1 for an invalid grouping. */
 int b2a_kv_head_for(int query_head, int num_heads, int num_kv_heads);

@@ -30,6 +30,8 @@ SIGNATURES = {
     "b2a_destroy": (_i, [_vp]),
     "b2a_set_stream": (_i, [_vp, _vp]),
     "b2a_synchronize": (_i, [_vp]),
+    "b2a_timing_enable": (_i, [_vp, _i]),
+    "b2a_timing_read": (_i, [_vp, _vp, _i, _ip]),
     "b2a_kv_head_for": (_i, [_i, _i, _i]),
     "b2a_rope_frequencies": (_i, [_i, _d, ctypes.POINTER(ctypes.c_double)]),
     "b2a_rope_tables": (_i, [_i, _d, _i, _f32p, _f32p]),

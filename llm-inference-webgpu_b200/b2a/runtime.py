@@ -119,6 +119,21 @@ class Context:
     def synchronize(self) -> None:
         check(self._lib.b2a_synchronize(self.handle))
 
+    def enable_timing(self, on: bool = True) -> None:
+        """Bracket every kernel launch with CUDA events (GpuContext.timed, src/gpu/device.js:301-338)."""
+        check(self._lib.b2a_timing_enable(self.handle, 1 if on else 0))
+
+    def read_timing(self) -> dict:
+        """{kernel kind: (launches, total device ms)} since the last read; waits for the stream."""
+        entries = (_KernelTime * 16)()
+        n = ctypes.c_int()
+        check(self._lib.b2a_timing_read(self.handle, entries, 16, ctypes.byref(n)))
+        return {entries[i].name.decode(): (entries[i].launches, entries[i].total_ms) for i in range(n.value)}
+
+
+class _KernelTime(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("launches", ctypes.c_int), ("total_ms", ctypes.c_double)]
+
 
 class RopeTable:
     """f64 cos/sin for positions 0..maxPositions-1 on the device (ropeTables, src/core/ops.js:123-136,

@@ -26,6 +26,47 @@ b2a_status cuda_fail(cudaError_t e, const char* what) {
   return fail(B2A_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
+const char* const kKernelNames[K_NUM_KINDS] = {"attention_simt", "attention_mma", "combine", "rope_append",
+                                               "write_at", "grouped_generic", "prefill_tc"};
+
+namespace {
+cudaEvent_t take_event(b2a_ctx* ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+}  // namespace
+
+KernelTimer::KernelTimer(b2a_ctx* ctx, int kind) : ctx_(ctx), kind_(kind) {
+  if (!ctx_->timing) {
+    done_ = true;
+    return;
+  }
+  start_ = take_event(ctx_);
+  if (start_ == nullptr) {
+    done_ = true;
+    return;
+  }
+  cudaEventRecord(start_, ctx_->stream);
+}
+
+void KernelTimer::stop() {
+  if (done_) return;
+  done_ = true;
+  cudaEvent_t stop = take_event(ctx_);
+  if (stop == nullptr) {
+    ctx_->event_pool.push_back(start_);
+    return;
+  }
+  cudaEventRecord(stop, ctx_->stream);
+  ctx_->timing_recs.push_back({kind_, start_, stop});
+}
+
 }  // namespace b2a
 
 using namespace b2a;
@@ -77,6 +118,41 @@ b2a_status ensure_buffer(void** buf, size_t* cap, size_t need, const char* what)
 
 bool valid_dtype(int d) { return d == B2A_F32 || d == B2A_F16 || d == B2A_BF16; }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library needs no link-time libcuda and still loads on a machine without one.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  }
+  return fn;
+}
+
+// A pool of `rows` rows of 64 16-bit elements (128 bytes) viewed as a 2D
+// tensor; each load is a 64-row box with the 128-byte swizzle the ldmatrix
+// reads of the tensor-core decode expect.
+bool encode_pool_map(CUtensorMap* map, void* base, uint64_t rows, b2a_dtype dtype) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr || rows >= (1ull << 32)) return false;
+  cuuint64_t dims[2] = {64, rows};
+  cuuint64_t strides[1] = {128};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype == B2A_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base,
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Carves device staging for host-pointer calls: each `add` reserves an
 // aligned slice of ctx->d_stage.
 struct Stage {
@@ -99,12 +175,24 @@ b2a_status h2d(b2a_ctx* ctx, void* dst, const void* src, size_t bytes) {
   return B2A_OK;
 }
 
+// Reads and clears the device error word after the stream is idle: a kernel
+// whose bounded wait gave up reports it there instead of hanging.
+b2a_status check_device_error(b2a_ctx* ctx) {
+  int32_t err = 0;
+  B2A_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(err), cudaMemcpyDeviceToHost), "reading the device error word");
+  if (err != 0) {
+    cudaMemset(ctx->d_err, 0, sizeof(err));
+    return fail(B2A_ETIMEDOUT, "a device-side wait gave up (error word 0x%x); results of that call are invalid", err);
+  }
+  return B2A_OK;
+}
+
 b2a_status d2h_sync(b2a_ctx* ctx, void* dst, const void* src, size_t bytes) {
   if (bytes) {
     B2A_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "copying results to the host");
   }
   B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the results");
-  return B2A_OK;
+  return check_device_error(ctx);
 }
 
 b2a_status check_cache_shape(const b2a_kvcache* c, const b2a_rope* rope, int num_heads) {
@@ -148,27 +236,37 @@ AttnParams base_params(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope) {
 // Splits every query row's keys into chunks, runs the attention kernel into
 // the context's scratch, and merges the chunks into `out` (mode 0) or into a
 // merged partial (mode 1). max_keys: the longest row's key count.
-b2a_status run_split_kv(b2a_ctx* ctx, AttnParams& p, int max_keys, void* out, int out_dtype, int mode) {
+b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int max_keys, void* out,
+                        int out_dtype, int mode) {
   const int64_t rows = static_cast<int64_t>(p.batch) * p.num_layers * p.tokens * p.heads;
   if (rows == 0) return B2A_OK;
+  if (c->has_tmaps) {
+    p.tmap_k = &c->tmap_k;
+    p.tmap_v = &c->tmap_v;
+  }
   const bool mma = attn_mma_supported(p);
   p.chunk = 256;
+  int64_t items = 0;
   if (mma) {
-    // Enough chunks for several waves over the SMs, but no chunk under 256 positions.
-    const int64_t groups = static_cast<int64_t>(p.batch) * p.num_layers * p.tokens * p.kv_heads;
-    int64_t want = 4LL * ctx->sm_count;
-    int64_t per = groups > 0 ? (want + groups - 1) / groups : 1;
-    int chunk = static_cast<int>((max_keys + per - 1) / per);
-    chunk = (chunk + 255) / 256 * 256;
-    if (chunk < 256) chunk = 256;
-    p.chunk = chunk;
+    // The longest chunk that still gives every SM several work items (three
+    // CTAs fit per SM); chunks are whole 64-position tiles.
+    const int64_t want = 12LL * ctx->sm_count;
+    for (int chunk : {4096, 2048, 1024, 512, 256}) {
+      p.chunk = chunk;
+      items = attn_mma_items(p, c->len.data());
+      if (items >= want) break;
+    }
   }
   p.nchunks = max_keys > 0 ? (max_keys + p.chunk - 1) / p.chunk : 1;
   const size_t need = static_cast<size_t>(rows) * p.nchunks * (p.head_dim + 4) * sizeof(float);
   b2a_status s = ensure_buffer(&ctx->d_scratch, &ctx->d_scratch_bytes, need, "allocating split-KV scratch");
   if (s != B2A_OK) return s;
   p.partial = static_cast<float*>(ctx->d_scratch);
-  cudaError_t e = mma ? launch_attn_mma(p, ctx->sm_count, ctx->stream) : launch_attn_simt(p, ctx->stream);
+  cudaError_t e;
+  {
+    KernelTimer kt(ctx, mma ? K_ATTN_MMA : K_ATTN_SIMT);
+    e = mma ? launch_attn_mma(p, items, ctx->stream) : launch_attn_simt(p, ctx->stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launching the attention kernel");
   CombineParams cp{};
   cp.partial = p.partial;
@@ -179,7 +277,17 @@ b2a_status run_split_kv(b2a_ctx* ctx, AttnParams& p, int max_keys, void* out, in
   cp.out = out;
   cp.out_dtype = out_dtype;
   cp.mode = mode;
-  e = launch_combine(cp, ctx->stream);
+  cp.len = p.len;
+  cp.seq_begin = p.seq_begin;
+  cp.chunk = p.chunk;
+  cp.extra = p.horizon_extra;
+  cp.tokens = p.tokens;
+  cp.heads = p.heads;
+  cp.num_layers = p.num_layers;
+  {
+    KernelTimer kt(ctx, K_COMBINE);
+    e = launch_combine(cp, ctx->stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launching the split-KV combine");
   return B2A_OK;
 }
@@ -253,6 +361,11 @@ b2a_status b2a_destroy(b2a_ctx* ctx) {
   if (ctx->d_scratch) cudaFree(ctx->d_scratch);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->d_positions) cudaFree(ctx->d_positions);
+  for (auto& r : ctx->timing_recs) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  for (auto ev : ctx->event_pool) cudaEventDestroy(ev);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
   return B2A_OK;
@@ -269,6 +382,42 @@ b2a_status b2a_synchronize(b2a_ctx* ctx) {
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
   B2A_CUDA(cudaStreamSynchronize(ctx->stream), "synchronizing the stream");
+  return check_device_error(ctx);
+}
+
+b2a_status b2a_timing_enable(b2a_ctx* ctx, int enable) {
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  ctx->timing = enable != 0;
+  return B2A_OK;
+}
+
+b2a_status b2a_timing_read(b2a_ctx* ctx, b2a_kernel_time* out, int max_entries, int* n_entries) {
+  if (out == nullptr || n_entries == nullptr || max_entries < 0) return fail(B2A_EINVAL, "null argument");
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for timed kernels");
+  int launches[K_NUM_KINDS] = {0};
+  double ms[K_NUM_KINDS] = {0};
+  for (auto& r : ctx->timing_recs) {
+    float t = 0.f;
+    if (cudaEventElapsedTime(&t, r.start, r.stop) == cudaSuccess) {
+      launches[r.kind]++;
+      ms[r.kind] += t;
+    }
+    ctx->event_pool.push_back(r.start);
+    ctx->event_pool.push_back(r.stop);
+  }
+  ctx->timing_recs.clear();
+  int n = 0;
+  for (int k = 0; k < K_NUM_KINDS && n < max_entries; k++) {
+    if (launches[k] == 0) continue;
+    snprintf(out[n].name, sizeof(out[n].name), "%s", kKernelNames[k]);
+    out[n].launches = launches[k];
+    out[n].total_ms = ms[k];
+    n++;
+  }
+  *n_entries = n;
   return B2A_OK;
 }
 
@@ -414,6 +563,10 @@ b2a_status b2a_kvcache_create(b2a_ctx* ctx, int num_layers, int num_kv_heads, in
     delete c;
     return cuda_fail(e, "allocating the KV cache");
   }
+  if (dtype != B2A_F32 && head_dim == 64) {
+    const uint64_t rows = static_cast<uint64_t>(batch) * num_layers * num_kv_heads * capacity;
+    c->has_tmaps = encode_pool_map(&c->tmap_k, c->d_k, rows, dtype) && encode_pool_map(&c->tmap_v, c->d_v, rows, dtype);
+  }
   *out = c;
   return B2A_OK;
 }
@@ -542,7 +695,11 @@ b2a_status b2a_kvcache_write_at(b2a_ctx* ctx, b2a_kvcache* c, int layer, int seq
     dk = st.ptr(ctx, ik);
     dv = st.ptr(ctx, iv);
   }
-  cudaError_t e = launch_write_at(c, layer, seq_idx, at, dk, dv, static_cast<int>(src_dtype), count, ctx->stream);
+  cudaError_t e;
+  {
+    KernelTimer kt(ctx, K_WRITE_AT);
+    e = launch_write_at(c, layer, seq_idx, at, dk, dv, static_cast<int>(src_dtype), count, ctx->stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launching writeAt");
   if (flags == B2A_HOST) return d2h_sync(ctx, nullptr, nullptr, 0);
   return B2A_OK;
@@ -606,7 +763,11 @@ b2a_status b2a_append_rope(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, i
     p.k_new = st.ptr(ctx, ik);
     p.v_new = st.ptr(ctx, iv);
   }
-  cudaError_t e = launch_rope_append(p, seq_idx, count, ctx->stream);
+  cudaError_t e;
+  {
+    KernelTimer kt(ctx, K_ROPE_APPEND);
+    e = launch_rope_append(p, seq_idx, count, ctx->stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launching the rope append");
   if (flags == B2A_HOST) return d2h_sync(ctx, nullptr, nullptr, 0);
   return B2A_OK;
@@ -672,7 +833,7 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* ro
     }
     dout = st.ptr(ctx, io);
   }
-  if ((s = run_split_kv(ctx, p, max_keys, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
+  if ((s = run_split_kv(ctx, c, p, max_keys, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
   if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
   return B2A_OK;
 }
@@ -730,11 +891,15 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* r
   }
   // RoPE(K) + append first (src/cpu/model.js:116 writes before attending), then
   // causal attention over past+count with RoPE(Q) fused into the Q load.
-  cudaError_t e = launch_rope_append(p, seq_idx, count, ctx->stream);
+  cudaError_t e;
+  {
+    KernelTimer kt(ctx, K_ROPE_APPEND);
+    e = launch_rope_append(p, seq_idx, count, ctx->stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launching the rope append");
   p.k_new = nullptr;
   p.v_new = nullptr;
-  if ((s = run_split_kv(ctx, p, past + count, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
+  if ((s = run_split_kv(ctx, c, p, past + count, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
   if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
   return B2A_OK;
 }
@@ -772,7 +937,11 @@ b2a_status b2a_grouped_attention(b2a_ctx* ctx, const float* q, const float* keys
     dv = static_cast<const float*>(st.ptr(ctx, iv));
     dout = static_cast<float*>(st.ptr(ctx, io));
   }
-  cudaError_t e = launch_grouped_generic(dq, dk, dv, dout, seq, past, num_heads, num_kv_heads, head_dim, ctx->stream);
+  cudaError_t e;
+  {
+    KernelTimer kt(ctx, K_GROUPED);
+    e = launch_grouped_generic(dq, dk, dv, dout, seq, past, num_heads, num_kv_heads, head_dim, ctx->stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launching groupedAttention");
   if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, q_bytes);
   return B2A_OK;
@@ -842,7 +1011,7 @@ b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* c, const b2a_
     p.q_pos = static_cast<const int32_t*>(st.ptr(ctx, ipos));
     dpart = static_cast<float*>(st.ptr(ctx, ip));
   }
-  if ((s = run_split_kv(ctx, p, max_keys, dpart, B2A_F32, 1)) != B2A_OK) return s;
+  if ((s = run_split_kv(ctx, c, p, max_keys, dpart, B2A_F32, 1)) != B2A_OK) return s;
   if (flags == B2A_HOST) return d2h_sync(ctx, partial, dpart, part_bytes);
   return B2A_OK;
 }

@@ -1,6 +1,7 @@
 // Internal declarations shared by the C ABI (api.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -26,7 +27,36 @@ struct b2a_ctx {
   int32_t* d_err = nullptr;             // device error word (bounded waits, bounds checks)
   int32_t* d_positions = nullptr;       // staging for host q_positions
   int d_positions_cap = 0;
+  // per-kernel timing (b2a_timing_enable / b2a_timing_read)
+  bool timing = false;
+  struct TimingRec {
+    int kind;
+    cudaEvent_t start, stop;
+  };
+  std::vector<TimingRec> timing_recs;
+  std::vector<cudaEvent_t> event_pool;
 };
+
+namespace b2a {
+// Kernel kinds reported by b2a_timing_read.
+enum KernelKind { K_ATTN_SIMT = 0, K_ATTN_MMA, K_COMBINE, K_ROPE_APPEND, K_WRITE_AT, K_GROUPED, K_PREFILL_TC,
+                  K_NUM_KINDS };
+extern const char* const kKernelNames[K_NUM_KINDS];
+
+// Brackets one launch with events on the context's stream while timing is on.
+class KernelTimer {
+ public:
+  KernelTimer(b2a_ctx* ctx, int kind);
+  void stop();
+  ~KernelTimer() { stop(); }
+
+ private:
+  b2a_ctx* ctx_;
+  int kind_;
+  cudaEvent_t start_ = nullptr;
+  bool done_ = false;
+};
+}  // namespace b2a
 
 struct b2a_rope {
   b2a_ctx* ctx = nullptr;   // creating context; not used after creation
@@ -48,6 +78,11 @@ struct b2a_kvcache {
   int32_t* d_len = nullptr;     // device mirror of len, updated in stream order
   std::vector<int32_t> len;     // committed length per sequence (host truth)
   int64_t s_seq = 0, s_layer = 0, s_head = 0;  // element strides; position stride = head_dim
+  // 2D TMA views of the pools as [rows][head_dim] with 64-row boxes and
+  // 128-byte swizzle (f16/bf16, head_dim 64); has_tmaps false otherwise
+  bool has_tmaps = false;
+  CUtensorMap tmap_k;
+  CUtensorMap tmap_v;
 };
 
 namespace b2a {
@@ -82,6 +117,8 @@ struct AttnParams {
   int chunk;                  // positions per chunk (multiple of 64)
   int nchunks;                // chunks per row (max over rows)
   int32_t* err;
+  const void* tmap_k;         // host CUtensorMap* of the pools (tensor-core path), or null
+  const void* tmap_v;
 };
 
 struct CombineParams {
@@ -92,6 +129,10 @@ struct CombineParams {
   void* out;                  // mode 0: [rows][D] in out_dtype; mode 1: merged partial [rows][D+4] f32
   int out_dtype;
   int mode;
+  // chunked layout only: when len is set, row (b, layer, t, head) holds
+  // max(1, ceil((len[seq_begin+b] + t + extra) / chunk)) valid chunks
+  const int32_t* len;
+  int seq_begin, chunk, extra, tokens, heads, num_layers;
 };
 
 cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st);
@@ -102,7 +143,8 @@ cudaError_t launch_read(const b2a_kvcache* c, int layer, int seq_idx, int n, voi
 cudaError_t launch_lengths_update(int32_t* d_len, int idx, int batch, int count, int mode, cudaStream_t st);
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t st);
 bool attn_mma_supported(const AttnParams& p);
-cudaError_t launch_attn_mma(const AttnParams& p, int sm_count, cudaStream_t st);
+int64_t attn_mma_items(const AttnParams& p, const int32_t* host_len);
+cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
 cudaError_t launch_grouped_generic(const float* q, const float* k, const float* v, float* out, int seq,
                                    int past, int heads, int kv_heads, int head_dim, cudaStream_t st);

@@ -178,14 +178,24 @@ cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// One warp per output row (b, layer, t, head): merge `parts` partials in
+// One warp per output row (b, layer, t, head): merge the row's partials in
 // ascending order. m* = max m_i, w_i = 2^(m_i - m*), out = sum w_i o_i / sum w_i l_i.
-__global__ void k_combine(const float* partial, int64_t rows, int parts, int D, int64_t row_stride,
-                          int64_t part_stride, void* out, int out_dtype, int mode) {
+__global__ void k_combine(CombineParams p, int64_t row_stride, int64_t part_stride) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const float* base = partial + row * row_stride;
+  const int D = p.head_dim;
+  if (row >= p.rows) return;
+  int parts = p.nchunks;
+  if (p.len != nullptr) {   // chunks this row actually wrote
+    int64_t r = row / p.heads;
+    const int t = static_cast<int>(r % p.tokens);
+    r /= p.tokens;
+    const int b = static_cast<int>(r / p.num_layers);
+    const int nk = p.len[p.seq_begin + b] + t + p.extra;
+    parts = nk > 0 ? (nk + p.chunk - 1) / p.chunk : 1;
+    if (parts > p.nchunks) parts = p.nchunks;
+  }
+  const float* base = p.partial + row * row_stride;
   float m = -CUDART_INF_F;
   for (int i = 0; i < parts; i++) {
     const float* pp = base + i * part_stride;
@@ -205,8 +215,8 @@ __global__ void k_combine(const float* partial, int64_t rows, int parts, int D, 
       if (d < D) acc[k] = fmaf(w, pp[d], acc[k]);
     }
   }
-  if (mode == 1) {   // merged partial: o and l rescaled to the common max m
-    float* o = static_cast<float*>(out) + row * (D + 4);
+  if (p.mode == 1) {   // merged partial: o and l rescaled to the common max m
+    float* o = static_cast<float*>(p.out) + row * (D + 4);
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       const int d = lane + 32 * k;
@@ -219,7 +229,7 @@ __global__ void k_combine(const float* partial, int64_t rows, int parts, int D, 
 #pragma unroll
   for (int k = 0; k < 4; k++) {
     const int d = lane + 32 * k;
-    if (d < D) st_from_f32(out, row * D + d, out_dtype, acc[k] * inv);
+    if (d < D) st_from_f32(p.out, row * D + d, p.out_dtype, acc[k] * inv);
   }
 }
 
@@ -232,9 +242,7 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
                                                 : static_cast<int64_t>(p.nchunks) * (p.head_dim + 4);
   const int threads = 256;
   const int64_t blocks = (static_cast<int64_t>(p.rows) * 32 + threads - 1) / threads;
-  k_combine<<<static_cast<unsigned>(blocks), threads, 0, st>>>(p.partial, p.rows, p.nchunks, p.head_dim,
-                                                                stride_row, stride_part, p.out, p.out_dtype,
-                                                                p.mode);
+  k_combine<<<static_cast<unsigned>(blocks), threads, 0, st>>>(p, stride_row, stride_part);
   return cudaGetLastError();
 }
 

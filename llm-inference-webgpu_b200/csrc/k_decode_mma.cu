@@ -1,7 +1,515 @@
-// Tensor-core split-KV decode (placeholder until the kernel lands).
+// Split-KV flash-decode on the tensor cores, for f16 / bf16 caches with
+// head_dim 64 and up to 8 query heads per KV head (Qwen2.5: 7).
+//
+// One CTA owns one work item (sequence b, layer, KV head g, chunk of
+// positions). A producer warp streams 64-position K and V tiles of the
+// head-major cache into shared memory with 2D TMA (128-byte swizzle, one
+// tensor map over the whole pool) through a 4-stage mbarrier ring; four
+// consumer warps each take 16 positions of every tile:
+//
+//   S^T[16 pos x 8 heads] = K[16 x 64] . Q^T[64 x 8]       (4 x mma m16n8k16)
+//   online softmax per head (a head's column lives in 8 lanes of one warp)
+//   O^T[64 x 8]         += V^T[64 x 16] . P^T[16 x 8]       (4 x mma m16n8k16)
+//
+// K is the A operand, so the 7 query heads of a group fill the n=8 side of the
+// MMA instead of padding a 16-row tile. P^T reaches B-fragment layout with two
+// movmatrix transposes, and V^T is read with ldmatrix.trans. For bf16 the
+// query and the probabilities are split into a bf16 high part and a bf16
+// residual (two MMAs each), which keeps ~16 mantissa bits on both products.
+// At the end the four warps' (m, l, O) merge in shared memory into one
+// unnormalised partial per query head; k_combine (k_attn_simt.cu) merges the
+// chunks. RoPE(q) and the fused append of the new token's K/V happen in the
+// prologue, in f64 from the host-built table, exactly as the CUDA-core path.
+#include <cuda.h>
+#include <math_constants.h>
+
+#include <type_traits>
+
 #include "b2a_internal.cuh"
+#include "k_util.cuh"
 
 namespace b2a {
-bool attn_mma_supported(const AttnParams&) { return false; }
-cudaError_t launch_attn_mma(const AttnParams&, int, cudaStream_t) { return cudaErrorNotSupported; }
+
+namespace {
+
+constexpr int kD = 64;
+constexpr int kTile = 64;                 // positions per TMA box
+constexpr int kStages = 4;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kTileBytes = kTile * kD * 2;          // 8 KiB per K or V tile
+constexpr int kStageBytes = 2 * kTileBytes;
+constexpr int kSmemRing = kStages * kStageBytes;   // 64 KiB
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at 1.9 GHz, then give up
+constexpr int kErrTimeout = 1;
+
+struct __align__(16) MergeSmem {
+  float o[kConsumerWarps][8][kD];
+  float m[kConsumerWarps][8];
+  float l[kConsumerWarps][8];
+  int item[4];
+};
+
+constexpr int kSmemTotal = kSmemRing + static_cast<int>(sizeof(MergeSmem)) + 2 * kStages * 8 + 1024;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after ~2 s, records the timeout in the error word and
+// returns false; the caller carries on so no thread of the CTA can hang.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      if (err) atomicOr(err, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1);
+
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two floats packed as the MMA input type (RNE), low half = first.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v);
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+  return __half22float2(*reinterpret_cast<__half2*>(&v));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
+}
+
+// Byte offset of (row, 16-byte chunk) in a 128-byte-swizzled tile of 128-byte rows.
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+}  // namespace
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 3)
+    k_decode_mma(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                 AttnParams p) {
+  constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  MergeSmem& ms = *reinterpret_cast<MergeSmem*>(smem + kSmemRing);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmemRing + sizeof(MergeSmem));
+  uint64_t* empty = full + kStages;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- which work item: items are numbered sequence-major, each sequence
+  // contributing num_layers * kv_heads * chunks(b) of them.
+  if (warp == 0) {
+    const int item = blockIdx.x;
+    int base = 0;
+    int found_b = -1, found_off = 0, found_cnt = 0;
+    for (int b0 = 0; b0 < p.batch && found_b < 0; b0 += 32) {
+      const int b = b0 + lane;
+      int cnt = 0;
+      if (b < p.batch) {
+        const int nk = p.len[p.seq_begin + b] + p.horizon_extra;
+        cnt = nk > 0 ? (nk + p.chunk - 1) / p.chunk : 1;
+      }
+      int items = cnt * p.num_layers * p.kv_heads;
+      int incl = items;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int excl = incl - items;
+      const bool mine = b < p.batch && item >= base + excl && item < base + incl;
+      const unsigned mask = __ballot_sync(0xffffffffu, mine);
+      if (mask) {
+        const int src = __ffs(mask) - 1;
+        found_b = __shfl_sync(0xffffffffu, b, src);
+        found_off = item - base - __shfl_sync(0xffffffffu, excl, src);
+        found_cnt = __shfl_sync(0xffffffffu, cnt, src);
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      ms.item[0] = found_b;
+      ms.item[1] = found_off;
+      ms.item[2] = found_cnt;
+    }
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int b = ms.item[0];
+  if (b < 0) return;   // grid larger than the item count (cannot happen with the host's count)
+  const int off = ms.item[1];
+  const int cnt = ms.item[2];
+  const int c = off % cnt;
+  const int gl = off / cnt;
+  const int g = gl % p.kv_heads;
+  const int l = gl / p.kv_heads;
+  const int G = p.group;
+  const int bc = p.seq_begin + b;
+
+  const int past = p.len[bc];
+  const int pos_q = p.q_pos ? p.q_pos[b] : past;
+  const int n_keys = past + p.horizon_extra;
+  const int p0 = c * p.chunk;
+  const int p1 = min(p0 + p.chunk, n_keys);
+  const int64_t cache_base = bc * p.s_seq + static_cast<int64_t>(p.layer_begin + l) * p.s_layer + g * p.s_head;
+  const int row_base = static_cast<int>(cache_base / kD);
+  const double* cosr = p.rope_cos + static_cast<int64_t>(pos_q) * (kD / 2);
+  const double* sinr = p.rope_sin + static_cast<int64_t>(pos_q) * (kD / 2);
+
+  // ---- fused append of the new token (the CTA whose chunk holds the slot)
+  if (p.k_new != nullptr && past >= p0 && past < p1) {
+    if (tid < kD / 2) {
+      const int j = tid;
+      const int64_t src = ((static_cast<int64_t>(b) * p.num_layers + l) * p.kv_heads + g) * kD;
+      const int64_t dst = cache_base + static_cast<int64_t>(past) * kD;
+      float lo, hi;
+      rope_pair_f64(ld_as_f32(p.k_new, src + j, p.in_dtype), ld_as_f32(p.k_new, src + j + kD / 2, p.in_dtype),
+                    cosr[j], sinr[j], lo, hi);
+      st_from_f32(p.kc_w, dst + j, p.cache_dtype, lo);
+      st_from_f32(p.kc_w, dst + j + kD / 2, p.cache_dtype, hi);
+      convert_elem(p.v_new, src + j, p.in_dtype, p.vc_w, dst + j, p.cache_dtype);
+      convert_elem(p.v_new, src + j + kD / 2, p.in_dtype, p.vc_w, dst + j + kD / 2, p.cache_dtype);
+      // the tensor-memory-access (async proxy) loads below must see these stores
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    __syncthreads();
+  }
+
+  const int ntiles = (p1 - p0 + kTile - 1) / kTile;
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      for (int i = 0; i < ntiles; i++) {
+        const int s = i % kStages;
+        if (i >= kStages) mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.err);
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        unsigned char* st = smem + s * kStageBytes;
+        const int y = row_base + p0 + i * kTile;
+        tma_load_2d(st, &tmap_k, &full[s], 0, y);
+        tma_load_2d(st + kTileBytes, &tmap_v, &full[s], 0, y);
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int gq = lane >> 2, tq = lane & 3;
+  // Q^T B-fragments for head gq (zero for padding heads): b0 = dims 16ks+2tq..+1,
+  // b1 = dims 16ks+8+2tq..+1. RoPE pairs (j, j+32) are both held by this thread.
+  uint32_t qb[4][2];
+  uint32_t qlo[4][2];
+  {
+    float qv[4][4];
+    const bool valid = gq < G;
+    const int64_t qrow = ((static_cast<int64_t>(b) * p.num_layers + l) * p.heads + g * G + (valid ? gq : 0)) * kD;
+#pragma unroll
+    for (int ks = 0; ks < 2; ks++) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int j = 16 * ks + (e >> 1) * 8 + 2 * tq + (e & 1);   // j < 32
+        float lo = 0.f, hi = 0.f;
+        if (valid) {
+          rope_pair_f64(ld_as_f32(p.q, qrow + j, p.in_dtype), ld_as_f32(p.q, qrow + j + 32, p.in_dtype), cosr[j],
+                        sinr[j], lo, hi);
+        }
+        qv[ks][e] = lo;
+        qv[ks + 2][e] = hi;
+      }
+    }
+#pragma unroll
+    for (int ks = 0; ks < 4; ks++) {
+      qb[ks][0] = pack2<T>(qv[ks][0], qv[ks][1]);
+      qb[ks][1] = pack2<T>(qv[ks][2], qv[ks][3]);
+      if (kSplit) {
+        const float2 h0 = unpack2<T>(qb[ks][0]), h1 = unpack2<T>(qb[ks][1]);
+        qlo[ks][0] = pack2<T>(qv[ks][0] - h0.x, qv[ks][1] - h0.y);
+        qlo[ks][1] = pack2<T>(qv[ks][2] - h1.x, qv[ks][3] - h1.y);
+      }
+    }
+  }
+
+  const float sc = rsqrtf(static_cast<float>(kD)) * kLog2e;   // score -> base-2 exponent
+  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F;                // raw-score max, heads 2tq, 2tq+1
+  float l0 = 0.f, l1 = 0.f;                                    // this thread's share of the sums
+  float o[4][4];
+#pragma unroll
+  for (int mb = 0; mb < 4; mb++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[mb][e] = 0.f;
+
+  const uint32_t ring = smem_u32(smem);
+  for (int i = 0; i < ntiles; i++) {
+    const int s = i % kStages;
+    mbar_wait(&full[s], (i / kStages) & 1, p.err);
+    const int valid = min(kTile, p1 - (p0 + i * kTile)) - 16 * warp;   // positions of my 16 that exist
+    if (valid > 0) {
+      const uint32_t kt = ring + s * kStageBytes;
+      const uint32_t vt = kt + kTileBytes;
+      if (valid < 16) {
+        // zero V rows past the end so 0 * (stale bits) cannot make NaN
+        unsigned char* vrow = smem + s * kStageBytes + kTileBytes + (16 * warp + valid) * 128;
+        for (int x = lane; x < (16 - valid) * 8; x += 32) reinterpret_cast<uint4*>(vrow)[x] = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+      }
+      // S^T = K . Q^T
+      float st[4] = {0.f, 0.f, 0.f, 0.f};
+      const int r = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int ks = 0; ks < 4; ks++) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(kt + swz(r, 2 * ks + (lane >> 4)), a0, a1, a2, a3);
+        mma16816<T>(st, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+        if (kSplit) mma16816<T>(st, a0, a1, a2, a3, qlo[ks][0], qlo[ks][1]);
+      }
+      if (valid < 16) {
+        if (gq >= valid) st[0] = st[1] = -CUDART_INF_F;
+        if (gq + 8 >= valid) st[2] = st[3] = -CUDART_INF_F;
+      }
+      // online softmax, heads 2tq (st[0], st[2]) and 2tq+1 (st[1], st[3])
+      float t0 = fmaxf(st[0], st[2]), t1 = fmaxf(st[1], st[3]);
+#pragma unroll
+      for (int x = 4; x < 32; x <<= 1) {
+        t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, x));
+        t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, x));
+      }
+      const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);
+      const float a0s = (m0 == -CUDART_INF_F) ? 0.f : exp2f((m0 - n0) * sc);
+      const float a1s = (m1 == -CUDART_INF_F) ? 0.f : exp2f((m1 - n1) * sc);
+      m0 = n0;
+      m1 = n1;
+      const float nb0 = -n0 * sc, nb1 = -n1 * sc;
+      const float p00 = exp2f(fmaf(st[0], sc, nb0)), p01 = exp2f(fmaf(st[1], sc, nb1));
+      const float p10 = exp2f(fmaf(st[2], sc, nb0)), p11 = exp2f(fmaf(st[3], sc, nb1));
+      l0 = fmaf(l0, a0s, p00 + p10);
+      l1 = fmaf(l1, a1s, p01 + p11);
+#pragma unroll
+      for (int mb = 0; mb < 4; mb++) {
+        o[mb][0] *= a0s;
+        o[mb][2] *= a0s;
+        o[mb][1] *= a1s;
+        o[mb][3] *= a1s;
+      }
+      // P^T as B fragments: transpose [pos][head] 8x8 blocks into [head][pos]
+      const uint32_t pk0 = pack2<T>(p00, p01), pk1 = pack2<T>(p10, p11);
+      const uint32_t pb0 = movmatrix_t(pk0), pb1 = movmatrix_t(pk1);
+      uint32_t pl0 = 0, pl1 = 0;
+      if (kSplit) {
+        const float2 h0 = unpack2<T>(pk0), h1 = unpack2<T>(pk1);
+        pl0 = movmatrix_t(pack2<T>(p00 - h0.x, p01 - h0.y));
+        pl1 = movmatrix_t(pack2<T>(p10 - h1.x, p11 - h1.y));
+      }
+      // O^T += V^T . P^T
+      const int vr = 16 * warp + (lane & 7) + (lane >> 4) * 8;
+#pragma unroll
+      for (int mb = 0; mb < 4; mb++) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(vt + swz(vr, 2 * mb + ((lane >> 3) & 1)), a0, a1, a2, a3);
+        mma16816<T>(o[mb], a0, a1, a2, a3, pb0, pb1);
+        if (kSplit) mma16816<T>(o[mb], a0, a1, a2, a3, pl0, pl1);
+      }
+      if (valid < 16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- merge the four warps: per head h, m* = max m_w, scale, sum
+#pragma unroll
+  for (int x = 4; x < 32; x <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, x);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, x);
+  }
+  if (gq == 0) {
+    ms.m[warp][2 * tq] = m0;
+    ms.m[warp][2 * tq + 1] = m1;
+    ms.l[warp][2 * tq] = l0;
+    ms.l[warp][2 * tq + 1] = l1;
+  }
+#pragma unroll
+  for (int mb = 0; mb < 4; mb++) {
+    ms.o[warp][2 * tq][16 * mb + gq] = o[mb][0];
+    ms.o[warp][2 * tq + 1][16 * mb + gq] = o[mb][1];
+    ms.o[warp][2 * tq][16 * mb + 8 + gq] = o[mb][2];
+    ms.o[warp][2 * tq + 1][16 * mb + 8 + gq] = o[mb][3];
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));   // consumers only
+
+  const int64_t row0 = (static_cast<int64_t>(b) * p.num_layers + l) * p.heads + g * G;
+  const int64_t part_row = static_cast<int64_t>(p.nchunks) * (kD + 4);
+  float* part = p.partial + (row0 * p.nchunks + c) * (kD + 4);
+  for (int idx = tid; idx < G * kD; idx += kConsumerWarps * 32) {
+    const int h = idx / kD, d = idx % kD;
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) mx = fmaxf(mx, ms.m[w][h]);
+    float acc = 0.f;
+    if (mx != -CUDART_INF_F) {
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; w++) {
+        const float mw = ms.m[w][h];
+        if (mw != -CUDART_INF_F) acc = fmaf(exp2f((mw - mx) * sc), ms.o[w][h][d], acc);
+      }
+    }
+    part[h * part_row + d] = acc;
+    if (d == 0) {
+      float ls = 0.f;
+      if (mx != -CUDART_INF_F) {
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; w++) {
+          const float mw = ms.m[w][h];
+          if (mw != -CUDART_INF_F) ls = fmaf(exp2f((mw - mx) * sc), ms.l[w][h], ls);
+        }
+      }
+      part[h * part_row + kD] = mx == -CUDART_INF_F ? -CUDART_INF_F : mx * sc;
+      part[h * part_row + kD + 1] = ls;
+    }
+  }
+}
+
+bool attn_mma_supported(const AttnParams& p) {
+  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.tokens == 1 && p.head_dim == kD && p.group <= 8 &&
+         (p.cache_dtype == DT_F16 || p.cache_dtype == DT_BF16);
+}
+
+int64_t attn_mma_items(const AttnParams& p, const int32_t* host_len) {
+  int64_t items = 0;
+  for (int b = 0; b < p.batch; b++) {
+    const int nk = host_len[p.seq_begin + b] + p.horizon_extra;
+    const int cnt = nk > 0 ? (nk + p.chunk - 1) / p.chunk : 1;
+    items += static_cast<int64_t>(cnt) * p.num_layers * p.kv_heads;
+  }
+  return items;
+}
+
+cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st) {
+  if (!attn_mma_supported(p) || p.chunk % kTile != 0) return cudaErrorInvalidValue;
+  if (items == 0) return cudaSuccess;
+  if (items > 0x7fffffff) return cudaErrorInvalidValue;
+  const CUtensorMap* mk = static_cast<const CUtensorMap*>(p.tmap_k);
+  const CUtensorMap* mv = static_cast<const CUtensorMap*>(p.tmap_v);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_f16[64] = {}, attr_bf16[64] = {};
+  if (p.cache_dtype == DT_F16) {
+    if (dev < 64 && !attr_f16[dev]) {
+      cudaFuncSetAttribute(k_decode_mma<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+      attr_f16[dev] = true;
+    }
+    k_decode_mma<__half><<<static_cast<unsigned>(items), kThreads, kSmemTotal, st>>>(*mk, *mv, p);
+  } else {
+    if (dev < 64 && !attr_bf16[dev]) {
+      cudaFuncSetAttribute(k_decode_mma<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+      attr_bf16[dev] = true;
+    }
+    k_decode_mma<__nv_bfloat16><<<static_cast<unsigned>(items), kThreads, kSmemTotal, st>>>(*mk, *mv, p);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace b2a
