@@ -163,6 +163,27 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope
                                 const void* q, const void* k_new, const void* v_new,
                                 b2a_dtype in_dtype, void* out, b2a_dtype out_dtype, int flags);
 
+/* ---- decode that allocates nothing ------------------------------------------
+ * No counterpart in the reference: its engine owns its WebGPU buffers itself.
+ * Same work, arguments and results as b2a_attention_decode, for callers that
+ * cannot allocate device memory: a server that has already handed the GPU's
+ * memory to its own pools, or a caller running several streams that must not
+ * be stalled by the device-wide synchronization cudaMalloc/cudaFree can cause.
+ * All pointers are device pointers (nothing is staged); the call only enqueues
+ * work on the context's stream and never calls cudaMalloc or cudaFree.
+ * The split-KV partials go to one fixed device array of
+ * B2A_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
+ * the process exits. A call whose partials would not fit returns B2A_ERANGE.
+ * All calls on a device share that array: calls that overlap on the GPU race
+ * and corrupt each other, so order them (e.g. one stream). The first call on
+ * each device looks up the array's device address; make it before any stream
+ * capture. */
+#define B2A_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+b2a_status b2a_attention_decode_noalloc(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
+                                        int layer_begin, int num_layers, int num_heads,
+                                        const void* q, const void* k_new, const void* v_new,
+                                        b2a_dtype in_dtype, void* out, b2a_dtype out_dtype);
+
 /* ---- causal prefill of one sequence ----------------------------------------
  * groupedAttention with seq=count, past=L (attention.js:32-66) for sequence
  * seq_idx, with RoPE on q and k at absolute positions L..L+count-1 and the K/V
