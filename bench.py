@@ -77,6 +77,12 @@ def ncu_traffic(kernel: str, workload: str):
     return None
 
 
+def workload_name() -> str:
+    if (SEQS, LAYERS) == (64, 24):
+        return "config3-batched-decode"
+    return f"config3-batched-decode-reduced(seqs={SEQS},layers={LAYERS})"
+
+
 def config3_lengths(rank: int) -> np.ndarray:
     rng = np.random.default_rng(1234 + rank)
     return rng.integers(LMIN, LMAX + 1, size=SEQS).astype(np.int32)
@@ -309,7 +315,7 @@ def run_ours(args) -> None:
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "config3-batched-decode", "sequences_per_gpu": SEQS, "layers": LAYERS,
+        "config": {"workload": workload_name(), "sequences_per_gpu": SEQS, "layers": LAYERS,
                    "heads": "14q/2kv", "head_dim": D, "kv_len": f"U{{{LMIN}..{LMAX}}} seeded per rank",
                    "cache_dtype": "f16", "q_dtype": "f16", "out_dtype": "f32", "rope_theta": THETA,
                    "bytes_per_step_per_gpu": nb["step"], "parallelism": f"dp{world} (sequences)",
@@ -434,7 +440,7 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "config3-batched-decode", "sequences_per_gpu": SEQS, "layers": LAYERS,
+        "config": {"workload": workload_name(), "sequences_per_gpu": SEQS, "layers": LAYERS,
                    "heads": "14q/2kv", "head_dim": D, "kv_len": f"U{{{LMIN}..{LMAX}}} seeded per rank",
                    "cache_dtype": "f16"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": used, "kind": "port",
@@ -456,9 +462,14 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192])
+    ap.add_argument("--seqs", type=int, default=SEQS,
+                    help="sequences per GPU (profiling of a smaller case; the headline is 64)")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (the headline is 24)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    global SEQS, LAYERS
+    SEQS, LAYERS = args.seqs, args.layers
     if args.impl == "reference":
         run_reference(args)
     else:
