@@ -453,6 +453,7 @@ def run_reference(args) -> None:
 
 
 def main() -> None:
+    global SEQS, LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
@@ -468,7 +469,6 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    global SEQS, LAYERS
     SEQS, LAYERS = args.seqs, args.layers
     if args.impl == "reference":
         run_reference(args)
