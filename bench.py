@@ -310,7 +310,7 @@ def run_ours(args) -> None:
 
     pk = peaks()
     achieved = nb["attention_kernel"] / (attn_ms / 1e3) / 1e9
-    traffic = ncu_traffic(attn_name, "config3")
+    traffic = ncu_traffic(attn_name, workload_name())
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,

@@ -899,7 +899,20 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* r
   if (e != cudaSuccess) return cuda_fail(e, "launching the rope append");
   p.k_new = nullptr;
   p.v_new = nullptr;
-  if ((s = run_split_kv(ctx, c, p, past + count, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
+  if (c->has_tmaps) {
+    p.tmap_k = &c->tmap_k;
+    p.tmap_v = &c->tmap_v;
+  }
+  if (prefill_tc_supported(p)) {
+    // tensor-core causal attention: one CTA per (128-query tile, head), no split
+    {
+      KernelTimer kt(ctx, K_PREFILL_TC);
+      e = launch_prefill_tc(p, dout, static_cast<int>(out_dtype), ctx->stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "launching the tensor-core prefill");
+  } else if ((s = run_split_kv(ctx, c, p, past + count, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) {
+    return s;
+  }
   if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
   return B2A_OK;
 }

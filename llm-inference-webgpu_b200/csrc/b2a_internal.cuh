@@ -146,6 +146,8 @@ bool attn_mma_supported(const AttnParams& p);
 int64_t attn_mma_items(const AttnParams& p, const int32_t* host_len);
 cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
+bool prefill_tc_supported(const AttnParams& p);
+cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cudaStream_t st);
 cudaError_t launch_grouped_generic(const float* q, const float* k, const float* v, float* out, int seq,
                                    int past, int heads, int kv_heads, int head_dim, cudaStream_t st);
 

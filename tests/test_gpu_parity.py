@@ -239,6 +239,40 @@ def test_config2_prefill_bf16(ctx, rope, oracle, S):
     assert np.array_equal(gk, oracle.to_bits(kr.reshape(S, KVH, D).transpose(1, 0, 2), "bf16"))
 
 
+@pytest.mark.parametrize("cache_dtype,splits", [
+    ("f16", [8]), ("f16", [130]), ("f16", [512]), ("f16", [2048]), ("f16", [300, 200, 1]),
+    ("bf16", [8]), ("bf16", [130]), ("bf16", [1000]), ("bf16", [129, 257]),
+])
+def test_prefill_tensor_core(ctx, rope, oracle, cache_dtype, splits):
+    """Causal prefill through the tcgen05 kernel: bf16 Q/K/V,
+    K/V cached as f16 (bf16 values are exact in f16) or bf16; several calls in a
+    row continue one sequence (chunked prefill, past > 0)."""
+    n = sum(splits)
+    q = oracle.round_to(oracle.normal_array(n * H * D, 71), "bf16").reshape(n, H * D)
+    k = oracle.round_to(oracle.normal_array(n * KVH * D, 72), "bf16").reshape(n, KVH * D)
+    v = oracle.round_to(oracle.normal_array(n * KVH * D, 73), "bf16").reshape(n, KVH * D)
+    c = b2a.GpuKVCache(ctx, cfg(1), n, dtype=cache_dtype)
+    outs = []
+    t0 = 0
+    for s in splits:
+        c.allocate(s)
+        o = np.empty(s * H * D, np.uint16)
+        b2a.attentionPrefill(ctx, c, rope, 0, oracle.to_bits(q[t0:t0 + s], "bf16"),
+                             oracle.to_bits(k[t0:t0 + s], "bf16"), oracle.to_bits(v[t0:t0 + s], "bf16"), o, s, H,
+                             dtype="bf16")
+        outs.append(oracle.from_bits(o, "bf16"))
+        c.commit(s)
+        t0 += s
+    got = np.concatenate(outs)
+    qr = oracle.rope_rows(q, range(n), D, THETA).reshape(-1)
+    kr = oracle.round_to(oracle.rope_rows(k, range(n), D, THETA), cache_dtype).reshape(-1)
+    ref = oracle.grouped_attention(qr, kr, oracle.round_to(v, cache_dtype), n, 0, H, KVH, D)
+    assert_parity(got, ref, "bf16", f"{cache_dtype} prefill {splits}")
+    gk, gv = c.read(0, n)
+    assert np.array_equal(gk, oracle.to_bits(kr.reshape(n, KVH, D).transpose(1, 0, 2), cache_dtype))
+    assert np.array_equal(gv, oracle.to_bits(v.reshape(n, KVH, D).transpose(1, 0, 2), cache_dtype))
+
+
 @pytest.mark.parametrize("splits", [[40], [1] * 12 + [28], [17, 1, 22]])
 def test_incremental_equals_full_recompute(ctx, rope, oracle, splits):
     """validate/phase2.js:83-121 on synthetic projections: prefill in one call,
