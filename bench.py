@@ -356,7 +356,7 @@ def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)   # > L2, rewritten between steps
     for S in args.prefill_seqs:
         with torch.cuda.stream(stream):
-            cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(1, KVH, D, H), S, batch=1, dtype="bf16")
+            cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(1, KVH, D, H), S, batch=1, dtype=args.prefill_cache)
             rope = b2a.RopeTable(ctx, D, THETA, S)
             q = torch.randn(S, H, D, device=dev).bfloat16()
             k = torch.randn(S, KVH, D, device=dev).bfloat16()
@@ -390,6 +390,7 @@ def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
     main = res["sweep"].get("512") or next(iter(res["sweep"].values()))
     res["value"] = main["tflops"]
     res["config"] = {"workload": "config2-causal-prefill", "seq": 512, "heads": "14q/2kv", "head_dim": D,
+                     "qkv_dtype": "bf16", "out_dtype": "bf16", "cache_dtype": args.prefill_cache,
                      "flops": "4*D*H*S(S+1)/2", "l2": "flushed (256 MiB write) between timed steps"}
     best_s = max(res["sweep"], key=lambda s: res["sweep"][s]["kernel_tflops"] or 0)
     bk = res["sweep"][best_s]
@@ -462,7 +463,10 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192])
+    ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192, 16384])
+    ap.add_argument("--prefill-cache", choices=["f16", "bf16"], default="f16",
+                    help="KV cache dtype for the prefill sweep: bf16 inputs are exact in f16, and the f16 "
+                         "tensor-core path needs no split products")
     ap.add_argument("--seqs", type=int, default=SEQS,
                     help="sequences per GPU (profiling of a smaller case; the headline is 64)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (the headline is 24)")

@@ -163,6 +163,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       B2A_IREG8(0), B2A_IREG8(8), B2A_IREG8(16), B2A_IREG8(24)
       : "memory");
 }
+// 2^x on the multi-function unit (flushes subnormal results to zero, which for
+// softmax weights below 2^-126 is harmless).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -330,17 +338,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t qrow = (static_cast<int64_t>(t) * p.heads + h) * kD;
       unsigned char* rh = smem + kOffQHi + r * 128;
       unsigned char* rl = smem + kOffQLo + r * 128;
+      const bool vec = p.in_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
 #pragma unroll
       for (int c = 0; c < 4; c++) {         // chunk c holds dims 8c..8c+7; chunk c+4 dims 32+8c..
         float lo[8], hi[8];
+        float x0[8], x1[8];
+        double cs[8], sn[8];
+        if (t < p.tokens) {
+          if (vec) {   // one 16-byte load per 8 elements
+            const uint4 u0 = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + qrow + 8 * c);
+            const uint4 u1 = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + qrow + 8 * c + 32);
+            const uint16_t* h0 = reinterpret_cast<const uint16_t*>(&u0);
+            const uint16_t* h1 = reinterpret_cast<const uint16_t*>(&u1);
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              x0[e] = p.in_dtype == DT_F16 ? __half2float(__ushort_as_half(h0[e]))
+                                           : __bfloat162float(__ushort_as_bfloat16(h0[e]));
+              x1[e] = p.in_dtype == DT_F16 ? __half2float(__ushort_as_half(h1[e]))
+                                           : __bfloat162float(__ushort_as_bfloat16(h1[e]));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              x0[e] = ld_as_f32(p.q, qrow + 8 * c + e, p.in_dtype);
+              x1[e] = ld_as_f32(p.q, qrow + 8 * c + e + 32, p.in_dtype);
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const double2 c2 = *reinterpret_cast<const double2*>(cosr + 8 * c + e);
+            const double2 s2 = *reinterpret_cast<const double2*>(sinr + 8 * c + e);
+            cs[e] = c2.x;
+            cs[e + 1] = c2.y;
+            sn[e] = s2.x;
+            sn[e + 1] = s2.y;
+          }
+        }
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-          const int j = 8 * c + e;
           lo[e] = hi[e] = 0.f;
-          if (t < p.tokens) {
-            rope_pair_f64(ld_as_f32(p.q, qrow + j, p.in_dtype), ld_as_f32(p.q, qrow + j + 32, p.in_dtype),
-                          cosr[j], sinr[j], lo[e], hi[e]);
-          }
+          if (t < p.tokens) rope_pair_f64(x0[e], x1[e], cs[e], sn[e], lo[e], hi[e]);
         }
         uint4 vh0, vh1, vl0, vl1;
         uint32_t* ph0 = reinterpret_cast<uint32_t*>(&vh0);
@@ -382,22 +419,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       // causal / end-of-sequence mask: key k visible iff k <= a
       const int kbase = j * kBN;
       const bool need_mask = kbase + kBN - 1 > past + q0;
-      float mx = -CUDART_INF_F;
+      if (need_mask) {
+        const int lim = a - kbase;   // columns > lim are masked
 #pragma unroll
-      for (int q4 = 0; q4 < 4; q4++) {
+        for (int q4 = 0; q4 < 4; q4++)
 #pragma unroll
-        for (int e = 0; e < 32; e++) {
-          float v = __uint_as_float(sr[q4][e]);
-          if (need_mask && kbase + q4 * 32 + e > a) v = -CUDART_INF_F;
-          sr[q4][e] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
-        }
+          for (int e = 0; e < 32; e++)
+            if (q4 * 32 + e > lim) sr[q4][e] = __float_as_uint(-CUDART_INF_F);
       }
+      // row max with 8 independent chains (a single chain is latency-bound)
+      float mxs[8];
+#pragma unroll
+      for (int x = 0; x < 8; x++) mxs[x] = -CUDART_INF_F;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; q4++)
+#pragma unroll
+        for (int e = 0; e < 32; e++) mxs[e & 7] = fmaxf(mxs[e & 7], __uint_as_float(sr[q4][e]));
+      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       const float tmx = mx * sc;
       const bool grow = tmx > m_used + kRescaleThreshold;
       if (__any_sync(0xffffffffu, grow)) {
         const float m_new = fmaxf(m_used, tmx);
-        const float alpha = (m_used == -CUDART_INF_F) ? 0.f : exp2f(m_used - m_new);
+        const float alpha = (m_used == -CUDART_INF_F) ? 0.f : ex2_approx(m_used - m_new);
         l *= alpha;
         if (j > 0) {
           // O holds the sum through PV_{j-1}: rescale it in place
@@ -420,15 +464,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float nb = -m_used;
       // P = 2^(s*sc - m), written over this S buffer's columns
-      float rowsum = 0.f;
+      float sums[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t ph[2][32];   // 64 columns of packed pairs; lo parts reuse sr storage
 #pragma unroll
       for (int q4 = 0; q4 < 4; q4++) {
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = exp2f(fmaf(__uint_as_float(sr[q4][e]), sc, nb));
-          const float p1 = exp2f(fmaf(__uint_as_float(sr[q4][e + 1]), sc, nb));
-          rowsum += p0 + p1;
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[q4][e]), sc, nb));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[q4][e + 1]), sc, nb));
+          sums[(e >> 1) & 3] += p0 + p1;
           const int col = q4 * 16 + e / 2;   // packed column 0..63
           if (kSplit) {
             uint32_t hi, lo;
@@ -440,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      l += rowsum;
+      l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
       // the last KV tile: zero V rows past the sequence end (0 * stale bits must not give NaN)
       if (j == n_kv - 1) {
         const int valid_rows = (past + p.tokens) - kbase;
@@ -474,10 +518,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t orow = (static_cast<int64_t>(t) * p.heads + h) * kD;
       void* out = p.partial;   // the output pointer travels in the partial slot for this kernel
       const int odt = p.nchunks;   // and its dtype in nchunks
+      if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) {
 #pragma unroll
-      for (int x = 0; x < 2; x++)
+        for (int x = 0; x < 2; x++)
 #pragma unroll
-        for (int e = 0; e < 32; e++) st_from_f32(out, orow + x * 32 + e, odt, __uint_as_float(ov[x][e]) * inv);
+          for (int e = 0; e < 32; e++) st_from_f32(out, orow + x * 32 + e, odt, __uint_as_float(ov[x][e]) * inv);
+      } else if (odt == DT_F32) {
+        float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(out) + orow);
+#pragma unroll
+        for (int x = 0; x < 16; x++) {
+          const int e = 4 * x;
+          o4[x] = make_float4(__uint_as_float(ov[e >> 5][e & 31]) * inv, __uint_as_float(ov[e >> 5][(e & 31) + 1]) * inv,
+                              __uint_as_float(ov[e >> 5][(e & 31) + 2]) * inv,
+                              __uint_as_float(ov[e >> 5][(e & 31) + 3]) * inv);
+        }
+      } else {
+        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + orow);
+#pragma unroll
+        for (int x = 0; x < 8; x++) {
+          uint32_t w[4];
+#pragma unroll
+          for (int y = 0; y < 4; y++) {
+            const int e = 8 * x + 2 * y;
+            const float f0 = __uint_as_float(ov[e >> 5][e & 31]) * inv;
+            const float f1 = __uint_as_float(ov[e >> 5][(e & 31) + 1]) * inv;
+            const uint32_t b0 = odt == DT_F16 ? f32_to_f16_bits(f0) : f32_to_bf16_bits(f0);
+            const uint32_t b1 = odt == DT_F16 ? f32_to_f16_bits(f1) : f32_to_bf16_bits(f1);
+            w[y] = b0 | (b1 << 16);
+          }
+          o4[x] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
     }
   }
   tc_fence_before();
