@@ -334,6 +334,8 @@ def run_ours(args) -> None:
     if clocks:
         line["clocks"] = clocks.summary(t_wall0, t_wall1)
 
+    if not args.no_splitkv:
+        line["split_kv"] = bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args)
     if world == 1 and not args.no_prefill:
         line["prefill"] = bench_prefill(torch, b2a, ctx, stream, dev, pk, args)
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -348,6 +350,72 @@ def run_ours(args) -> None:
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict:
+    """8 sequences with a 32768-position f16 cache and one new
+    token each, the KV positions split across the ranks; per step: this rank's
+    partial (o, m, l) kernel, an NCCL all-gather of the partials, the LSE combine."""
+    from b2a import dist as bd
+    nseq, total = 8, 32768
+    lo, hi = bd.position_slice(total, world, rank)
+    n_local = hi - lo
+    last = rank == world - 1
+    with torch.cuda.stream(stream):
+        cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(1, KVH, D, H), n_local + 1, batch=nseq, dtype="f16")
+        rope = b2a.RopeTable(ctx, D, THETA, total + 1)
+        kp, vp, _ = cache.pools()
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(777 + rank)
+        shape = (nseq, 1, KVH, n_local + 1, D)
+        torch.as_tensor(_CAI(kp, shape, "<f2"), device=dev).normal_(generator=gen)
+        torch.as_tensor(_CAI(vp, shape, "<f2"), device=dev).normal_(generator=gen)
+        cache.setLengths([n_local] * nseq)
+        g2 = torch.Generator(device=dev)
+        g2.manual_seed(4242)   # the same query and new token on every rank
+        q = torch.randn(nseq, H, D, device=dev, generator=g2).half()
+        kn = torch.randn(nseq, KVH, D, device=dev, generator=g2).half()
+        vn = torch.randn(nseq, KVH, D, device=dev, generator=g2).half()
+        pos = torch.full((nseq,), total, dtype=torch.int32, device=dev)
+        local = torch.empty(nseq, H, D + 4, device=dev)
+        out = torch.empty(nseq, H, D, device=dev)
+    if world > 1:
+        step = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world)
+    else:
+        def single_gather(x):
+            return x.view((1,) + tuple(x.shape))
+        step = bd.SplitKVDecode(rank, 1,
+                                lambda qq, k, v, ps, o: b2a.decodePartial(ctx, cache, rope, 0, qq, k, v, ps, o, H),
+                                single_gather,
+                                lambda st, o: b2a.lseCombine(ctx, st, 1, nseq, H, D, o))
+    steps = max(10, min(args.steps, 300))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step.step(q, kn, vn, pos, local, out)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step.step(q, kn, vn, pos, local, out)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kv_bytes = nseq * KVH * (total + 1) * D * 2 * 2
+    cache.close()
+    rope.close()
+    return {"metric": "split-KV decode GB/s", "value": round(kv_bytes * steps / (ms / 1e3) / 1e9, 1),
+            "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps,
+            "config": {"workload": "config5-split-kv-decode", "sequences": nseq, "kv_len": total,
+                       "cache_dtype": "f16", "layers": 1, "kv_bytes_per_step": kv_bytes,
+                       "parallelism": f"context-parallel over {world} GPU(s)",
+                       "collective": "NCCL all_gather of (o, m, l) partials, then LSE combine in rank order"
+                       if world > 1 else "none"}}
 
 
 def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
@@ -461,6 +529,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-splitkv", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192, 16384])

@@ -1,0 +1,107 @@
+"""Multi-GPU decode: one process per GPU, torch.distributed (NCCL over NVLink)
+for the plumbing.
+
+Two ways the hot path spreads over the GPUs of one box:
+
+* Batched decode (independent sequences): each rank owns whole sequences and
+  decodes them with no collective on the data path. `lpt_partition` balances a
+  fixed set of sequences over ranks by KV bytes (strong scaling); the benchmark
+  gives every rank its own set (weak scaling).
+
+* Split-KV decode (long contexts): every rank holds the same contiguous slice
+  of every sequence's positions (`position_slice`), the new token landing on the
+  last rank. `SplitKVDecode.step` computes this rank's partial (o, m, l) per
+  (sequence, query head), gathers all ranks' partials with one all-gather, and
+  merges them with the log-sum-exp combine in ascending rank order, so every
+  rank gets the same bits.
+
+The compute and the gather are pluggable so the orchestration can be tested
+with the gloo backend on CPU; by default they are the CUDA kernels of
+libb2a.so and torch.distributed's NCCL all-gather.
+"""
+from __future__ import annotations
+
+import heapq
+from typing import Callable, Sequence
+
+
+def position_slice(total: int, world: int, rank: int) -> tuple[int, int]:
+    """[lo, hi) of the positions 0..total-1 that `rank` holds: contiguous ceil-divided slices."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    per = (total + world - 1) // world
+    lo = min(total, rank * per)
+    hi = min(total, lo + per)
+    return lo, hi
+
+
+def lpt_partition(weights: Sequence[int], world: int) -> list[list[int]]:
+    """Greedy longest-processing-time assignment of items (sequence indices) to
+    `world` bins by weight (KV positions): heaviest first onto the lightest bin.
+    Deterministic: ties go to the lower rank."""
+    order = sorted(range(len(weights)), key=lambda i: (-weights[i], i))
+    heap = [(0, r) for r in range(world)]
+    bins: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        bins[r].append(i)
+        heapq.heappush(heap, (load + int(weights[i]), r))
+    return [sorted(b) for b in bins]
+
+
+class SplitKVDecode:
+    """One split-KV decode step across the ranks of a process group.
+
+    partial_fn(q, k_new, v_new, positions, out_partial) -> None
+        writes this rank's [batch, heads, head_dim + 4] partial; k_new/v_new are
+        given only on the rank that holds the new token (the last one).
+    gather_fn(local) -> stacked [world, ...] partials in rank order.
+    combine_fn(stacked, out) -> None
+        merges the world partials into out [batch, heads, head_dim].
+    """
+
+    def __init__(self, rank: int, world: int, partial_fn: Callable, gather_fn: Callable, combine_fn: Callable):
+        self.rank, self.world = rank, world
+        self.partial_fn, self.gather_fn, self.combine_fn = partial_fn, gather_fn, combine_fn
+
+    @property
+    def holds_new_token(self) -> bool:
+        return self.rank == self.world - 1
+
+    def step(self, q, k_new, v_new, positions, local_partial, out):
+        self.partial_fn(q, k_new if self.holds_new_token else None, v_new if self.holds_new_token else None,
+                        positions, local_partial)
+        stacked = self.gather_fn(local_partial)
+        self.combine_fn(stacked, out)
+        return out
+
+
+def nccl_gather_fn(group=None):
+    """All-gather of a CUDA tensor into a new [world, *shape] tensor (NCCL)."""
+    import torch
+    import torch.distributed as dist
+
+    def gather(local):
+        world = dist.get_world_size(group)
+        flat = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                           device=local.device)
+        dist.all_gather_into_tensor(flat, local.contiguous(), group=group)
+        return flat.view((world,) + tuple(local.shape))
+
+    return gather
+
+
+def cuda_split_kv(ctx, cache, rope, layer: int, num_heads: int, rank: int, world: int, group=None,
+                  dtype: str | None = None) -> SplitKVDecode:
+    """SplitKVDecode wired to libb2a's partial and combine kernels and NCCL."""
+    from . import attention as A
+
+    head_dim = cache.config.headDim
+
+    def partial_fn(q, k_new, v_new, positions, out_partial):
+        A.decodePartial(ctx, cache, rope, layer, q, k_new, v_new, positions, out_partial, num_heads, dtype=dtype)
+
+    def combine_fn(stacked, out):
+        A.lseCombine(ctx, stacked, world, stacked.shape[1], num_heads, head_dim, out)
+
+    return SplitKVDecode(rank, world, partial_fn, nccl_gather_fn(group), combine_fn)
