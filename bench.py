@@ -392,6 +392,11 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
     with torch.cuda.stream(stream):
         for _ in range(max(3, args.warmup)):
             step.step(q, kn, vn, pos, local, out)
+        ctx.enable_timing(True)
+        for _ in range(10):
+            step.step(q, kn, vn, pos, local, out)
+        kt = ctx.read_timing()
+        ctx.enable_timing(False)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
@@ -411,6 +416,7 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
     rope.close()
     return {"metric": "split-KV decode GB/s", "value": round(kv_bytes * steps / (ms / 1e3) / 1e9, 1),
             "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps,
+            "kernels": {k: {"launches": v[0], "avg_ms": round(v[1] / v[0], 4)} for k, v in kt.items()},
             "config": {"workload": "config5-split-kv-decode", "sequences": nseq, "kv_len": total,
                        "cache_dtype": "f16", "layers": 1, "kv_bytes_per_step": kv_bytes,
                        "parallelism": f"context-parallel over {world} GPU(s)",

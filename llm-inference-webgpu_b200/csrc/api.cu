@@ -249,8 +249,9 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
   int64_t items = 0;
   if (mma) {
     // The longest chunk that still gives every SM several work items (three
-    // CTAs fit per SM); chunks are whole 64-position tiles.
-    const int64_t want = 12LL * ctx->sm_count;
+    // CTAs fit per SM, so this is about three waves); chunks are whole
+    // 64-position tiles.
+    const int64_t want = 8LL * ctx->sm_count;
     for (int chunk : {4096, 2048, 1024, 512, 256}) {
       p.chunk = chunk;
       items = attn_mma_items(p, c->len.data());

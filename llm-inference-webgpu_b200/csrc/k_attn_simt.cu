@@ -233,6 +233,108 @@ __global__ void k_combine(CombineParams p, int64_t row_stride, int64_t part_stri
   }
 }
 
+// Rows with many partials (long contexts split into many chunks): one CTA per
+// row, each of its 8 warps merges every 8th partial with an online rescale,
+// then warp 0 merges the 8 results in warp order (a fixed order: the same
+// inputs always give the same bits).
+__global__ void __launch_bounds__(256) k_combine_wide(CombineParams p, int64_t row_stride, int64_t part_stride) {
+  __shared__ float sm_m[8], sm_l[8], sm_o[8][128];
+  const int64_t row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = p.head_dim;
+  int parts = p.nchunks;
+  if (p.len != nullptr) {
+    int64_t r = row / p.heads;
+    const int t = static_cast<int>(r % p.tokens);
+    r /= p.tokens;
+    const int b = static_cast<int>(r / p.num_layers);
+    const int nk = p.len[p.seq_begin + b] + t + p.extra;
+    parts = nk > 0 ? (nk + p.chunk - 1) / p.chunk : 1;
+    if (parts > p.nchunks) parts = p.nchunks;
+  }
+  const float* base = p.partial + row * row_stride;
+  // this warp's parts are i = warp + 8 k; lane k holds part k's (m, l), so one
+  // load instruction fetches up to 32 of them, and the weighted sum below
+  // issues its loads independently of each other
+  float m = -CUDART_INF_F, lsum = 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; warp + 8 * k0 < parts; k0 += 32) {
+    const int i = warp + 8 * (k0 + lane);
+    float mi = -CUDART_INF_F, li = 0.f;
+    if (i < parts) {
+      const float* pp = base + i * part_stride;
+      mi = pp[D];
+      li = pp[D + 1];
+      if (!(li > 0.f)) mi = -CUDART_INF_F;
+    }
+    float mx = mi;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float mn = fmaxf(m, mx);
+    if (mn == -CUDART_INF_F) continue;
+    const float a = (m == -CUDART_INF_F) ? 0.f : exp2f(m - mn);
+    const float wi = (mi == -CUDART_INF_F) ? 0.f : exp2f(mi - mn);
+    float lw = wi * li;
+    for (int o = 16; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+    lsum = fmaf(lsum, a, lw);
+#pragma unroll
+    for (int k = 0; k < 4; k++) acc[k] *= a;
+    const int nk = min(32, (parts - warp + 7) / 8 - k0);
+#pragma unroll 4
+    for (int kk = 0; kk < nk; kk++) {
+      const float w = __shfl_sync(0xffffffffu, wi, kk);
+      const float* pp = base + (warp + 8 * (k0 + kk)) * part_stride;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int d = lane + 32 * k;
+        if (d < D) acc[k] = fmaf(w, pp[d], acc[k]);
+      }
+    }
+    m = mn;
+  }
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_l[warp] = lsum;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int d = lane + 32 * k;
+    if (d < D) sm_o[warp][d] = acc[k];
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  float mx = -CUDART_INF_F;
+  for (int w = 0; w < 8; w++)
+    if (sm_l[w] > 0.f) mx = fmaxf(mx, sm_m[w]);
+  float L = 0.f;
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < 8; w++) {
+    if (!(sm_l[w] > 0.f)) continue;
+    const float s = exp2f(sm_m[w] - mx);
+    L = fmaf(s, sm_l[w], L);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int d = lane + 32 * k;
+      if (d < D) o[k] = fmaf(s, sm_o[w][d], o[k]);
+    }
+  }
+  if (p.mode == 1) {
+    float* out = static_cast<float*>(p.out) + row * (D + 4);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int d = lane + 32 * k;
+      if (d < D) out[d] = o[k];
+    }
+    if (lane == 0) { out[D] = mx; out[D + 1] = L; out[D + 2] = 0.f; out[D + 3] = 0.f; }
+    return;
+  }
+  const float inv = 1.f / L;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int d = lane + 32 * k;
+    if (d < D) st_from_f32(p.out, row * D + d, p.out_dtype, o[k] * inv);
+  }
+}
+
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
   if (p.head_dim > 128) return cudaErrorInvalidValue;
   if (p.rows == 0) return cudaSuccess;
@@ -240,6 +342,10 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
                                                  : (p.head_dim + 4);
   const int64_t stride_row = p.part_stride_rows ? (p.head_dim + 4)
                                                 : static_cast<int64_t>(p.nchunks) * (p.head_dim + 4);
+  if (p.nchunks >= 16) {
+    k_combine_wide<<<static_cast<unsigned>(p.rows), 256, 0, st>>>(p, stride_row, stride_part);
+    return cudaGetLastError();
+  }
   const int threads = 256;
   const int64_t blocks = (static_cast<int64_t>(p.rows) * 32 + threads - 1) / threads;
   k_combine<<<static_cast<unsigned>(blocks), threads, 0, st>>>(p, stride_row, stride_part);
