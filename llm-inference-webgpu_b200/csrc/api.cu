@@ -182,6 +182,8 @@ b2a_status check_device_error(b2a_ctx* ctx) {
   B2A_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(err), cudaMemcpyDeviceToHost), "reading the device error word");
   if (err != 0) {
     cudaMemset(ctx->d_err, 0, sizeof(err));
+    // a kernel that gave up may have left merge counters non-zero
+    if (ctx->d_counters) cudaMemset(ctx->d_counters, 0, ctx->d_counters_bytes);
     return fail(B2A_ETIMEDOUT, "a device-side wait gave up (error word 0x%x); results of that call are invalid", err);
   }
   return B2A_OK;
@@ -263,12 +265,31 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
   b2a_status s = ensure_buffer(&ctx->d_scratch, &ctx->d_scratch_bytes, need, "allocating split-KV scratch");
   if (s != B2A_OK) return s;
   p.partial = static_cast<float*>(ctx->d_scratch);
+  // the tensor-core kernel merges its own chunks when they are few: one CTA
+  // walking many chunks would be a long tail, which the parallel combine avoids
+  const bool fused = mma && p.nchunks <= std::min(16, attn_mma_max_fused_chunks());
+  if (fused) {
+    const size_t cbytes = static_cast<size_t>(p.batch) * p.num_layers * p.kv_heads * sizeof(int32_t);
+    if (cbytes > ctx->d_counters_bytes) {
+      void* buf = ctx->d_counters;
+      size_t cap = ctx->d_counters_bytes;
+      if ((s = ensure_buffer(&buf, &cap, cbytes, "allocating merge counters")) != B2A_OK) return s;
+      ctx->d_counters = static_cast<int32_t*>(buf);
+      ctx->d_counters_bytes = cap;
+      B2A_CUDA(cudaMemsetAsync(ctx->d_counters, 0, cap, ctx->stream), "clearing merge counters");
+    }
+    p.fuse_out = out;
+    p.fuse_dtype = out_dtype;
+    p.fuse_mode = mode;
+    p.counters = ctx->d_counters;
+  }
   cudaError_t e;
   {
     KernelTimer kt(ctx, mma ? K_ATTN_MMA : K_ATTN_SIMT);
     e = mma ? launch_attn_mma(p, items, ctx->stream) : launch_attn_simt(p, ctx->stream);
   }
   if (e != cudaSuccess) return cuda_fail(e, "launching the attention kernel");
+  if (fused) return B2A_OK;
   CombineParams cp{};
   cp.partial = p.partial;
   cp.rows = rows;
@@ -291,6 +312,86 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
   }
   if (e != cudaSuccess) return cuda_fail(e, "launching the split-KV combine");
   return B2A_OK;
+}
+
+// Host-pointer decode, pipelined over groups of sequences: each group's upload
+// (copy_in stream), attention kernels (the context's stream) and download
+// (copy_out stream) overlap those of its neighbours, so the PCIe transfers hide
+// behind the HBM-bound kernels. p carries the device staging pointers of the
+// whole batch; q_seq / kv_seq / out_seq are the bytes per sequence.
+b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnParams& p, const void* hq,
+                                 const void* hk, const void* hv, void* hout, void* dout, int out_dtype, size_t q_seq,
+                                 size_t kv_seq, size_t out_seq) {
+  const int batch = p.batch;
+  const size_t seq_bytes = q_seq + (hk ? 2 * kv_seq : 0) + out_seq;
+  // ~3 MiB of transfers per group and at most 3 groups: more, smaller groups
+  // lose more kernel efficiency (tails, shorter chunks) than they hide copies
+  int groups = static_cast<int>(std::min<size_t>(3, std::max<size_t>(1, batch * seq_bytes / (3u << 20))));
+  if (groups > batch) groups = batch;
+  if (ctx->copy_in == nullptr) {
+    B2A_CUDA(cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking), "creating the upload stream");
+  }
+  if (ctx->copy_out == nullptr) {
+    B2A_CUDA(cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking), "creating the download stream");
+  }
+  while (ctx->pipe_events.size() < static_cast<size_t>(2 * groups + 1)) {
+    cudaEvent_t e;
+    B2A_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "creating pipeline events");
+    ctx->pipe_events.push_back(e);
+  }
+  // uploads wait for earlier work on the context's stream (it may still read the staging buffer)
+  cudaEvent_t start = ctx->pipe_events[2 * groups];
+  B2A_CUDA(cudaEventRecord(start, ctx->stream), "ordering the upload");
+  B2A_CUDA(cudaStreamWaitEvent(ctx->copy_in, start, 0), "ordering the upload");
+  const char* src_q = static_cast<const char*>(hq);
+  char* dst_q = static_cast<char*>(const_cast<void*>(p.q));
+  for (int gi = 0; gi < groups; gi++) {
+    const int b0 = static_cast<int>(static_cast<int64_t>(batch) * gi / groups);
+    const int b1 = static_cast<int>(static_cast<int64_t>(batch) * (gi + 1) / groups);
+    const int n = b1 - b0;
+    if (n == 0) continue;
+    B2A_CUDA(cudaMemcpyAsync(dst_q + b0 * q_seq, src_q + b0 * q_seq, n * q_seq, cudaMemcpyHostToDevice,
+                             ctx->copy_in),
+             "copying q to the device");
+    if (hk) {
+      B2A_CUDA(cudaMemcpyAsync(static_cast<char*>(const_cast<void*>(p.k_new)) + b0 * kv_seq,
+                               static_cast<const char*>(hk) + b0 * kv_seq, n * kv_seq, cudaMemcpyHostToDevice,
+                               ctx->copy_in),
+               "copying new keys to the device");
+      B2A_CUDA(cudaMemcpyAsync(static_cast<char*>(const_cast<void*>(p.v_new)) + b0 * kv_seq,
+                               static_cast<const char*>(hv) + b0 * kv_seq, n * kv_seq, cudaMemcpyHostToDevice,
+                               ctx->copy_in),
+               "copying new values to the device");
+    }
+    B2A_CUDA(cudaEventRecord(ctx->pipe_events[2 * gi], ctx->copy_in), "recording an upload");
+  }
+  for (int gi = 0; gi < groups; gi++) {
+    const int b0 = static_cast<int>(static_cast<int64_t>(batch) * gi / groups);
+    const int b1 = static_cast<int>(static_cast<int64_t>(batch) * (gi + 1) / groups);
+    const int n = b1 - b0;
+    if (n == 0) continue;
+    B2A_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->pipe_events[2 * gi], 0), "waiting for an upload");
+    AttnParams pg = p;
+    pg.seq_begin = p.seq_begin + b0;
+    pg.batch = n;
+    pg.q = dst_q + b0 * q_seq;
+    if (hk) {
+      pg.k_new = static_cast<const char*>(p.k_new) + b0 * kv_seq;
+      pg.v_new = static_cast<const char*>(p.v_new) + b0 * kv_seq;
+    }
+    int max_keys = 0;
+    for (int b = pg.seq_begin; b < pg.seq_begin + n; b++) max_keys = std::max(max_keys, c->len[b] + p.horizon_extra);
+    b2a_status s = run_split_kv(ctx, c, pg, max_keys, static_cast<char*>(dout) + b0 * out_seq, out_dtype, 0);
+    if (s != B2A_OK) return s;
+    B2A_CUDA(cudaEventRecord(ctx->pipe_events[2 * gi + 1], ctx->stream), "recording a group");
+    B2A_CUDA(cudaStreamWaitEvent(ctx->copy_out, ctx->pipe_events[2 * gi + 1], 0), "ordering a download");
+    B2A_CUDA(cudaMemcpyAsync(static_cast<char*>(hout) + b0 * out_seq, static_cast<char*>(dout) + b0 * out_seq,
+                             n * out_seq, cudaMemcpyDeviceToHost, ctx->copy_out),
+             "copying results to the host");
+  }
+  B2A_CUDA(cudaStreamSynchronize(ctx->copy_out), "waiting for the results");
+  B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the kernels");
+  return check_device_error(ctx);
 }
 
 }  // namespace
@@ -362,11 +463,15 @@ b2a_status b2a_destroy(b2a_ctx* ctx) {
   if (ctx->d_scratch) cudaFree(ctx->d_scratch);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->d_positions) cudaFree(ctx->d_positions);
+  if (ctx->d_counters) cudaFree(ctx->d_counters);
   for (auto& r : ctx->timing_recs) {
     cudaEventDestroy(r.start);
     cudaEventDestroy(r.stop);
   }
   for (auto ev : ctx->event_pool) cudaEventDestroy(ev);
+  for (auto ev : ctx->pipe_events) cudaEventDestroy(ev);
+  if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
+  if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
   return B2A_OK;
@@ -824,19 +929,18 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* ro
     int iq = st.add(q_bytes), ik = st.add(k_new ? kv_bytes : 0), iv = st.add(k_new ? kv_bytes : 0),
         io = st.add(out_bytes);
     if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
-    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
     p.q = st.ptr(ctx, iq);
     if (k_new) {
-      if ((s = h2d(ctx, st.ptr(ctx, ik), k_new, kv_bytes)) != B2A_OK) return s;
-      if ((s = h2d(ctx, st.ptr(ctx, iv), v_new, kv_bytes)) != B2A_OK) return s;
       p.k_new = st.ptr(ctx, ik);
       p.v_new = st.ptr(ctx, iv);
     }
     dout = st.ptr(ctx, io);
+    return decode_host_pipelined(ctx, c, p, q, k_new, v_new, out, dout, static_cast<int>(out_dtype),
+                                 static_cast<size_t>(num_layers) * num_heads * c->head_dim * ies,
+                                 static_cast<size_t>(num_layers) * c->kv_heads * c->head_dim * ies,
+                                 static_cast<size_t>(num_layers) * num_heads * c->head_dim * dtype_size(out_dtype));
   }
-  if ((s = run_split_kv(ctx, c, p, max_keys, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) return s;
-  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
-  return B2A_OK;
+  return run_split_kv(ctx, c, p, max_keys, dout, static_cast<int>(out_dtype), 0);
 }
 
 // ----------------------------------------------------------------- prefill --

@@ -25,6 +25,8 @@ struct b2a_ctx {
   void* d_scratch = nullptr;
   size_t d_scratch_bytes = 0;
   int32_t* d_err = nullptr;             // device error word (bounded waits, bounds checks)
+  int32_t* d_counters = nullptr;        // fused split-KV merge counters, kept zeroed
+  size_t d_counters_bytes = 0;
   int32_t* d_positions = nullptr;       // staging for host q_positions
   int d_positions_cap = 0;
   // per-kernel timing (b2a_timing_enable / b2a_timing_read)
@@ -35,6 +37,10 @@ struct b2a_ctx {
   };
   std::vector<TimingRec> timing_recs;
   std::vector<cudaEvent_t> event_pool;
+  // host-pointer decode pipeline: uploads and downloads overlap the kernels
+  cudaStream_t copy_in = nullptr;
+  cudaStream_t copy_out = nullptr;
+  std::vector<cudaEvent_t> pipe_events;
 };
 
 namespace b2a {
@@ -119,6 +125,16 @@ struct AttnParams {
   int32_t* err;
   const void* tmap_k;         // host CUtensorMap* of the pools (tensor-core path), or null
   const void* tmap_v;
+  // Fused split-KV merge (tensor-core path): when fuse_out is set, a group
+  // whose keys fit one chunk writes its result straight to fuse_out, and the
+  // last CTA of every other group merges that group's chunk partials, so no
+  // separate combine launch is needed. fuse_mode 0: normalised output
+  // [rows][D] in fuse_dtype; 1: merged partial [rows][D+4] f32. counters: one
+  // zeroed int per (sequence, layer, KV head) of the call, left zeroed.
+  void* fuse_out;
+  int fuse_dtype;
+  int fuse_mode;
+  int32_t* counters;
 };
 
 struct CombineParams {
@@ -144,6 +160,7 @@ cudaError_t launch_lengths_update(int32_t* d_len, int idx, int batch, int count,
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t st);
 bool attn_mma_supported(const AttnParams& p);
 int64_t attn_mma_items(const AttnParams& p, const int32_t* host_len);
+int attn_mma_max_fused_chunks();
 cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
 bool prefill_tc_supported(const AttnParams& p);

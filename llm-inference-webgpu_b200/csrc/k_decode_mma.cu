@@ -43,6 +43,7 @@ constexpr int kSmemRing = kStages * kStageBytes;   // 64 KiB
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at 1.9 GHz, then give up
 constexpr int kErrTimeout = 1;
+constexpr int kMaxFusedChunks = 256;                // weights of the fused merge: 8 heads x 256 floats
 
 struct __align__(16) MergeSmem {
   float o[kConsumerWarps][8][kD];
@@ -442,35 +443,118 @@ __global__ void __launch_bounds__(kThreads, 3)
 
   const int64_t row0 = (static_cast<int64_t>(b) * p.num_layers + l) * p.heads + g * G;
   const int64_t part_row = static_cast<int64_t>(p.nchunks) * (kD + 4);
-  float* part = p.partial + (row0 * p.nchunks + c) * (kD + 4);
+  float* part_base = p.partial + row0 * part_row;            // chunk 0 of head 0 of this group
+  float* part = part_base + c * (kD + 4);
+  // A group whose keys fit in one chunk writes its final result directly.
+  const bool direct = p.fuse_out != nullptr && cnt == 1;
   for (int idx = tid; idx < G * kD; idx += kConsumerWarps * 32) {
     const int h = idx / kD, d = idx % kD;
     float mx = -CUDART_INF_F;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; w++) mx = fmaxf(mx, ms.m[w][h]);
-    float acc = 0.f;
+    float acc = 0.f, ls = 0.f;
     if (mx != -CUDART_INF_F) {
 #pragma unroll
       for (int w = 0; w < kConsumerWarps; w++) {
         const float mw = ms.m[w][h];
-        if (mw != -CUDART_INF_F) acc = fmaf(exp2f((mw - mx) * sc), ms.o[w][h][d], acc);
-      }
-    }
-    part[h * part_row + d] = acc;
-    if (d == 0) {
-      float ls = 0.f;
-      if (mx != -CUDART_INF_F) {
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; w++) {
-          const float mw = ms.m[w][h];
-          if (mw != -CUDART_INF_F) ls = fmaf(exp2f((mw - mx) * sc), ms.l[w][h], ls);
+        if (mw != -CUDART_INF_F) {
+          const float sw = exp2f((mw - mx) * sc);
+          acc = fmaf(sw, ms.o[w][h][d], acc);
+          ls = fmaf(sw, ms.l[w][h], ls);
         }
       }
-      part[h * part_row + kD] = mx == -CUDART_INF_F ? -CUDART_INF_F : mx * sc;
-      part[h * part_row + kD + 1] = ls;
+    }
+    const float m2 = mx == -CUDART_INF_F ? -CUDART_INF_F : mx * sc;
+    if (direct) {
+      if (p.fuse_mode == 0) {
+        st_from_f32(p.fuse_out, (row0 + h) * kD + d, p.fuse_dtype, acc / ls);
+      } else {
+        float* o = static_cast<float*>(p.fuse_out) + (row0 + h) * (kD + 4);
+        o[d] = acc;
+        if (d == 0) {
+          o[kD] = m2;
+          o[kD + 1] = ls;
+          o[kD + 2] = 0.f;
+          o[kD + 3] = 0.f;
+        }
+      }
+    } else {
+      part[h * part_row + d] = acc;
+      if (d == 0) {
+        part[h * part_row + kD] = m2;
+        part[h * part_row + kD + 1] = ls;
+      }
+    }
+  }
+  if (p.fuse_out == nullptr || direct) return;
+
+  // ---- fused merge: the last CTA of this (sequence, layer, KV head) to finish
+  // merges the group's `cnt` chunk partials (threadfence-and-count pattern).
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  if (tid == 0) {
+    int32_t* ctr = p.counters + (static_cast<int64_t>(b) * p.num_layers + l) * p.kv_heads + g;
+    const int prev = atomicAdd(ctr, 1);
+    const bool last = prev == cnt - 1;
+    if (last) *ctr = 0;   // ready for the next launch
+    ms.item[3] = last ? 1 : 0;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  if (ms.item[3] == 0) return;
+  __threadfence();
+  // per head: chunk weights 2^(m_c - m*) into shared memory (the warp-merge
+  // area is free now), with one warp per head and one lane per chunk
+  float* wts = &ms.o[0][0][0];   // [8 heads][kMaxFusedChunks]
+  float* hinv = &ms.l[0][0];     // per head: 1/L (or L), and m* in ms.m
+  for (int h = warp; h < G; h += kConsumerWarps) {
+    const float* ph = part_base + h * part_row;
+    float mx = -CUDART_INF_F;
+    for (int cc = lane; cc < cnt; cc += 32) {
+      const float li = __ldcg(ph + cc * (kD + 4) + kD + 1);
+      if (li > 0.f) mx = fmaxf(mx, __ldcg(ph + cc * (kD + 4) + kD));
+    }
+    for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+    float L = 0.f;
+    for (int cc = lane; cc < cnt; cc += 32) {
+      const float li = __ldcg(ph + cc * (kD + 4) + kD + 1);
+      const float w = li > 0.f ? exp2f(__ldcg(ph + cc * (kD + 4) + kD) - mx) : 0.f;
+      wts[h * kMaxFusedChunks + cc] = w;
+      L = fmaf(w, li, L);
+    }
+    for (int x = 16; x > 0; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+    if (lane == 0) {
+      hinv[h] = p.fuse_mode == 0 ? 1.f / L : L;
+      ms.m[0][h] = mx;
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  for (int idx = tid; idx < G * kD; idx += kConsumerWarps * 32) {
+    const int h = idx / kD, d = idx % kD;
+    const float* ph = part_base + h * part_row + d;
+    float acc0 = 0.f, acc1 = 0.f;
+    int cc = 0;
+    for (; cc + 1 < cnt; cc += 2) {
+      acc0 = fmaf(wts[h * kMaxFusedChunks + cc], __ldcg(ph + cc * (kD + 4)), acc0);
+      acc1 = fmaf(wts[h * kMaxFusedChunks + cc + 1], __ldcg(ph + (cc + 1) * (kD + 4)), acc1);
+    }
+    if (cc < cnt) acc0 = fmaf(wts[h * kMaxFusedChunks + cc], __ldcg(ph + cc * (kD + 4)), acc0);
+    const float acc = acc0 + acc1;
+    if (p.fuse_mode == 0) {
+      st_from_f32(p.fuse_out, (row0 + h) * kD + d, p.fuse_dtype, acc * hinv[h]);
+    } else {
+      float* o = static_cast<float*>(p.fuse_out) + (row0 + h) * (kD + 4);
+      o[d] = acc;
+      if (d == 0) {
+        o[kD] = ms.m[0][h];
+        o[kD + 1] = hinv[h];
+        o[kD + 2] = 0.f;
+        o[kD + 3] = 0.f;
+      }
     }
   }
 }
+
+int attn_mma_max_fused_chunks() { return kMaxFusedChunks; }
 
 bool attn_mma_supported(const AttnParams& p) {
   return p.tmap_k != nullptr && p.tmap_v != nullptr && p.tokens == 1 && p.head_dim == kD && p.group <= 8 &&

@@ -339,3 +339,37 @@ def test_split_kv_partials_combine_to_full_decode(ctx, rope, oracle):
                                    np.ascontiguousarray(vfull[b].transpose(1, 0, 2)), L, dtype)
         assert_parity(out[b].reshape(-1), ref, "f32", f"split seq {b}")
 
+
+
+def test_host_pipelined_decode_matches_device_path(ctx, rope, oracle):
+    """The host-pointer decode splits the batch into groups whose uploads,
+    kernels and downloads overlap; its output equals the device-pointer call's."""
+    import torch
+    batch, layers, cap = 32, 24, 700
+    c = b2a.GpuKVCache(ctx, cfg(layers), cap, batch=batch, dtype="f16")
+    dev = torch.device("cuda", 0)
+    kp, vp, _ = c.pools()
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+
+    class _CAI:
+        def __init__(self, ptr, shape):
+            self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f2", "data": (ptr, False), "version": 3}
+
+    torch.as_tensor(_CAI(kp, (batch, layers, KVH, cap, D)), device=dev).normal_(generator=g)
+    torch.as_tensor(_CAI(vp, (batch, layers, KVH, cap, D)), device=dev).normal_(generator=g)
+    torch.cuda.synchronize(dev)
+    rng = np.random.default_rng(2)
+    c.setLengths(rng.integers(1, cap - 1, size=batch).astype(np.int32))
+    q = torch.randn(batch, layers, H, D, device=dev, generator=g).half()
+    kn = torch.randn(batch, layers, KVH, D, device=dev, generator=g).half()
+    vn = torch.randn(batch, layers, KVH, D, device=dev, generator=g).half()
+    out_dev = torch.empty(batch, layers, H, D, device=dev)
+    b2a.attentionDecode(ctx, c, rope, 0, q, kn, vn, out_dev, H, numLayers=layers)
+    ctx.synchronize()
+    qh, knh, vnh = q.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    out_host = torch.empty(batch, layers, H, D).pin_memory()
+    for _ in range(2):
+        b2a.attentionDecode(ctx, c, rope, 0, qh, knh, vnh, out_host, H, numLayers=layers)
+        diff = (out_host - out_dev.cpu()).abs().max().item()
+        assert diff < 1e-4, diff
