@@ -230,6 +230,8 @@ AttnParams base_params(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope) {
   p.head_dim = c->head_dim;
   p.rope_cos = rope->d_cos;
   p.rope_sin = rope->d_sin;
+  p.rope_cos32 = rope->d_cos32;
+  p.rope_sin32 = rope->d_sin32;
   p.rope_max = rope->max_positions;
   p.err = ctx->d_err;
   return p;
@@ -576,38 +578,49 @@ b2a_status b2a_rope_create(b2a_ctx* ctx, int head_dim, double theta, int max_pos
   double inv[512];
   b2a_rope_frequencies(head_dim, theta, inv);
   const size_t n = static_cast<size_t>(max_positions) * half;
-  double* hc = nullptr;
-  double* hs = nullptr;
-  B2A_CUDA(cudaMallocHost(&hc, n * sizeof(double)), "allocating the host rope table");
-  cudaError_t e = cudaMallocHost(&hs, n * sizeof(double));
-  if (e != cudaSuccess) {
-    cudaFreeHost(hc);
-    return cuda_fail(e, "allocating the host rope table");
-  }
+  // one pinned block: cos f64, sin f64, cos f32, sin f32
+  void* host = nullptr;
+  B2A_CUDA(cudaMallocHost(&host, n * 2 * (sizeof(double) + sizeof(float))), "allocating the host rope table");
+  double* hc = static_cast<double*>(host);
+  double* hs = hc + n;
+  float* hc32 = reinterpret_cast<float*>(hs + n);
+  float* hs32 = hc32 + n;
   // The angle ropeInPlace evaluates (src/core/ops.js:150-152), in f64.
   for (int p = 0; p < max_positions; p++) {
     for (int j = 0; j < half; j++) {
+      const size_t i = static_cast<size_t>(p) * half + j;
       const double angle = static_cast<double>(p) * inv[j];
-      hc[static_cast<size_t>(p) * half + j] = std::cos(angle);
-      hs[static_cast<size_t>(p) * half + j] = std::sin(angle);
+      hc[i] = std::cos(angle);
+      hs[i] = std::sin(angle);
+      hc32[i] = static_cast<float>(hc[i]);
+      hs32[i] = static_cast<float>(hs[i]);
     }
   }
   b2a_rope* r = new (std::nothrow) b2a_rope();
+  if (r == nullptr) {
+    cudaFreeHost(host);
+    return fail(B2A_ECUDA, "out of host memory for the rope table");
+  }
   r->ctx = ctx;
   r->device = ctx->device;
   r->head_dim = head_dim;
   r->theta = theta;
   r->max_positions = max_positions;
-  e = cudaMalloc(&r->d_cos, n * sizeof(double));
+  cudaError_t e = cudaMalloc(&r->d_cos, n * sizeof(double));
   if (e == cudaSuccess) e = cudaMalloc(&r->d_sin, n * sizeof(double));
+  if (e == cudaSuccess) e = cudaMalloc(&r->d_cos32, n * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&r->d_sin32, n * sizeof(float));
   if (e == cudaSuccess) e = cudaMemcpyAsync(r->d_cos, hc, n * sizeof(double), cudaMemcpyHostToDevice, ctx->stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(r->d_sin, hs, n * sizeof(double), cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(r->d_cos32, hc32, n * sizeof(float), cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(r->d_sin32, hs32, n * sizeof(float), cudaMemcpyHostToDevice, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-  cudaFreeHost(hc);
-  cudaFreeHost(hs);
+  cudaFreeHost(host);
   if (e != cudaSuccess) {
-    if (r->d_cos) cudaFree(r->d_cos);
-    if (r->d_sin) cudaFree(r->d_sin);
+    cudaFree(r->d_cos);
+    cudaFree(r->d_sin);
+    cudaFree(r->d_cos32);
+    cudaFree(r->d_sin32);
     delete r;
     return cuda_fail(e, "uploading the rope table");
   }
@@ -622,6 +635,8 @@ b2a_status b2a_rope_destroy(b2a_rope* rope) {
   cudaSetDevice(rope->device);
   cudaFree(rope->d_cos);
   cudaFree(rope->d_sin);
+  cudaFree(rope->d_cos32);
+  cudaFree(rope->d_sin32);
   delete rope;
   return B2A_OK;
 }

@@ -72,6 +72,8 @@ struct b2a_rope {
   int max_positions = 0;
   double* d_cos = nullptr;  // [max_positions][head_dim/2]
   double* d_sin = nullptr;
+  float* d_cos32 = nullptr; // the same tables rounded to f32 (query rotation
+  float* d_sin32 = nullptr; // ahead of a 16-bit tensor-core operand)
 };
 
 struct b2a_kvcache {
@@ -118,6 +120,8 @@ struct AttnParams {
   int horizon_extra;          // decode/prefill: 1 (slot L+t inclusive); partial: (k_new?1:0)
   const double* rope_cos;
   const double* rope_sin;
+  const float* rope_cos32;    // f32 copies, for queries rounded to 16 bits afterwards
+  const float* rope_sin32;
   int rope_max;
   float* partial;             // [rows][nchunks][D+4]
   int chunk;                  // positions per chunk (multiple of 64)

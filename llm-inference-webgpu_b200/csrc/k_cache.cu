@@ -9,6 +9,9 @@ namespace b2a {
 // kv.writeAt), src/gpu/model.js:327-338 (ROPE on k, two copies). One thread
 // per rotation pair (t, kv head, j); the same thread stores both halves of V.
 __global__ void k_rope_append(AttnParams p, int seq_idx, int count) {
+  // a kernel launched after this one as a programmatic dependent may start its
+  // prologue now; it waits for this grid before reading the cache
+  asm volatile("griddepcontrol.launch_dependents;");
   const int half = p.head_dim >> 1;
   const int64_t n = static_cast<int64_t>(count) * p.kv_heads * half;
   const int past = p.len[seq_idx];

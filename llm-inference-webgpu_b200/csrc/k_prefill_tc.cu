@@ -17,7 +17,11 @@
 //               2^8), so O in TMEM is rescaled rarely. P is written back into
 //               the S buffer's columns (it aliases the consumed S).
 // RoPE(q) is applied while the softmax warps stage the Q tile into swizzled
-// shared memory (f64 rotation from the host table, as every kernel here does).
+// shared memory (f32 rotation: the operand is rounded to 16 bits next).
+// The kernel is launched as a programmatic dependent of the RoPE(K) + append
+// kernel before it: everything up to the first K/V load (barriers, TMEM, the
+// Q tile) overlaps that kernel, and the producer waits on the grid dependency
+// before its first TMA load of the cache.
 // With a bf16 cache the rotated query and P are each split into a bf16 high
 // part and a bf16 residual (two MMAs each): a single bf16 rounding of either
 // puts the output about 5e-3 off the f32 reference, the split keeps it ~1e-6.
@@ -28,11 +32,14 @@
 #include <type_traits>
 
 #include "b2a_internal.cuh"
+#include "k_sm100.cuh"
 #include "k_util.cuh"
 
 namespace b2a {
 
 namespace {
+
+using namespace sm100;
 
 constexpr int kD = 64;
 constexpr int kBM = 128;                       // query rows per CTA
@@ -46,8 +53,6 @@ constexpr int kTmemCols = 512;                 // S0 [0,128) S1 [128,256) O [256
 constexpr int kOCol = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
-constexpr long long kWaitCycles = 1000000000LL;
-constexpr int kErrTimeout = 2;
 
 // smem layout (offsets from a 1024-aligned base)
 constexpr int kOffQHi = 0;
@@ -56,123 +61,6 @@ constexpr int kOffRing = kOffQLo + kQBytes;
 constexpr int kOffBars = kOffRing + kStages * kStageBytes;
 constexpr int kNumBars = 2 * kStages + 2 /*s_full*/ + 2 /*p_full*/ + 1 /*o_done*/ + 1 /*q_ready*/;
 constexpr int kSmemTotal = kOffBars + kNumBars * 8 + 16 + 1024;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
-                   smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait (~0.5 s): on timeout, record it in the error word, mark this
-// thread dead and carry on; a dead thread skips every later wait, so a broken
-// pipeline ends the CTA quickly instead of hanging.
-__device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err, bool& dead) {
-  if (dead || mbar_try_wait(bar, parity)) return;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
-      if (err) atomicOr(err, kErrTimeout);
-      dead = true;
-      return;
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// ---- tcgen05 wrappers -------------------------------------------------------
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: 128-byte swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
-  return static_cast<uint64_t>((saddr & 0x3FFFF) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-
-// kind::f16 instruction descriptor: f32 accumulate, A/B type (0 f16, 1 bf16),
-// B major-ness (0 K-major, 1 MN-major), shape M x N.
-__host__ __device__ constexpr uint32_t idesc_f16(int ab_type, int b_mn_major, int M, int N) {
-  return (1u << 4) | (static_cast<uint32_t>(ab_type) << 7) | (static_cast<uint32_t>(ab_type) << 10) |
-         (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
-         (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-#define B2A_REG8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
-                    "=r"(r[i + 6]), "=r"(r[i + 7])
-#define B2A_IREG8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), \
-                     "r"(r[i + 6]), "r"(r[i + 7])
-
-// 32 consecutive TMEM columns of this thread's lane -> r[0..31]
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : B2A_REG8(0), B2A_REG8(8), B2A_REG8(16), B2A_REG8(24)
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      B2A_IREG8(0), B2A_IREG8(8), B2A_IREG8(16), B2A_IREG8(24)
-      : "memory");
-}
-// 2^x on the multi-function unit (flushes subnormal results to zero, which for
-// softmax weights below 2^-126 is harmless).
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);
@@ -262,6 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      // the cache rows come from the preceding append kernel
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int j = 0; j < n_kv; j++) {
         const int s = j % kStages;
         if (j >= kStages) mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, dead);
@@ -331,53 +221,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = q0 + r;                          // token index within this call
     const int a = past + t;                        // absolute position
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    // stage RoPE(q) into Q_hi (and Q_lo), 128-byte-swizzled K-major rows
+    // stage RoPE(q) into Q_hi (and Q_lo), 128-byte-swizzled K-major rows.
+    // Every global load of the row (q, cos, sin) is issued before the first
+    // use so the thread pays one memory latency, not one per chunk. The
+    // rotation runs in f32 from the f32 table: its error (~2^-24) is far below
+    // the 16-bit rounding of the MMA operand that follows.
     {
-      const double* cosr = p.rope_cos + static_cast<int64_t>(a) * (kD / 2);
-      const double* sinr = p.rope_sin + static_cast<int64_t>(a) * (kD / 2);
-      const int64_t qrow = (static_cast<int64_t>(t) * p.heads + h) * kD;
+      float x[kD], cs[kD / 2], sn[kD / 2];
+      if (t < p.tokens) {
+        const int64_t qrow = (static_cast<int64_t>(t) * p.heads + h) * kD;
+        const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos32 + static_cast<int64_t>(a) * (kD / 2));
+        const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin32 + static_cast<int64_t>(a) * (kD / 2));
+        if (p.in_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0) {
+          uint4 u[8];   // one 16-byte load per 8 elements
+          const uint4* q4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + qrow);
+#pragma unroll
+          for (int i = 0; i < 8; i++) u[i] = q4[i];
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            reinterpret_cast<float4*>(cs)[i] = c4[i];
+            reinterpret_cast<float4*>(sn)[i] = s4[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const uint16_t* hw = reinterpret_cast<const uint16_t*>(&u[i]);
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+              x[8 * i + e] = p.in_dtype == DT_F16 ? __half2float(__ushort_as_half(hw[e]))
+                                                  : __bfloat162float(__ushort_as_bfloat16(hw[e]));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < kD; e++) x[e] = ld_as_f32(p.q, qrow + e, p.in_dtype);
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            reinterpret_cast<float4*>(cs)[i] = c4[i];
+            reinterpret_cast<float4*>(sn)[i] = s4[i];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < kD; e++) x[e] = 0.f;
+#pragma unroll
+        for (int e = 0; e < kD / 2; e++) cs[e] = sn[e] = 0.f;
+      }
       unsigned char* rh = smem + kOffQHi + r * 128;
       unsigned char* rl = smem + kOffQLo + r * 128;
-      const bool vec = p.in_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
 #pragma unroll
       for (int c = 0; c < 4; c++) {         // chunk c holds dims 8c..8c+7; chunk c+4 dims 32+8c..
         float lo[8], hi[8];
-        float x0[8], x1[8];
-        double cs[8], sn[8];
-        if (t < p.tokens) {
-          if (vec) {   // one 16-byte load per 8 elements
-            const uint4 u0 = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + qrow + 8 * c);
-            const uint4 u1 = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + qrow + 8 * c + 32);
-            const uint16_t* h0 = reinterpret_cast<const uint16_t*>(&u0);
-            const uint16_t* h1 = reinterpret_cast<const uint16_t*>(&u1);
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-              x0[e] = p.in_dtype == DT_F16 ? __half2float(__ushort_as_half(h0[e]))
-                                           : __bfloat162float(__ushort_as_bfloat16(h0[e]));
-              x1[e] = p.in_dtype == DT_F16 ? __half2float(__ushort_as_half(h1[e]))
-                                           : __bfloat162float(__ushort_as_bfloat16(h1[e]));
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-              x0[e] = ld_as_f32(p.q, qrow + 8 * c + e, p.in_dtype);
-              x1[e] = ld_as_f32(p.q, qrow + 8 * c + e + 32, p.in_dtype);
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const double2 c2 = *reinterpret_cast<const double2*>(cosr + 8 * c + e);
-            const double2 s2 = *reinterpret_cast<const double2*>(sinr + 8 * c + e);
-            cs[e] = c2.x;
-            cs[e + 1] = c2.y;
-            sn[e] = s2.x;
-            sn[e + 1] = s2.y;
-          }
-        }
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-          lo[e] = hi[e] = 0.f;
-          if (t < p.tokens) rope_pair_f64(x0[e], x1[e], cs[e], sn[e], lo[e], hi[e]);
+          const int d = 8 * c + e;
+          lo[e] = fmaf(x[d], cs[d], -(x[d + 32] * sn[d]));
+          hi[e] = fmaf(x[d + 32], cs[d], x[d] * sn[d]);
         }
         uint4 vh0, vh1, vl0, vl1;
         uint32_t* ph0 = reinterpret_cast<uint32_t*>(&vh0);
@@ -576,19 +473,27 @@ cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cud
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr_f16[64] = {}, attr_bf16[64] = {};
-  if (p.cache_dtype == DT_F16) {
-    if (dev < 64 && !attr_f16[dev]) {
-      cudaFuncSetAttribute(k_prefill_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
-      attr_f16[dev] = true;
-    }
-    k_prefill_tc<__half><<<grid, kThreads, kSmemTotal, st>>>(*mk, *mv, q);
-  } else {
-    if (dev < 64 && !attr_bf16[dev]) {
-      cudaFuncSetAttribute(k_prefill_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
-      attr_bf16[dev] = true;
-    }
-    k_prefill_tc<__nv_bfloat16><<<grid, kThreads, kSmemTotal, st>>>(*mk, *mv, q);
+  const bool f16 = p.cache_dtype == DT_F16;
+  void (*kern)(const CUtensorMap, const CUtensorMap, AttnParams) =
+      f16 ? k_prefill_tc<__half> : k_prefill_tc<__nv_bfloat16>;
+  bool* attr = f16 ? attr_f16 : attr_bf16;
+  if (dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+    attr[dev] = true;
   }
+  // programmatic dependent launch: may start while the append kernel runs
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemTotal;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *mk, *mv, q);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

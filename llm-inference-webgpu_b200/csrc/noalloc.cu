@@ -122,6 +122,8 @@ extern "C" b2a_status b2a_attention_decode_noalloc(b2a_ctx* ctx, b2a_kvcache* c,
   p.horizon_extra = 1;
   p.rope_cos = rope->d_cos;
   p.rope_sin = rope->d_sin;
+  p.rope_cos32 = rope->d_cos32;
+  p.rope_sin32 = rope->d_sin32;
   p.rope_max = rope->max_positions;
   p.err = ctx->d_err;
   if (c->has_tmaps) {
