@@ -382,12 +382,13 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
     if world > 1:
         step = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world)
     else:
-        def single_gather(x):
-            return x.view((1,) + tuple(x.shape))
-        step = bd.SplitKVDecode(rank, 1,
-                                lambda qq, k, v, ps, o: b2a.decodePartial(ctx, cache, rope, 0, qq, k, v, ps, o, H),
-                                single_gather,
-                                lambda st, o: b2a.lseCombine(ctx, st, 1, nseq, H, D, o))
+        # one GPU holds the whole context: the plain decode call, whose kernel
+        # splits the positions over the CTAs and merges the chunks itself
+        class _Single:
+            @staticmethod
+            def step(qq, k, v, ps, loc, o):
+                b2a.attentionDecode(ctx, cache, rope, 0, qq, k, v, o, H)
+        step = _Single()
     steps = max(10, min(args.steps, 300))
     with torch.cuda.stream(stream):
         for _ in range(max(3, args.warmup)):
@@ -421,7 +422,7 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
                        "cache_dtype": "f16", "layers": 1, "kv_bytes_per_step": kv_bytes,
                        "parallelism": f"context-parallel over {world} GPU(s)",
                        "collective": "NCCL all_gather of (o, m, l) partials, then LSE combine in rank order"
-                       if world > 1 else "none"}}
+                       if world > 1 else "none (b2a_attention_decode: chunks merged inside the kernel)"}}
 
 
 def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
@@ -463,7 +464,7 @@ def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
         torch.cuda.synchronize(dev)
         kt = ctx.read_timing()
         ctx.enable_timing(False)
-        attn = "prefill_tc" if "prefill_tc" in kt else ("attention_simt" if "attention_simt" in kt else None)
+        attn = next((k for k in ("prefill_pair", "prefill_tc", "attention_simt") if k in kt), None)
         kms = kt[attn][1] / kt[attn][0] if attn else None
         res["sweep"][str(S)] = {"ms": round(total / steps, 4), "tflops": round(flops / (total / steps / 1e3) / 1e12, 3),
                                 "kernel": attn, "kernel_ms": round(kms, 4) if kms else None,

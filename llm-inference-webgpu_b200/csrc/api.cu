@@ -1,8 +1,11 @@
 // The C ABI of libb2a.so (include/b2a.h): argument validation with the
 // reference's error messages, host<->device staging, planning and launches.
+#include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -27,7 +30,8 @@ b2a_status cuda_fail(cudaError_t e, const char* what) {
 }
 
 const char* const kKernelNames[K_NUM_KINDS] = {"attention_simt", "attention_mma", "combine", "rope_append",
-                                               "write_at", "grouped_generic", "prefill_tc"};
+                                               "write_at", "grouped_generic", "prefill_tc",
+                                               "prefill_pair"};
 
 namespace {
 cudaEvent_t take_event(b2a_ctx* ctx) {
@@ -249,17 +253,44 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
     p.tmap_v = &c->tmap_v;
   }
   const bool mma = attn_mma_supported(p);
+  // small batches carry their lengths by value: the kernel's work-item lookup
+  // then starts without a dependent global load (host and device lengths
+  // agree in stream order)
+  p.n_len_inline = 0;
+  if (p.batch <= kLenInline) {
+    for (int b = 0; b < p.batch; b++) p.len_inline[b] = c->len[p.seq_begin + b];
+    p.n_len_inline = p.batch;
+  }
   p.chunk = 256;
   int64_t items = 0;
   if (mma) {
-    // The longest chunk that still gives every SM several work items (three
-    // CTAs fit per SM, so this is about three waves); chunks are whole
-    // 64-position tiles.
-    const int64_t want = 8LL * ctx->sm_count;
-    for (int chunk : {4096, 2048, 1024, 512, 256}) {
-      p.chunk = chunk;
+    // Chunks are whole 64-position tiles. When every (sequence, layer, KV
+    // head) group has about the same number of keys and there are fewer
+    // groups than resident CTAs (three per SM), split each group into equal
+    // chunks that fill the resident CTAs once: one wave of equal items.
+    // Otherwise take the longest chunk that still gives every SM several
+    // items (about three waves), so the hardware scheduler balances uneven
+    // lengths.
+    const int64_t slots = 3LL * ctx->sm_count;
+    const int64_t groups = static_cast<int64_t>(p.batch) * p.num_layers * p.kv_heads;
+    int min_nk = INT32_MAX, max_nk = 0;
+    for (int b = 0; b < p.batch; b++) {
+      const int nk = c->len[p.seq_begin + b] + p.horizon_extra;
+      min_nk = std::min(min_nk, nk);
+      max_nk = std::max(max_nk, nk);
+    }
+    const int64_t per_group = groups > 0 ? slots / groups : 0;
+    if (per_group >= 2 && max_nk > 0 && static_cast<int64_t>(min_nk) * 8 >= static_cast<int64_t>(max_nk) * 7) {
+      const int64_t tiles = (max_nk + 63) / 64;
+      p.chunk = static_cast<int>(64 * ((tiles + per_group - 1) / per_group));
       items = attn_mma_items(p, c->len.data());
-      if (items >= want) break;
+    } else {
+      const int64_t want = 8LL * ctx->sm_count;
+      for (int chunk : {4096, 2048, 1024, 512, 256}) {
+        p.chunk = chunk;
+        items = attn_mma_items(p, c->len.data());
+        if (items >= want) break;
+      }
     }
   }
   p.nchunks = max_keys > 0 ? (max_keys + p.chunk - 1) / p.chunk : 1;
@@ -269,7 +300,7 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
   p.partial = static_cast<float*>(ctx->d_scratch);
   // the tensor-core kernel merges its own chunks when they are few: one CTA
   // walking many chunks would be a long tail, which the parallel combine avoids
-  const bool fused = mma && p.nchunks <= std::min(16, attn_mma_max_fused_chunks());
+  const bool fused = mma && p.nchunks <= attn_mma_max_fused_chunks();
   if (fused) {
     const size_t cbytes = static_cast<size_t>(p.batch) * p.num_layers * p.kv_heads * sizeof(int32_t);
     if (cbytes > ctx->d_counters_bytes) {
@@ -960,6 +991,16 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* ro
 
 // ----------------------------------------------------------------- prefill --
 
+namespace {
+// B2A_PREFILL_TILES=1 selects the one-tile-per-CTA prefill kernel for f16
+// caches (the two-tile kernel is the default); read on every call so a
+// process can compare both.
+int prefill_tiles_per_cta() {
+  const char* v = std::getenv("B2A_PREFILL_TILES");
+  return (v != nullptr && v[0] == '1' && v[1] == 0) ? 1 : 2;
+}
+}  // namespace
+
 b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx,
                                  int num_heads, const void* q, const void* k, const void* v, b2a_dtype in_dtype,
                                  int count, void* out, b2a_dtype out_dtype, int flags) {
@@ -1023,7 +1064,14 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* r
     p.tmap_k = &c->tmap_k;
     p.tmap_v = &c->tmap_v;
   }
-  if (prefill_tc_supported(p)) {
+  if (prefill_pair_supported(p) && prefill_tiles_per_cta() != 1) {
+    // tensor-core causal attention, two heads' 128-query tiles per CTA (f16 cache)
+    {
+      KernelTimer kt(ctx, K_PREFILL_PAIR);
+      e = launch_prefill_pair(p, dout, static_cast<int>(out_dtype), ctx->stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "launching the tensor-core prefill");
+  } else if (prefill_tc_supported(p)) {
     // tensor-core causal attention: one CTA per (128-query tile, head), no split
     {
       KernelTimer kt(ctx, K_PREFILL_TC);

@@ -46,7 +46,7 @@ struct b2a_ctx {
 namespace b2a {
 // Kernel kinds reported by b2a_timing_read.
 enum KernelKind { K_ATTN_SIMT = 0, K_ATTN_MMA, K_COMBINE, K_ROPE_APPEND, K_WRITE_AT, K_GROUPED, K_PREFILL_TC,
-                  K_NUM_KINDS };
+                  K_PREFILL_PAIR, K_NUM_KINDS };
 extern const char* const kKernelNames[K_NUM_KINDS];
 
 // Brackets one launch with events on the context's stream while timing is on.
@@ -102,6 +102,8 @@ inline size_t dtype_size(b2a_dtype d) { return d == B2A_F32 ? 4 : 2; }
 
 // ---- kernel parameter blocks -------------------------------------------------
 // Attention over a head-major cache: rows of queries (b, layer, t, head).
+constexpr int kLenInline = 64;
+
 struct AttnParams {
   const void* kc;
   const void* vc;
@@ -111,6 +113,10 @@ struct AttnParams {
   int cache_dtype;
   const int32_t* len;         // [cache batch] past length per sequence (device)
   int seq_begin;              // first cache sequence of this call
+  // the same lengths for this call's sequences, by value, when there are at
+  // most kLenInline of them (n_len_inline = batch; 0: read len)
+  int n_len_inline;
+  int32_t len_inline[64];
   int batch, num_layers, layer_begin, tokens, heads, kv_heads, group, head_dim;
   const void* q;              // [batch][num_layers][tokens][heads][D]
   const void* k_new;          // [batch][num_layers][tokens][kv_heads][D] or null
@@ -155,6 +161,11 @@ struct CombineParams {
   int seq_begin, chunk, extra, tokens, heads, num_layers;
 };
 
+// Past length of the call's sequence b (by value when the host passed it).
+__host__ __device__ inline int len_of(const AttnParams& p, int b) {
+  return b < p.n_len_inline ? p.len_inline[b] : p.len[p.seq_begin + b];
+}
+
 cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st);
 cudaError_t launch_write_at(const b2a_kvcache* c, int layer, int seq_idx, int at, const void* k,
                             const void* v, int src_dtype, int count, cudaStream_t st);
@@ -169,6 +180,8 @@ cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st)
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
 bool prefill_tc_supported(const AttnParams& p);
 cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cudaStream_t st);
+bool prefill_pair_supported(const AttnParams& p);
+cudaError_t launch_prefill_pair(const AttnParams& p, void* out, int out_dtype, cudaStream_t st);
 cudaError_t launch_grouped_generic(const float* q, const float* k, const float* v, float* out, int seq,
                                    int past, int heads, int kv_heads, int head_dim, cudaStream_t st);
 

@@ -18,8 +18,9 @@
 // residual (two MMAs each), which keeps ~16 mantissa bits on both products.
 // At the end the four warps' (m, l, O) merge in shared memory into one
 // unnormalised partial per query head; k_combine (k_attn_simt.cu) merges the
-// chunks. RoPE(q) and the fused append of the new token's K/V happen in the
-// prologue, in f64 from the host-built table, exactly as the CUDA-core path.
+// chunks. RoPE(q) happens in the prologue in f32 (its operand is rounded to
+// 16 bits next); the fused append of the new token's K/V rotates in f64 from
+// the host-built table, as every cache write does.
 #include <cuda.h>
 #include <math_constants.h>
 
@@ -43,7 +44,7 @@ constexpr int kSmemRing = kStages * kStageBytes;   // 64 KiB
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at 1.9 GHz, then give up
 constexpr int kErrTimeout = 1;
-constexpr int kMaxFusedChunks = 256;                // weights of the fused merge: 8 heads x 256 floats
+constexpr int kMaxFusedChunks = 64;                 // chunks the fused merge takes (two per lane)
 
 struct __align__(16) MergeSmem {
   float o[kConsumerWarps][8][kD];
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 3)
       const int b = b0 + lane;
       int cnt = 0;
       if (b < p.batch) {
-        const int nk = p.len[p.seq_begin + b] + p.horizon_extra;
+        const int nk = len_of(p, b) + p.horizon_extra;
         cnt = nk > 0 ? (nk + p.chunk - 1) / p.chunk : 1;
       }
       int items = cnt * p.num_layers * p.kv_heads;
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int G = p.group;
   const int bc = p.seq_begin + b;
 
-  const int past = p.len[bc];
+  const int past = len_of(p, b);
   const int pos_q = p.q_pos ? p.q_pos[b] : past;
   const int n_keys = past + p.horizon_extra;
   const int p0 = c * p.chunk;
@@ -301,39 +302,63 @@ __global__ void __launch_bounds__(kThreads, 3)
 
   // ---------------------------------------------------------------- consumers
   const int gq = lane >> 2, tq = lane & 3;
-  // Q^T B-fragments for head gq (zero for padding heads): b0 = dims 16ks+2tq..+1,
-  // b1 = dims 16ks+8+2tq..+1. RoPE pairs (j, j+32) are both held by this thread.
-  uint32_t qb[4][2];
-  uint32_t qlo[4][2];
+  // RoPE(q) of the group's G heads, staged once in shared memory (the merge
+  // area is free until the tile loop ends): every global load is issued before
+  // the first use, the rotation runs in f32 (the operand is rounded to 16 bits
+  // next, or split into two bf16 parts that keep ~16 bits).
   {
-    float qv[4][4];
-    const bool valid = gq < G;
-    const int64_t qrow = ((static_cast<int64_t>(b) * p.num_layers + l) * p.heads + g * G + (valid ? gq : 0)) * kD;
+    float* qs = &ms.o[0][0][0];   // [G][64] rotated queries
+    const int64_t qbase = ((static_cast<int64_t>(b) * p.num_layers + l) * p.heads + g * G) * kD;
+    const float* c32 = p.rope_cos32 + static_cast<int64_t>(pos_q) * (kD / 2);
+    const float* s32 = p.rope_sin32 + static_cast<int64_t>(pos_q) * (kD / 2);
+    constexpr int kPairsPerThread = 2;   // 8 heads x 32 pairs over 128 consumer threads
+    float x0[kPairsPerThread], x1[kPairsPerThread], cv[kPairsPerThread], sv[kPairsPerThread];
 #pragma unroll
-    for (int ks = 0; ks < 2; ks++) {
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const int j = 16 * ks + (e >> 1) * 8 + 2 * tq + (e & 1);   // j < 32
-        float lo = 0.f, hi = 0.f;
-        if (valid) {
-          rope_pair_f64(ld_as_f32(p.q, qrow + j, p.in_dtype), ld_as_f32(p.q, qrow + j + 32, p.in_dtype), cosr[j],
-                        sinr[j], lo, hi);
-        }
-        qv[ks][e] = lo;
-        qv[ks + 2][e] = hi;
+    for (int r = 0; r < kPairsPerThread; r++) {
+      const int idx = tid + r * kConsumerWarps * 32;
+      const int h = idx >> 5, j = idx & 31;
+      x0[r] = x1[r] = cv[r] = sv[r] = 0.f;
+      if (h < G) {
+        x0[r] = ld_as_f32(p.q, qbase + h * kD + j, p.in_dtype);
+        x1[r] = ld_as_f32(p.q, qbase + h * kD + j + 32, p.in_dtype);
+        cv[r] = c32[j];
+        sv[r] = s32[j];
       }
     }
 #pragma unroll
-    for (int ks = 0; ks < 4; ks++) {
-      qb[ks][0] = pack2<T>(qv[ks][0], qv[ks][1]);
-      qb[ks][1] = pack2<T>(qv[ks][2], qv[ks][3]);
-      if (kSplit) {
-        const float2 h0 = unpack2<T>(qb[ks][0]), h1 = unpack2<T>(qb[ks][1]);
-        qlo[ks][0] = pack2<T>(qv[ks][0] - h0.x, qv[ks][1] - h0.y);
-        qlo[ks][1] = pack2<T>(qv[ks][2] - h1.x, qv[ks][3] - h1.y);
+    for (int r = 0; r < kPairsPerThread; r++) {
+      const int idx = tid + r * kConsumerWarps * 32;
+      const int h = idx >> 5, j = idx & 31;
+      if (h < G) {
+        qs[h * kD + j] = fmaf(x0[r], cv[r], -(x1[r] * sv[r]));
+        qs[h * kD + j + 32] = fmaf(x1[r], cv[r], x0[r] * sv[r]);
       }
     }
   }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  // Q^T B-fragments for head gq (zero for padding heads): b0 = dims 16ks+2tq..+1,
+  // b1 = dims 16ks+8+2tq..+1; ks 0-1 are dims 0..31, ks 2-3 dims 32..63.
+  uint32_t qb[4][2];
+  uint32_t qlo[4][2];
+  {
+    const float* qh = &ms.o[0][0][0] + gq * kD;
+    const bool valid = gq < G;
+#pragma unroll
+    for (int ks = 0; ks < 4; ks++) {
+      float qv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) qv[e] = valid ? qh[16 * ks + (e >> 1) * 8 + 2 * tq + (e & 1)] : 0.f;
+      qb[ks][0] = pack2<T>(qv[0], qv[1]);
+      qb[ks][1] = pack2<T>(qv[2], qv[3]);
+      if (kSplit) {
+        const float2 h0 = unpack2<T>(qb[ks][0]), h1 = unpack2<T>(qb[ks][1]);
+        qlo[ks][0] = pack2<T>(qv[0] - h0.x, qv[1] - h0.y);
+        qlo[ks][1] = pack2<T>(qv[2] - h1.x, qv[3] - h1.y);
+      }
+    }
+  }
+  // every consumer has its fragments before any warp reuses the merge area
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
 
   const float sc = rsqrtf(static_cast<float>(kD)) * kLog2e;   // score -> base-2 exponent
   float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F;                // raw-score max, heads 2tq, 2tq+1
@@ -502,24 +527,32 @@ __global__ void __launch_bounds__(kThreads, 3)
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
   if (ms.item[3] == 0) return;
   __threadfence();
-  // per head: chunk weights 2^(m_c - m*) into shared memory (the warp-merge
-  // area is free now), with one warp per head and one lane per chunk
+  // per head (one warp each, a lane per chunk and chunk + 32): the chunk
+  // weights 2^(m_c - m*) into shared memory (the warp-merge area is free now)
   float* wts = &ms.o[0][0][0];   // [8 heads][kMaxFusedChunks]
   float* hinv = &ms.l[0][0];     // per head: 1/L (or L), and m* in ms.m
   for (int h = warp; h < G; h += kConsumerWarps) {
     const float* ph = part_base + h * part_row;
+    float mi[2], li[2];
     float mx = -CUDART_INF_F;
-    for (int cc = lane; cc < cnt; cc += 32) {
-      const float li = __ldcg(ph + cc * (kD + 4) + kD + 1);
-      if (li > 0.f) mx = fmaxf(mx, __ldcg(ph + cc * (kD + 4) + kD));
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int cc = lane + 32 * u;
+      mi[u] = -CUDART_INF_F;
+      li[u] = 0.f;
+      if (cc < cnt) {
+        mi[u] = __ldcg(ph + cc * (kD + 4) + kD);
+        li[u] = __ldcg(ph + cc * (kD + 4) + kD + 1);
+      }
+      if (li[u] > 0.f) mx = fmaxf(mx, mi[u]);
     }
     for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
     float L = 0.f;
-    for (int cc = lane; cc < cnt; cc += 32) {
-      const float li = __ldcg(ph + cc * (kD + 4) + kD + 1);
-      const float w = li > 0.f ? exp2f(__ldcg(ph + cc * (kD + 4) + kD) - mx) : 0.f;
-      wts[h * kMaxFusedChunks + cc] = w;
-      L = fmaf(w, li, L);
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const float w = li[u] > 0.f ? exp2f(mi[u] - mx) : 0.f;
+      wts[h * kMaxFusedChunks + lane + 32 * u] = w;
+      L = fmaf(w, li[u], L);
     }
     for (int x = 16; x > 0; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
     if (lane == 0) {
@@ -528,23 +561,37 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  for (int idx = tid; idx < G * kD; idx += kConsumerWarps * 32) {
-    const int h = idx / kD, d = idx % kD;
-    const float* ph = part_base + h * part_row + d;
-    float acc0 = 0.f, acc1 = 0.f;
-    int cc = 0;
-    for (; cc + 1 < cnt; cc += 2) {
-      acc0 = fmaf(wts[h * kMaxFusedChunks + cc], __ldcg(ph + cc * (kD + 4)), acc0);
-      acc1 = fmaf(wts[h * kMaxFusedChunks + cc + 1], __ldcg(ph + (cc + 1) * (kD + 4)), acc1);
+  // weighted sum of the chunks' O rows: a thread per (head, 4 dims), 32
+  // chunk loads in flight at a time (16-byte loads, rows are 272 bytes)
+  for (int t = tid; t < G * (kD / 4); t += kConsumerWarps * 32) {
+    const int h = t / (kD / 4), d4 = t % (kD / 4);
+    const float4* src = reinterpret_cast<const float4*>(part_base + h * part_row) + d4;
+    constexpr int kRowVec = (kD + 4) / 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < cnt; c0 += 32) {
+      float4 v[32];
+#pragma unroll
+      for (int u = 0; u < 32; u++)
+        v[u] = c0 + u < cnt ? __ldcg(src + (c0 + u) * kRowVec) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 32; u++) {
+        const float w = wts[h * kMaxFusedChunks + c0 + u];   // 0 past cnt
+        acc.x = fmaf(w, v[u].x, acc.x);
+        acc.y = fmaf(w, v[u].y, acc.y);
+        acc.z = fmaf(w, v[u].z, acc.z);
+        acc.w = fmaf(w, v[u].w, acc.w);
+      }
     }
-    if (cc < cnt) acc0 = fmaf(wts[h * kMaxFusedChunks + cc], __ldcg(ph + cc * (kD + 4)), acc0);
-    const float acc = acc0 + acc1;
+    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
     if (p.fuse_mode == 0) {
-      st_from_f32(p.fuse_out, (row0 + h) * kD + d, p.fuse_dtype, acc * hinv[h]);
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+        st_from_f32(p.fuse_out, (row0 + h) * kD + 4 * d4 + e, p.fuse_dtype, a4[e] * hinv[h]);
     } else {
       float* o = static_cast<float*>(p.fuse_out) + (row0 + h) * (kD + 4);
-      o[d] = acc;
-      if (d == 0) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) o[4 * d4 + e] = a4[e];
+      if (d4 == 0) {
         o[kD] = ms.m[0][h];
         o[kD + 1] = hinv[h];
         o[kD + 2] = 0.f;

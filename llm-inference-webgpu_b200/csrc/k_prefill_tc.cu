@@ -324,16 +324,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; e++)
             if (q4 * 32 + e > lim) sr[q4][e] = __float_as_uint(-CUDART_INF_F);
       }
-      // row max with 8 independent chains (a single chain is latency-bound)
+      // row max: eight independent chains of three-input max
       float mxs[8];
 #pragma unroll
       for (int x = 0; x < 8; x++) mxs[x] = -CUDART_INF_F;
 #pragma unroll
       for (int q4 = 0; q4 < 4; q4++)
 #pragma unroll
-        for (int e = 0; e < 32; e++) mxs[e & 7] = fmaxf(mxs[e & 7], __uint_as_float(sr[q4][e]));
-      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        for (int e = 0; e < 32; e += 2)
+          mxs[(e >> 1) & 7] = max3f(mxs[(e >> 1) & 7], __uint_as_float(sr[q4][e]), __uint_as_float(sr[q4][e + 1]));
+      const float mx = max3f(max3f(mxs[0], mxs[1], mxs[2]), max3f(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
       const float tmx = mx * sc;
       const bool grow = tmx > m_used + kRescaleThreshold;
       if (__any_sync(0xffffffffu, grow)) {
@@ -361,15 +361,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float nb = -m_used;
       // P = 2^(s*sc - m), written over this S buffer's columns
-      float sums[4] = {0.f, 0.f, 0.f, 0.f};
+      // (the scale-and-shift and the row sums run as packed f32 pairs)
+      const uint64_t sc2 = f2_pack(sc, sc), nb2 = f2_pack(nb, nb);
+      uint64_t sums[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t ph[2][32];   // 64 columns of packed pairs; lo parts reuse sr storage
 #pragma unroll
       for (int q4 = 0; q4 < 4; q4++) {
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[q4][e]), sc, nb));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[q4][e + 1]), sc, nb));
-          sums[(e >> 1) & 3] += p0 + p1;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[q4][e]), __uint_as_float(sr[q4][e + 1])), sc2, nb2), x0, x1);
+          const float p0 = ex2_approx(x0);
+          const float p1 = ex2_approx(x1);
+          sums[(e >> 1) & 3] = f2_add(sums[(e >> 1) & 3], f2_pack(p0, p1));
           const int col = q4 * 16 + e / 2;   // packed column 0..63
           if (kSplit) {
             uint32_t hi, lo;
@@ -381,7 +385,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
+      {
+        float a0, a1;
+        f2_unpack(f2_add(f2_add(sums[0], sums[1]), f2_add(sums[2], sums[3])), a0, a1);
+        l += a0 + a1;
+      }
       // the last KV tile: zero V rows past the sequence end (0 * stale bits must not give NaN)
       if (j == n_kv - 1) {
         const int valid_rows = (past + p.tokens) - kbase;

@@ -216,6 +216,24 @@ def test_batched_decode_multilayer(ctx, rope, oracle, dtype):
             assert np.array_equal(gv[:, lengths[b]], oracle.to_bits(vr, dtype))
 
 
+@pytest.mark.parametrize("batch,length", [(8, 4000), (8, 9000), (2, 20000)])
+def test_uniform_long_decode_equal_chunks(ctx, rope, oracle, batch, length):
+    """BASELINE config 5 shapes, scaled down: sequences of equal length are cut
+    into equal chunks that fill the resident CTAs once; up to 32 chunks per
+    group are merged inside the attention kernel, more by the combine kernel."""
+    c = b2a.GpuKVCache(ctx, cfg(1), length + 1, batch=batch, dtype="f16")
+    hk, hv = _fill_cache(ctx, c, oracle, [length] * batch, 1, "f16", 500)
+    q = oracle.round_to(oracle.normal_array(batch * H * D, 8), "f16").reshape(batch, 1, H, D)
+    kn = oracle.round_to(oracle.normal_array(batch * KVH * D, 9), "f16").reshape(batch, 1, KVH, D)
+    vn = oracle.round_to(oracle.normal_array(batch * KVH * D, 10), "f16").reshape(batch, 1, KVH, D)
+    out = np.empty((batch, 1, H, D), np.float32)
+    b2a.attentionDecode(ctx, c, rope, 0, oracle.to_bits(q, "f16"), oracle.to_bits(kn, "f16"),
+                        oracle.to_bits(vn, "f16"), out, H, dtype="f16")
+    for b in range(batch):
+        ref, _, _ = _oracle_decode(oracle, q[b, 0], kn[b, 0], vn[b, 0], hk[b, 0], hv[b, 0], length, "f16")
+        assert_parity(out[b, 0].reshape(-1), ref, "f32", f"seq {b} of {batch} x {length}")
+
+
 # ---------------------------------------------------------- config 2 prefill --
 
 @pytest.mark.parametrize("S", [8, 64, 512])
@@ -239,14 +257,21 @@ def test_config2_prefill_bf16(ctx, rope, oracle, S):
     assert np.array_equal(gk, oracle.to_bits(kr.reshape(S, KVH, D).transpose(1, 0, 2), "bf16"))
 
 
-@pytest.mark.parametrize("cache_dtype,splits", [
-    ("f16", [8]), ("f16", [130]), ("f16", [512]), ("f16", [2048]), ("f16", [300, 200, 1]),
-    ("bf16", [8]), ("bf16", [130]), ("bf16", [1000]), ("bf16", [129, 257]),
+@pytest.mark.parametrize("cache_dtype,splits,tiles", [
+    ("f16", [8], 2), ("f16", [130], 2), ("f16", [512], 2), ("f16", [2048], 2), ("f16", [300, 200, 1], 2),
+    ("f16", [8], 1), ("f16", [130], 1), ("f16", [512], 1), ("f16", [300, 200, 1], 1),
+    ("bf16", [8], 1), ("bf16", [130], 1), ("bf16", [1000], 1), ("bf16", [129, 257], 1),
 ])
-def test_prefill_tensor_core(ctx, rope, oracle, cache_dtype, splits):
-    """Causal prefill through the tcgen05 kernel: bf16 Q/K/V,
+def test_prefill_tensor_core(ctx, rope, oracle, monkeypatch, cache_dtype, splits, tiles):
+    """Causal prefill through the tcgen05 kernels: bf16 Q/K/V,
     K/V cached as f16 (bf16 values are exact in f16) or bf16; several calls in a
-    row continue one sequence (chunked prefill, past > 0)."""
+    row continue one sequence (chunked prefill, past > 0). tiles: query tiles per
+    CTA (the two-head kernel serves f16 caches; B2A_PREFILL_TILES=1 selects the
+    one-tile kernel)."""
+    if tiles == 1:
+        monkeypatch.setenv("B2A_PREFILL_TILES", "1")
+    else:
+        monkeypatch.delenv("B2A_PREFILL_TILES", raising=False)
     n = sum(splits)
     q = oracle.round_to(oracle.normal_array(n * H * D, 71), "bf16").reshape(n, H * D)
     k = oracle.round_to(oracle.normal_array(n * KVH * D, 72), "bf16").reshape(n, KVH * D)
@@ -271,6 +296,34 @@ def test_prefill_tensor_core(ctx, rope, oracle, cache_dtype, splits):
     gk, gv = c.read(0, n)
     assert np.array_equal(gk, oracle.to_bits(kr.reshape(n, KVH, D).transpose(1, 0, 2), cache_dtype))
     assert np.array_equal(gv, oracle.to_bits(v.reshape(n, KVH, D).transpose(1, 0, 2), cache_dtype))
+
+
+@pytest.mark.parametrize("nh,nkv,in_dt,out_dt,n", [
+    (2, 2, "bf16", "bf16", 300),   # group 1: one head per CTA
+    (4, 2, "f16", "f16", 257),     # group 2: one full pair
+    (6, 2, "f32", "f32", 200),     # group 3: a pair and a single head; f32 staging path
+    (8, 1, "bf16", "f32", 129),    # one KV head, group 8
+])
+def test_prefill_pairs_over_group_shapes(ctx, rope, oracle, monkeypatch, nh, nkv, in_dt, out_dt, n):
+    """The two-head prefill kernel pairs the query heads of each KV group (an odd
+    group leaves one head alone): other group sizes, input and output dtypes."""
+    monkeypatch.delenv("B2A_PREFILL_TILES", raising=False)
+    q = oracle.normal_array(n * nh * D, 81).reshape(n, nh * D)
+    k = oracle.normal_array(n * nkv * D, 82).reshape(n, nkv * D)
+    v = oracle.normal_array(n * nkv * D, 83).reshape(n, nkv * D)
+    if in_dt != "f32":
+        q, k, v = (oracle.round_to(x, in_dt) for x in (q, k, v))
+    c = b2a.GpuKVCache(ctx, b2a.CacheConfig(numLayers=1, numKVHeads=nkv, headDim=D, numHeads=nh), n, dtype="f16")
+    c.allocate(n)
+    wrap = (lambda x: x.astype(np.float32)) if in_dt == "f32" else (lambda x: oracle.to_bits(x, in_dt))
+    o = np.empty(n * nh * D, np.float32 if out_dt == "f32" else np.uint16)
+    b2a.attentionPrefill(ctx, c, rope, 0, wrap(q), wrap(k), wrap(v), o, n, nh, dtype=in_dt,
+                         out_dtype=out_dt)
+    got = o if out_dt == "f32" else oracle.from_bits(o, out_dt)
+    qr = oracle.rope_rows(q, range(n), D, THETA).reshape(-1)
+    kr = oracle.round_to(oracle.rope_rows(k, range(n), D, THETA), "f16").reshape(-1)
+    ref = oracle.grouped_attention(qr, kr, oracle.round_to(v, "f16"), n, 0, nh, nkv, D)
+    assert_parity(got, ref, out_dt, f"prefill pairs nh={nh} nkv={nkv} {in_dt}->{out_dt}")
 
 
 @pytest.mark.parametrize("splits", [[40], [1] * 12 + [28], [17, 1, 22]])
