@@ -379,49 +379,98 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
         pos = torch.full((nseq,), total, dtype=torch.int32, device=dev)
         local = torch.empty(nseq, H, D + 4, device=dev)
         out = torch.empty(nseq, H, D, device=dev)
-    if world > 1:
-        step = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world)
-    else:
-        # one GPU holds the whole context: the plain decode call, whose kernel
-        # splits the positions over the CTAs and merges the chunks itself
-        class _Single:
-            @staticmethod
-            def step(qq, k, v, ps, loc, o):
-                b2a.attentionDecode(ctx, cache, rope, 0, qq, k, v, o, H)
-        step = _Single()
-    steps = max(10, min(args.steps, 300))
-    with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
-            step.step(q, kn, vn, pos, local, out)
-        ctx.enable_timing(True)
-        for _ in range(10):
-            step.step(q, kn, vn, pos, local, out)
-        kt = ctx.read_timing()
-        ctx.enable_timing(False)
+    def timed(step_fn, n):
+        """Device time of n back-to-back steps (max over ranks)."""
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            step.step(q, kn, vn, pos, local, out)
-        e1.record(stream)
+        with torch.cuda.stream(stream):   # graph replays launch on the current stream
+            e0.record(stream)
+            for _ in range(n):
+                step_fn()
+            e1.record(stream)
         torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    steps = max(10, min(args.steps, 300))
+    extra = {}
+    peer, peer_error = None, None
     if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        try:
+            peer = bd.PeerSplitKV(ctx, cache, rope, 0, H, rank, world)
+        except RuntimeError as e:   # raised on every rank alike
+            peer_error = str(e)[:200]
+    if peer is not None:
+        # the in-kernel exchange (peer stores + flags over NVLink), one launch
+        # per step, replayed from a CUDA graph so the host adds nothing per step
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                peer.step(q, kn, vn, pos, out)
+            ctx.enable_timing(True)
+            for _ in range(10):
+                peer.step(q, kn, vn, pos, out)
+            kt = ctx.read_timing()
+            ctx.enable_timing(False)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            peer.step(q, kn, vn, pos, out)
+        ms = timed(graph.replay, steps)
+        # the NCCL all-gather baseline (partials kernel, all-gather, combine kernel)
+        nccl = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world)
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                nccl.step(q, kn, vn, pos, local, out)
+        ms_nccl = timed(lambda: nccl.step(q, kn, vn, pos, local, out), steps)
+        extra = {"nccl_baseline": {"ms_per_step": round(ms_nccl / steps, 4),
+                                   "path": "partials kernel + NCCL all_gather + combine kernel, eager"}}
+        del graph
+        peer.close()
+    elif world > 1:
+        # no peer mapping: the NCCL path is the measured one
+        nccl = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world)
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                nccl.step(q, kn, vn, pos, local, out)
+            ctx.enable_timing(True)
+            for _ in range(10):
+                nccl.step(q, kn, vn, pos, local, out)
+            kt = ctx.read_timing()
+            ctx.enable_timing(False)
+        ms = timed(lambda: nccl.step(q, kn, vn, pos, local, out), steps)
+        extra = {"peer_error": peer_error}
+    else:
+        # one GPU holds the whole context: the plain decode call, whose kernel
+        # splits the positions over the CTAs and merges the chunks itself
+        def one():
+            b2a.attentionDecode(ctx, cache, rope, 0, q, kn, vn, out, H)
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                one()
+            ctx.enable_timing(True)
+            for _ in range(10):
+                one()
+            kt = ctx.read_timing()
+            ctx.enable_timing(False)
+            ms = timed(one, steps)
     kv_bytes = nseq * KVH * (total + 1) * D * 2 * 2
     cache.close()
     rope.close()
     return {"metric": "split-KV decode GB/s", "value": round(kv_bytes * steps / (ms / 1e3) / 1e9, 1),
-            "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps,
+            "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps, **extra,
             "kernels": {k: {"launches": v[0], "avg_ms": round(v[1] / v[0], 4)} for k, v in kt.items()},
             "config": {"workload": "config5-split-kv-decode", "sequences": nseq, "kv_len": total,
                        "cache_dtype": "f16", "layers": 1, "kv_bytes_per_step": kv_bytes,
                        "parallelism": f"context-parallel over {world} GPU(s)",
-                       "collective": "NCCL all_gather of (o, m, l) partials, then LSE combine in rank order"
+                       "collective": ("in-kernel exchange: peer stores of (o, m, l) partials + flags over NVLink, "
+                                      "LSE combine in rank order (CUDA graph replay)" if peer is not None else
+                                      "NCCL all_gather of (o, m, l) partials, then LSE combine in rank order")
                        if world > 1 else "none (b2a_attention_decode: chunks merged inside the kernel)"}}
 
 

@@ -222,6 +222,44 @@ b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* cache, const 
 b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch,
                            int num_heads, int head_dim, void* out, b2a_dtype out_dtype, int flags);
 
+/* ---- split-KV decode with the exchange fused into the attention kernel ------
+ * No reference counterpart (the reference runs on one device). The merge is the
+ * log-sum-exp combine of b2a_lse_combine, in ascending rank order, so every rank
+ * writes the same bits.
+ *
+ * An exchange connects `world` (<= 8) processes, one GPU each, for caches of
+ * `batch` sequences with num_heads query and num_kv_heads KV heads. Every rank
+ * creates one, publishes its handle (b2a_exchange_handle, B2A_EXCHANGE_HANDLE_BYTES
+ * bytes) to the others over any host channel and opens all of them in rank order
+ * (b2a_exchange_open). Then every rank calls b2a_attention_decode_split once per
+ * step, the same number of times: inside the attention kernel the last CTA of
+ * each (sequence, KV head) stores the group's merged partial into every rank's
+ * exchange buffer (peer stores over NVLink), raises a per-group flag there, waits
+ * (at most ~1 s) for the group's partials from all ranks and writes the combined,
+ * normalised output. A wait that gives up makes that call (host pointers) or the
+ * next b2a_synchronize return B2A_ETIMEDOUT; recreate the exchange on every rank
+ * after that. The cache's (sequence, KV head) groups must not outnumber the
+ * CTAs that fit on the GPU at once (three per SM). */
+typedef struct b2a_exchange b2a_exchange;
+#define B2A_EXCHANGE_HANDLE_BYTES 64
+b2a_status b2a_exchange_create(b2a_ctx* ctx, int world, int rank, int batch, int num_heads, int num_kv_heads,
+                               b2a_exchange** out);
+b2a_status b2a_exchange_handle(const b2a_exchange* ex, void* handle);
+b2a_status b2a_exchange_open(b2a_exchange* ex, const void* handles);
+/* Wires rank `peer` of ex to another exchange object of this process on the same
+ * device, instead of an IPC handle (single-GPU tests of the timeout path). Two
+ * ranks wired this way must never run their steps at the same time: kernels that
+ * wait on each other cannot share one GPU. */
+b2a_status b2a_exchange_connect_local(b2a_exchange* ex, int peer, const b2a_exchange* other);
+b2a_status b2a_exchange_destroy(b2a_exchange* ex);
+/* One decode step: like b2a_attention_decode_partial for this rank's positions
+ * (k_new/v_new only on the rank holding the new token), then the exchange, with
+ * out [batch][num_heads][head_dim] in out_dtype. f16 or bf16 caches. */
+b2a_status b2a_attention_decode_split(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope, int layer,
+                                      int num_heads, const void* q, const void* k_new, const void* v_new,
+                                      b2a_dtype in_dtype, const int32_t* q_positions, b2a_exchange* ex,
+                                      void* out, b2a_dtype out_dtype, int flags);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,6 +7,6 @@ src/gpu/model.js) over libb2a.so. There is no CPU fallback: without the built
 library, or without a CUDA device, calls raise.
 """
 from ._lib import B2AError, BusyError, RangeError, load, lib_path  # noqa: F401
-from .attention import (appendRope, attentionDecode, attentionPrefill, decodePartial,  # noqa: F401
+from .attention import (appendRope, attentionDecode, attentionPrefill, decodePartial, decodeSplit,  # noqa: F401
                         default_context, groupedAttention, kvHeadFor, lseCombine, ropeFrequencies, ropeTables)
-from .runtime import CacheConfig, Context, GpuKVCache, RopeTable  # noqa: F401
+from .runtime import CacheConfig, Context, Exchange, GpuKVCache, RopeTable  # noqa: F401

@@ -55,7 +55,14 @@ SIGNATURES = {
     "b2a_grouped_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i]),
     "b2a_attention_decode_partial": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i]),
     "b2a_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _i, _i]),
+    "b2a_exchange_create": (_i, [_vp, _i, _i, _i, _i, _i, _pp]),
+    "b2a_exchange_handle": (_i, [_vp, _vp]),
+    "b2a_exchange_open": (_i, [_vp, _vp]),
+    "b2a_exchange_connect_local": (_i, [_vp, _i, _vp]),
+    "b2a_exchange_destroy": (_i, [_vp]),
+    "b2a_attention_decode_split": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
 }
+EXCHANGE_HANDLE_BYTES = 64
 
 _lib = None
 

@@ -123,6 +123,30 @@ def decodePartial(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, 
     del keep
 
 
+def decodeSplit(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, q_positions,
+                exchange, out, numHeads: int, dtype: str | None = None, out_dtype: str | None = None) -> None:
+    """One split-KV decode step with the cross-rank exchange inside the kernel
+    (b2a_attention_decode_split): this rank's positions, then every rank's
+    partials combined in rank order into out [batch, numHeads, headDim]."""
+    qa, ka, va = _arg(q, dtype), _arg(k_new, dtype), _arg(v_new, dtype)
+    oa = _arg(out, out_dtype, writable=True)
+    in_dt = _same_dtype(qa, ka, va)
+    where = _where(qa, ka, va, oa)
+    if where == _lib.B2A_HOST:
+        pos = np.ascontiguousarray(q_positions, dtype=np.int32)
+        pos_ptr, keep = pos.ctypes.data, pos
+    else:
+        import torch
+        pos = q_positions if isinstance(q_positions, torch.Tensor) else torch.as_tensor(
+            np.asarray(q_positions, np.int32), device=f"cuda:{ctx.device}")
+        pos = pos.to(torch.int32).contiguous()
+        pos_ptr, keep = pos.data_ptr(), pos
+    check(load().b2a_attention_decode_split(ctx.handle, cache.handle, rope.handle, layer, numHeads, qa.ptr,
+                                            ka.ptr if ka else None, va.ptr if va else None, DTYPES[in_dt], pos_ptr,
+                                            exchange.handle, oa.ptr, DTYPES[oa.dtype], where))
+    del keep
+
+
 def lseCombine(ctx: Context, partials, numParts: int, batch: int, numHeads: int, headDim: int, out,
                out_dtype: str | None = None) -> None:
     """Merge [numParts, batch, numHeads, headDim+4] partials in ascending part order."""

@@ -13,7 +13,10 @@ Two ways the hot path spreads over the GPUs of one box:
   last rank. `SplitKVDecode.step` computes this rank's partial (o, m, l) per
   (sequence, query head), gathers all ranks' partials with one all-gather, and
   merges them with the log-sum-exp combine in ascending rank order, so every
-  rank gets the same bits.
+  rank gets the same bits. `PeerSplitKV` does the same exchange inside the
+  attention kernel (peer stores and flags over NVLink, b2a_attention_decode_split):
+  one launch per step and no library collective; `SplitKVDecode` with NCCL is
+  the baseline it replaces.
 
 The compute and the gather are pluggable so the orchestration can be tested
 with the gloo backend on CPU; by default they are the CUDA kernels of
@@ -105,3 +108,76 @@ def cuda_split_kv(ctx, cache, rope, layer: int, num_heads: int, rank: int, world
         A.lseCombine(ctx, stacked, world, stacked.shape[1], num_heads, head_dim, out)
 
     return SplitKVDecode(rank, world, partial_fn, nccl_gather_fn(group), combine_fn)
+
+
+def gather_handles(handle: bytes, world: int, group=None) -> bytes:
+    """Every rank's exchange handle in rank order: one all-gather of a byte tensor
+    (a CUDA tensor under NCCL, a CPU tensor under gloo)."""
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" \
+        else torch.device("cpu")
+    local = torch.tensor(list(handle), dtype=torch.uint8, device=dev)
+    flat = torch.empty(world * len(handle), dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(flat, local, group=group)
+    return bytes(flat.cpu().tolist())
+
+
+def _all_ranks_ok(ok: bool, group=None) -> bool:
+    """True on every rank iff ok is true on every rank (an all-reduce of a flag)."""
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" \
+        else torch.device("cpu")
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return bool(t.item())
+
+
+class PeerSplitKV:
+    """Split-KV decode whose cross-rank exchange runs inside the attention kernel.
+
+    Construction is collective: every rank makes its exchange, the handles are
+    all-gathered once, and each rank maps the others' buffers. step() is one
+    launch per rank; every rank must call it the same number of times."""
+
+    def __init__(self, ctx, cache, rope, layer: int, num_heads: int, rank: int, world: int, group=None,
+                 dtype: str | None = None):
+        from .runtime import Exchange
+
+        self.ctx, self.cache, self.rope, self.layer = ctx, cache, rope, layer
+        self.num_heads, self.rank, self.world, self.dtype = num_heads, rank, world, dtype
+        self.exchange = None
+        err = None
+        try:
+            self.exchange = Exchange(ctx, world, rank, cache.batch, num_heads, cache.config.numKVHeads)
+            handle = self.exchange.handle_bytes()
+        except Exception as e:   # every rank must still reach the collectives below
+            err, handle = e, bytes(64)
+        if not _all_ranks_ok(err is None, group):
+            raise RuntimeError(f"creating the exchange failed on some rank: {err}") from err
+        handles = gather_handles(handle, world, group)
+        try:
+            self.exchange.open(handles)
+        except Exception as e:
+            err = e
+        if not _all_ranks_ok(err is None, group):
+            raise RuntimeError(f"opening the peers' exchange buffers failed on some rank: {err}") from err
+
+    @property
+    def holds_new_token(self) -> bool:
+        return self.rank == self.world - 1
+
+    def step(self, q, k_new, v_new, positions, out):
+        from . import attention as A
+
+        A.decodeSplit(self.ctx, self.cache, self.rope, self.layer, q, k_new if self.holds_new_token else None,
+                      v_new if self.holds_new_token else None, positions, self.exchange, out, self.num_heads,
+                      dtype=self.dtype)
+        return out
+
+    def close(self) -> None:
+        if self.exchange is not None:
+            self.exchange.close()

@@ -17,7 +17,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from ._lib import B2A_DEVICE, B2A_HOST, DTYPES, DTYPE_SIZE, check, load
+from ._lib import B2A_DEVICE, B2A_HOST, DTYPES, DTYPE_SIZE, EXCHANGE_HANDLE_BYTES, check, load
 
 try:  # torch is optional: only needed for device-pointer calls
     import torch
@@ -270,3 +270,45 @@ class GpuKVCache:
     def valuesUpTo(self, layer: int, n: int, seq: int = 0) -> np.ndarray:
         _, v = self.read(layer, n, seq)
         return np.ascontiguousarray(v.transpose(1, 0, 2)).reshape(-1)
+
+
+class Exchange:
+    """A split-KV exchange between `world` ranks, one GPU each (b2a_exchange_*):
+    partials travel by peer stores inside the attention kernel. Every rank makes
+    one, shares handle() with the others, and calls open() with all handles in
+    rank order."""
+
+    def __init__(self, ctx: Context, world: int, rank: int, batch: int, numHeads: int, numKVHeads: int):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        check(ctx._lib.b2a_exchange_create(ctx.handle, world, rank, batch, numHeads, numKVHeads, ctypes.byref(h)))
+        self.handle = h
+        self.world, self.rank = world, rank
+        ctx._children.add(self)
+
+    def handle_bytes(self) -> bytes:
+        buf = ctypes.create_string_buffer(EXCHANGE_HANDLE_BYTES)
+        check(self.ctx._lib.b2a_exchange_handle(self.handle, buf))
+        return buf.raw
+
+    def open(self, handles: bytes) -> None:
+        """handles: world * 64 bytes in rank order (this rank's slot is ignored)."""
+        if len(handles) != self.world * EXCHANGE_HANDLE_BYTES:
+            raise ValueError(f"expected {self.world * EXCHANGE_HANDLE_BYTES} handle bytes, got {len(handles)}")
+        buf = ctypes.create_string_buffer(bytes(handles), len(handles))
+        check(self.ctx._lib.b2a_exchange_open(self.handle, buf))
+
+    def connect_local(self, peer: int, other: "Exchange") -> None:
+        """Wire rank `peer` to another exchange of this process (single-GPU tests only)."""
+        check(self.ctx._lib.b2a_exchange_connect_local(self.handle, peer, other.handle))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.ctx._lib.b2a_exchange_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -11,6 +11,18 @@
 
 #include "b2a_internal.cuh"
 
+// A split-KV exchange (include/b2a.h): one device allocation holding the
+// partials [2 parities][world][rows][68] f32, the flags [2][world][groups] i32
+// and the step / done counters; peer[r] is rank r's allocation as mapped here.
+struct b2a_exchange {
+  int device = 0;
+  int world = 1, rank = 0, batch = 0, heads = 0, kv_heads = 0, rows = 0, groups = 0;
+  void* base = nullptr;
+  size_t bytes = 0, f_off = 0, c_off = 0;
+  void* peer[b2a::kMaxWorld] = {};
+  bool opened[b2a::kMaxWorld] = {};   // peer[r] came from cudaIpcOpenMemHandle
+};
+
 namespace {
 thread_local char g_err[1024] = "";
 }
@@ -280,7 +292,19 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
       max_nk = std::max(max_nk, nk);
     }
     const int64_t per_group = groups > 0 ? slots / groups : 0;
-    if (per_group >= 2 && max_nk > 0 && static_cast<int64_t>(min_nk) * 8 >= static_cast<int64_t>(max_nk) * 7) {
+    if (mode == 2) {
+      // the exchange waits inside the kernel: every CTA must be resident at
+      // once, so one wave with at most kMaxFusedChunks chunks per group
+      if (per_group < 1) {
+        return fail(B2A_EINVAL, "%lld (sequence, KV head) groups exceed the %lld CTAs resident at once",
+                    static_cast<long long>(groups), static_cast<long long>(slots));
+      }
+      const int64_t tiles = (std::max(max_nk, 1) + 63) / 64;
+      const int64_t n = std::min<int64_t>(per_group, attn_mma_max_fused_chunks());
+      p.chunk = static_cast<int>(64 * ((tiles + n - 1) / n));
+      items = attn_mma_items(p, c->len.data());
+    } else if (per_group >= 2 && max_nk > 0 &&
+               static_cast<int64_t>(min_nk) * 8 >= static_cast<int64_t>(max_nk) * 7) {
       const int64_t tiles = (max_nk + 63) / 64;
       p.chunk = static_cast<int>(64 * ((tiles + per_group - 1) / per_group));
       items = attn_mma_items(p, c->len.data());
@@ -301,6 +325,7 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
   // the tensor-core kernel merges its own chunks when they are few: one CTA
   // walking many chunks would be a long tail, which the parallel combine avoids
   const bool fused = mma && p.nchunks <= attn_mma_max_fused_chunks();
+  if (mode == 2 && !fused) return fail(B2A_EINVAL, "the split exchange needs an f16 or bf16 cache");
   if (fused) {
     const size_t cbytes = static_cast<size_t>(p.batch) * p.num_layers * p.kv_heads * sizeof(int32_t);
     if (cbytes > ctx->d_counters_bytes) {
@@ -425,6 +450,95 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
   B2A_CUDA(cudaStreamSynchronize(ctx->copy_out), "waiting for the results");
   B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the kernels");
   return check_device_error(ctx);
+}
+
+
+// A new token's attention over the positions this cache holds (split-KV
+// decode): ex == nullptr writes the partials [batch][heads][D+4] (fuse mode 1);
+// otherwise the kernel exchanges them with the other ranks and writes the
+// combined output in out_dtype (fuse mode 2).
+b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_heads,
+                            const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
+                            const int32_t* q_positions, b2a_exchange* ex, void* out, b2a_dtype out_dtype, int flags) {
+  b2a_status s = check_cache_shape(c, rope, num_heads);
+  if (s != B2A_OK) return s;
+  if (q == nullptr || out == nullptr || q_positions == nullptr) return fail(B2A_EINVAL, "null argument");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(B2A_EINVAL, "give both new keys and values, or neither");
+  if (!valid_dtype(in_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  const int extra = k_new ? 1 : 0;
+  int max_keys = 0;
+  for (int b = 0; b < c->batch; b++) {
+    if (c->len[b] + extra > c->capacity) {
+      return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", c->len[b], c->capacity, extra);
+    }
+    if (c->len[b] + extra > max_keys) max_keys = c->len[b] + extra;
+  }
+  if (flags == B2A_HOST) {
+    for (int b = 0; b < c->batch; b++) {
+      if (q_positions[b] < 0 || q_positions[b] >= rope->max_positions) {
+        return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", q_positions[b] + 1, rope->max_positions);
+      }
+    }
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  AttnParams p = base_params(ctx, c, rope);
+  p.seq_begin = 0;
+  p.batch = c->batch;
+  p.num_layers = 1;
+  p.layer_begin = layer;
+  p.tokens = 1;
+  p.heads = num_heads;
+  p.group = num_heads / c->kv_heads;
+  p.in_dtype = static_cast<int>(in_dtype);
+  p.q = q;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.q_pos = q_positions;
+  p.horizon_extra = extra;
+  const int mode = ex ? 2 : 1;
+  const b2a_dtype odt = ex ? out_dtype : B2A_F32;
+  if (ex) {
+    for (int r = 0; r < ex->world; r++) {
+      p.x_peer[r] = static_cast<float*>(ex->peer[r]);
+      p.f_peer[r] = reinterpret_cast<int32_t*>(static_cast<char*>(ex->peer[r]) + ex->f_off);
+    }
+    p.x_local = static_cast<const float*>(ex->base);
+    p.f_local = reinterpret_cast<const int32_t*>(static_cast<char*>(ex->base) + ex->f_off);
+    p.x_epoch = reinterpret_cast<int32_t*>(static_cast<char*>(ex->base) + ex->c_off);
+    p.x_done = p.x_epoch + 1;
+    p.x_world = ex->world;
+    p.x_rank = ex->rank;
+    p.x_rows = ex->rows;
+    p.x_groups = ex->groups;
+  }
+  const size_t ies = dtype_size(in_dtype);
+  const size_t q_bytes = static_cast<size_t>(c->batch) * num_heads * c->head_dim * ies;
+  const size_t kv_bytes = static_cast<size_t>(c->batch) * c->kv_heads * c->head_dim * ies;
+  const size_t out_bytes = static_cast<size_t>(c->batch) * num_heads *
+                           (ex ? c->head_dim * dtype_size(out_dtype) : (c->head_dim + 4) * sizeof(float));
+  void* dout = out;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int iq = st.add(q_bytes), ik = st.add(k_new ? kv_bytes : 0), iv = st.add(k_new ? kv_bytes : 0),
+        io = st.add(out_bytes), ipos = st.add(sizeof(int32_t) * c->batch);
+    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
+    p.q = st.ptr(ctx, iq);
+    if (k_new) {
+      if ((s = h2d(ctx, st.ptr(ctx, ik), k_new, kv_bytes)) != B2A_OK) return s;
+      if ((s = h2d(ctx, st.ptr(ctx, iv), v_new, kv_bytes)) != B2A_OK) return s;
+      p.k_new = st.ptr(ctx, ik);
+      p.v_new = st.ptr(ctx, iv);
+    }
+    if ((s = h2d(ctx, st.ptr(ctx, ipos), q_positions, sizeof(int32_t) * c->batch)) != B2A_OK) return s;
+    p.q_pos = static_cast<const int32_t*>(st.ptr(ctx, ipos));
+    dout = st.ptr(ctx, io);
+  }
+  if ((s = run_split_kv(ctx, c, p, max_keys, dout, static_cast<int>(odt), mode)) != B2A_OK) return s;
+  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
+  return B2A_OK;
 }
 
 }  // namespace
@@ -1133,68 +1247,114 @@ b2a_status b2a_grouped_attention(b2a_ctx* ctx, const float* q, const float* keys
 b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_heads,
                                         const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
                                         const int32_t* q_positions, float* partial, int flags) {
-  b2a_status s = check_cache_shape(c, rope, num_heads);
-  if (s != B2A_OK) return s;
-  if (q == nullptr || partial == nullptr || q_positions == nullptr) return fail(B2A_EINVAL, "null argument");
-  if ((k_new == nullptr) != (v_new == nullptr)) return fail(B2A_EINVAL, "give both new keys and values, or neither");
-  if (!valid_dtype(in_dtype)) return fail(B2A_EINVAL, "unknown dtype");
-  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
-  const int extra = k_new ? 1 : 0;
-  int max_keys = 0;
-  for (int b = 0; b < c->batch; b++) {
-    if (c->len[b] + extra > c->capacity) {
-      return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", c->len[b], c->capacity, extra);
-    }
-    if (c->len[b] + extra > max_keys) max_keys = c->len[b] + extra;
+  if (partial == nullptr) return fail(B2A_EINVAL, "null argument");
+  return decode_positions(ctx, c, rope, layer, num_heads, q, k_new, v_new, in_dtype, q_positions, nullptr, partial,
+                          B2A_F32, flags);
+}
+
+b2a_status b2a_exchange_create(b2a_ctx* ctx, int world, int rank, int batch, int num_heads, int num_kv_heads,
+                               b2a_exchange** out) {
+  if (ctx == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
+  *out = nullptr;
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world) {
+    return fail(B2A_EINVAL, "rank %d of world %d: the exchange takes 1..%d ranks", rank, world, kMaxWorld);
   }
-  if (flags == B2A_HOST) {
-    for (int b = 0; b < c->batch; b++) {
-      if (q_positions[b] < 0 || q_positions[b] >= rope->max_positions) {
-        return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", q_positions[b] + 1, rope->max_positions);
-      }
-    }
+  if (batch < 1 || num_kv_heads < 1 || num_heads < 1 || num_heads % num_kv_heads != 0) {
+    return fail(B2A_EINVAL, "bad exchange shape: batch %d, heads %d, kv heads %d", batch, num_heads, num_kv_heads);
   }
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
-  AttnParams p = base_params(ctx, c, rope);
-  p.seq_begin = 0;
-  p.batch = c->batch;
-  p.num_layers = 1;
-  p.layer_begin = layer;
-  p.tokens = 1;
-  p.heads = num_heads;
-  p.group = num_heads / c->kv_heads;
-  p.in_dtype = static_cast<int>(in_dtype);
-  p.q = q;
-  p.k_new = k_new;
-  p.v_new = v_new;
-  p.q_pos = q_positions;
-  p.horizon_extra = extra;
-  const size_t ies = dtype_size(in_dtype);
-  const size_t q_bytes = static_cast<size_t>(c->batch) * num_heads * c->head_dim * ies;
-  const size_t kv_bytes = static_cast<size_t>(c->batch) * c->kv_heads * c->head_dim * ies;
-  const size_t part_bytes = static_cast<size_t>(c->batch) * num_heads * (c->head_dim + 4) * 4;
-  float* dpart = partial;
-  if (flags == B2A_HOST) {
-    Stage st;
-    int iq = st.add(q_bytes), ik = st.add(k_new ? kv_bytes : 0), iv = st.add(k_new ? kv_bytes : 0),
-        ip = st.add(part_bytes), ipos = st.add(sizeof(int32_t) * c->batch);
-    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
-    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
-    p.q = st.ptr(ctx, iq);
-    if (k_new) {
-      if ((s = h2d(ctx, st.ptr(ctx, ik), k_new, kv_bytes)) != B2A_OK) return s;
-      if ((s = h2d(ctx, st.ptr(ctx, iv), v_new, kv_bytes)) != B2A_OK) return s;
-      p.k_new = st.ptr(ctx, ik);
-      p.v_new = st.ptr(ctx, iv);
-    }
-    if ((s = h2d(ctx, st.ptr(ctx, ipos), q_positions, sizeof(int32_t) * c->batch)) != B2A_OK) return s;
-    p.q_pos = static_cast<const int32_t*>(st.ptr(ctx, ipos));
-    dpart = static_cast<float*>(st.ptr(ctx, ip));
+  b2a_exchange* ex = new (std::nothrow) b2a_exchange();
+  if (ex == nullptr) return fail(B2A_ECUDA, "out of host memory for the exchange");
+  ex->device = ctx->device;
+  ex->world = world;
+  ex->rank = rank;
+  ex->batch = batch;
+  ex->heads = num_heads;
+  ex->kv_heads = num_kv_heads;
+  ex->rows = batch * num_heads;
+  ex->groups = batch * num_kv_heads;
+  const size_t x_bytes = 2ull * world * ex->rows * (64 + 4) * sizeof(float);
+  const size_t f_bytes = 2ull * world * ex->groups * sizeof(int32_t);
+  ex->f_off = (x_bytes + 255) & ~size_t(255);
+  ex->c_off = (ex->f_off + f_bytes + 255) & ~size_t(255);
+  ex->bytes = ex->c_off + 256;
+  cudaError_t e = cudaMalloc(&ex->base, ex->bytes);
+  if (e == cudaSuccess) e = cudaMemset(ex->base, 0, ex->bytes);
+  if (e != cudaSuccess) {
+    if (ex->base) cudaFree(ex->base);
+    delete ex;
+    return cuda_fail(e, "allocating the exchange buffer");
   }
-  if ((s = run_split_kv(ctx, c, p, max_keys, dpart, B2A_F32, 1)) != B2A_OK) return s;
-  if (flags == B2A_HOST) return d2h_sync(ctx, partial, dpart, part_bytes);
+  for (int r = 0; r < kMaxWorld; r++) ex->peer[r] = nullptr;
+  ex->peer[rank] = ex->base;
+  *out = ex;
   return B2A_OK;
+}
+
+b2a_status b2a_exchange_handle(const b2a_exchange* ex, void* handle) {
+  if (ex == nullptr || handle == nullptr) return fail(B2A_EINVAL, "null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == B2A_EXCHANGE_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  cudaSetDevice(ex->device);
+  B2A_CUDA(cudaIpcGetMemHandle(&h, ex->base), "exporting the exchange buffer");
+  std::memcpy(handle, &h, sizeof(h));
+  return B2A_OK;
+}
+
+b2a_status b2a_exchange_open(b2a_exchange* ex, const void* handles) {
+  if (ex == nullptr || handles == nullptr) return fail(B2A_EINVAL, "null argument");
+  cudaSetDevice(ex->device);
+  for (int r = 0; r < ex->world; r++) {
+    if (r == ex->rank || ex->peer[r] != nullptr) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(handles) + static_cast<size_t>(r) * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    B2A_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess), "opening a peer's exchange buffer");
+    ex->peer[r] = ptr;
+    ex->opened[r] = true;
+  }
+  return B2A_OK;
+}
+
+b2a_status b2a_exchange_connect_local(b2a_exchange* ex, int peer, const b2a_exchange* other) {
+  if (ex == nullptr || other == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (peer < 0 || peer >= ex->world || peer == ex->rank) return fail(B2A_EINVAL, "bad peer rank %d", peer);
+  if (other->device != ex->device || other->bytes != ex->bytes || other->world != ex->world || other->rank != peer) {
+    return fail(B2A_EINVAL, "exchange %d is not rank %d of the same shape on this device", other->rank, peer);
+  }
+  ex->peer[peer] = other->base;
+  ex->opened[peer] = false;
+  return B2A_OK;
+}
+
+b2a_status b2a_exchange_destroy(b2a_exchange* ex) {
+  if (ex == nullptr) return B2A_OK;
+  cudaSetDevice(ex->device);
+  for (int r = 0; r < kMaxWorld; r++) {
+    if (ex->opened[r] && ex->peer[r] != nullptr) cudaIpcCloseMemHandle(ex->peer[r]);
+  }
+  cudaFree(ex->base);
+  delete ex;
+  return B2A_OK;
+}
+
+b2a_status b2a_attention_decode_split(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_heads,
+                                      const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
+                                      const int32_t* q_positions, b2a_exchange* ex, void* out, b2a_dtype out_dtype,
+                                      int flags) {
+  if (ex == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (!valid_dtype(out_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  if (c != nullptr && (c->batch != ex->batch || c->kv_heads != ex->kv_heads || num_heads != ex->heads)) {
+    return fail(B2A_EINVAL, "the exchange was made for batch %d, %d/%d heads; the call has batch %d, %d/%d", ex->batch,
+                ex->heads, ex->kv_heads, c->batch, num_heads, c->kv_heads);
+  }
+  if (c != nullptr && c->device != ex->device) return fail(B2A_EINVAL, "the exchange lives on another device");
+  for (int r = 0; r < ex->world; r++) {
+    if (ex->peer[r] == nullptr) return fail(B2A_EINVAL, "exchange rank %d is not connected; open the handles first", r);
+  }
+  return decode_positions(ctx, c, rope, layer, num_heads, q, k_new, v_new, in_dtype, q_positions, ex, out, out_dtype,
+                          flags);
 }
 
 b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch, int num_heads, int head_dim,

@@ -103,6 +103,7 @@ inline size_t dtype_size(b2a_dtype d) { return d == B2A_F32 ? 4 : 2; }
 // ---- kernel parameter blocks -------------------------------------------------
 // Attention over a head-major cache: rows of queries (b, layer, t, head).
 constexpr int kLenInline = 64;
+constexpr int kMaxWorld = 8;   // ranks of a peer exchange
 
 struct AttnParams {
   const void* kc;
@@ -145,6 +146,19 @@ struct AttnParams {
   int fuse_dtype;
   int fuse_mode;
   int32_t* counters;
+  // fuse_mode 2 (split-KV across ranks): each group's merged partial is stored
+  // into every rank's exchange buffer, x_peer[r] = [2][world][x_rows][D+4] f32,
+  // with a flag per (parity, source rank, group) in f_peer[r]; the group's last
+  // CTA then waits for all ranks' flags in its own buffer (x_local, f_local)
+  // and writes the combined output to fuse_out. x_epoch counts steps (bumped
+  // by the launch's last CTA, counted in x_done).
+  float* x_peer[kMaxWorld];
+  int32_t* f_peer[kMaxWorld];
+  const float* x_local;
+  const int32_t* f_local;
+  int32_t* x_epoch;
+  int32_t* x_done;
+  int x_world, x_rank, x_rows, x_groups;
 };
 
 struct CombineParams {

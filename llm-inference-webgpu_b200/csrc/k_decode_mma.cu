@@ -178,6 +178,28 @@ __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
   return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
 }
 
+constexpr long long kPeerWaitNs = 1000000000LL;     // exchange waits give up after ~1 s
+constexpr int kErrPeerTimeout = 4;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ int ld_acquire_sys(const int32_t* f) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+// fuse_mode 2: counts this CTA as finished; the launch's last CTA advances the
+// exchange's step counter (every CTA that reads it has done so before counting).
+__device__ __forceinline__ void exchange_done(const AttnParams& p) {
+  if (atomicAdd(p.x_done, 1) == static_cast<int>(gridDim.x) - 1) {
+    *p.x_done = 0;
+    atomicAdd(p.x_epoch, 1);
+  }
+}
+
 // Byte offset of (row, 16-byte chunk) in a 128-byte-swizzled tile of 128-byte rows.
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -470,8 +492,9 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int64_t part_row = static_cast<int64_t>(p.nchunks) * (kD + 4);
   float* part_base = p.partial + row0 * part_row;            // chunk 0 of head 0 of this group
   float* part = part_base + c * (kD + 4);
-  // A group whose keys fit in one chunk writes its final result directly.
-  const bool direct = p.fuse_out != nullptr && cnt == 1;
+  // A group whose keys fit in one chunk writes its final result directly
+  // (except across ranks, where every group goes through the exchange).
+  const bool direct = p.fuse_out != nullptr && cnt == 1 && p.fuse_mode != 2;
   for (int idx = tid; idx < G * kD; idx += kConsumerWarps * 32) {
     const int h = idx / kD, d = idx % kD;
     float mx = -CUDART_INF_F;
@@ -514,91 +537,177 @@ __global__ void __launch_bounds__(kThreads, 3)
   if (p.fuse_out == nullptr || direct) return;
 
   // ---- fused merge: the last CTA of this (sequence, layer, KV head) to finish
-  // merges the group's `cnt` chunk partials (threadfence-and-count pattern).
-  __threadfence();
+  // merges the group's `cnt` chunk partials. The barrier orders every thread's
+  // partial stores before thread 0's acquire-release add (cumulative at GPU
+  // scope); in the last CTA the same add acquires every other CTA's stores.
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
   if (tid == 0) {
     int32_t* ctr = p.counters + (static_cast<int64_t>(b) * p.num_layers + l) * p.kv_heads + g;
-    const int prev = atomicAdd(ctr, 1);
+    int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
     const bool last = prev == cnt - 1;
     if (last) *ctr = 0;   // ready for the next launch
     ms.item[3] = last ? 1 : 0;
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  if (ms.item[3] == 0) return;
-  __threadfence();
-  // per head (one warp each, a lane per chunk and chunk + 32): the chunk
-  // weights 2^(m_c - m*) into shared memory (the warp-merge area is free now)
-  float* wts = &ms.o[0][0][0];   // [8 heads][kMaxFusedChunks]
+  if (ms.item[3] == 0) {
+    if (p.fuse_mode == 2 && tid == 0) exchange_done(p);
+    return;
+  }
+  float* wts = &ms.o[0][0][0];   // two-pass merge: [8 heads][kMaxFusedChunks] chunk weights
+  float* xs = wts + 8 * kMaxFusedChunks;   // fuse_mode 2: the group's merged partial [G][D+4]
   float* hinv = &ms.l[0][0];     // per head: 1/L (or L), and m* in ms.m
-  for (int h = warp; h < G; h += kConsumerWarps) {
-    const float* ph = part_base + h * part_row;
-    float mi[2], li[2];
-    float mx = -CUDART_INF_F;
+  // one merged element of head h, dim d (unnormalised sum v)
+  auto put = [&](int h, int d, float v) {
+    if (p.fuse_mode == 0) {
+      st_from_f32(p.fuse_out, (row0 + h) * kD + d, p.fuse_dtype, v * hinv[h]);
+      return;
+    }
+    float* o = p.fuse_mode == 2 ? xs + h * (kD + 4) : static_cast<float*>(p.fuse_out) + (row0 + h) * (kD + 4);
+    o[d] = v;
+    if (d == 0) {
+      o[kD] = ms.m[0][h];
+      o[kD + 1] = hinv[h];
+      o[kD + 2] = 0.f;
+      o[kD + 3] = 0.f;
+    }
+  };
+  {
+    // two passes over the partials (L2): per head (one warp each, a lane per
+    // chunk and chunk + 32) the chunk weights 2^(m_c - m*) into shared memory,
+    // then the weighted sum with a thread per (head, 4 dims), whose loads are
+    // coalesced across the warp
+    for (int h = warp; h < G; h += kConsumerWarps) {
+      const float* ph = part_base + h * part_row;
+      float mi[2], li[2];
+      float mx = -CUDART_INF_F;
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int cc = lane + 32 * u;
-      mi[u] = -CUDART_INF_F;
-      li[u] = 0.f;
-      if (cc < cnt) {
-        mi[u] = __ldcg(ph + cc * (kD + 4) + kD);
-        li[u] = __ldcg(ph + cc * (kD + 4) + kD + 1);
+      for (int u = 0; u < 2; u++) {
+        const int cc = lane + 32 * u;
+        mi[u] = -CUDART_INF_F;
+        li[u] = 0.f;
+        if (cc < cnt) {
+          mi[u] = __ldcg(ph + cc * (kD + 4) + kD);
+          li[u] = __ldcg(ph + cc * (kD + 4) + kD + 1);
+        }
+        if (li[u] > 0.f) mx = fmaxf(mx, mi[u]);
       }
-      if (li[u] > 0.f) mx = fmaxf(mx, mi[u]);
-    }
-    for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
-    float L = 0.f;
+      for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+      float L = 0.f;
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const float w = li[u] > 0.f ? exp2f(mi[u] - mx) : 0.f;
-      wts[h * kMaxFusedChunks + lane + 32 * u] = w;
-      L = fmaf(w, li[u], L);
+      for (int u = 0; u < 2; u++) {
+        const float w = li[u] > 0.f ? exp2f(mi[u] - mx) : 0.f;
+        wts[h * kMaxFusedChunks + lane + 32 * u] = w;
+        L = fmaf(w, li[u], L);
+      }
+      for (int x = 16; x > 0; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+      if (lane == 0) {
+        hinv[h] = p.fuse_mode == 0 ? 1.f / L : L;
+        ms.m[0][h] = mx;
+      }
     }
-    for (int x = 16; x > 0; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
-    if (lane == 0) {
-      hinv[h] = p.fuse_mode == 0 ? 1.f / L : L;
-      ms.m[0][h] = mx;
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    // a thread per (head, 4 dims), 32 chunk loads in flight at a time
+    for (int t = tid; t < G * (kD / 4); t += kConsumerWarps * 32) {
+      const int h = t / (kD / 4), d4 = t % (kD / 4);
+      const float4* src = reinterpret_cast<const float4*>(part_base + h * part_row) + d4;
+      constexpr int kRowVec = (kD + 4) / 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c0 = 0; c0 < cnt; c0 += 32) {
+        float4 v[32];
+#pragma unroll
+        for (int u = 0; u < 32; u++)
+          v[u] = c0 + u < cnt ? __ldcg(src + (c0 + u) * kRowVec) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 32; u++) {
+          const float w = wts[h * kMaxFusedChunks + c0 + u];   // 0 past cnt
+          acc.x = fmaf(w, v[u].x, acc.x);
+          acc.y = fmaf(w, v[u].y, acc.y);
+          acc.z = fmaf(w, v[u].z, acc.z);
+          acc.w = fmaf(w, v[u].w, acc.w);
+        }
+      }
+      put(h, 4 * d4, acc.x);
+      put(h, 4 * d4 + 1, acc.y);
+      put(h, 4 * d4 + 2, acc.z);
+      put(h, 4 * d4 + 3, acc.w);
+    }
+  }
+  if (p.fuse_mode != 2) return;
+
+  // ---- exchange across ranks: store this group's merged partial into every
+  // rank's buffer (peer stores over NVLink), raise this rank's flag there,
+  // wait for every rank's flag here, then combine in ascending rank order.
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  const int epoch = __ldcg(p.x_epoch) + 1;
+  const int parity = epoch & 1;
+  const int grp = (b * p.num_layers + l) * p.kv_heads + g;
+  constexpr int kRowVec = (kD + 4) / 4;
+  const int nvec = G * kRowVec;
+  const float4* xs4 = reinterpret_cast<const float4*>(xs);
+  for (int i = tid; i < p.x_world * nvec; i += kConsumerWarps * 32) {
+    const int r = i / nvec, k = i % nvec;
+    float4* dst = reinterpret_cast<float4*>(
+        p.x_peer[r] + ((static_cast<int64_t>(parity) * p.x_world + p.x_rank) * p.x_rows + row0) * (kD + 4));
+    dst[k] = xs4[k];
+  }
+  // the barrier orders all threads' peer stores before the flag stores, whose
+  // release at system scope makes them visible to the rank that acquires the flag
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  if (tid < p.x_world) {
+    int32_t* f = p.f_peer[tid] + (parity * p.x_world + p.x_rank) * p.x_groups + grp;
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+    const int32_t* mine = p.f_local + (parity * p.x_world + tid) * p.x_groups + grp;
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_sys(mine) != epoch) {
+      if (globaltimer_ns() - t0 > kPeerWaitNs) {
+        atomicOr(p.err, kErrPeerTimeout);
+        break;
+      }
+      __nanosleep(100);
     }
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  // weighted sum of the chunks' O rows: a thread per (head, 4 dims), 32
-  // chunk loads in flight at a time (16-byte loads, rows are 272 bytes)
+  // every rank's (m, l, 4 dims) for this thread's (head, 4 dims) in one round trip
   for (int t = tid; t < G * (kD / 4); t += kConsumerWarps * 32) {
     const int h = t / (kD / 4), d4 = t % (kD / 4);
-    const float4* src = reinterpret_cast<const float4*>(part_base + h * part_row) + d4;
-    constexpr int kRowVec = (kD + 4) / 4;
+    float mr[kMaxWorld], lr[kMaxWorld];
+    float4 vr[kMaxWorld];
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; r++) {
+      mr[r] = -CUDART_INF_F;
+      lr[r] = 0.f;
+      vr[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < p.x_world) {
+        const float* xr = p.x_local + ((static_cast<int64_t>(parity) * p.x_world + r) * p.x_rows + row0 + h) * (kD + 4);
+        mr[r] = __ldcg(xr + kD);
+        lr[r] = __ldcg(xr + kD + 1);
+        vr[r] = __ldcg(reinterpret_cast<const float4*>(xr) + d4);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; r++)
+      if (lr[r] > 0.f) mx = fmaxf(mx, mr[r]);
+    float L = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c0 = 0; c0 < cnt; c0 += 32) {
-      float4 v[32];
 #pragma unroll
-      for (int u = 0; u < 32; u++)
-        v[u] = c0 + u < cnt ? __ldcg(src + (c0 + u) * kRowVec) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int u = 0; u < 32; u++) {
-        const float w = wts[h * kMaxFusedChunks + c0 + u];   // 0 past cnt
-        acc.x = fmaf(w, v[u].x, acc.x);
-        acc.y = fmaf(w, v[u].y, acc.y);
-        acc.z = fmaf(w, v[u].z, acc.z);
-        acc.w = fmaf(w, v[u].w, acc.w);
+    for (int r = 0; r < kMaxWorld; r++) {
+      if (lr[r] > 0.f) {
+        const float w = exp2f(mr[r] - mx);
+        L = fmaf(w, lr[r], L);
+        acc.x = fmaf(w, vr[r].x, acc.x);
+        acc.y = fmaf(w, vr[r].y, acc.y);
+        acc.z = fmaf(w, vr[r].z, acc.z);
+        acc.w = fmaf(w, vr[r].w, acc.w);
       }
     }
+    const float inv = 1.f / L;
     const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-    if (p.fuse_mode == 0) {
 #pragma unroll
-      for (int e = 0; e < 4; e++)
-        st_from_f32(p.fuse_out, (row0 + h) * kD + 4 * d4 + e, p.fuse_dtype, a4[e] * hinv[h]);
-    } else {
-      float* o = static_cast<float*>(p.fuse_out) + (row0 + h) * (kD + 4);
-#pragma unroll
-      for (int e = 0; e < 4; e++) o[4 * d4 + e] = a4[e];
-      if (d4 == 0) {
-        o[kD] = ms.m[0][h];
-        o[kD + 1] = hinv[h];
-        o[kD + 2] = 0.f;
-        o[kD + 3] = 0.f;
-      }
-    }
+    for (int e = 0; e < 4; e++) st_from_f32(p.fuse_out, (row0 + h) * kD + 4 * d4 + e, p.fuse_dtype, a4[e] * inv);
   }
+  if (tid == 0) exchange_done(p);
 }
 
 int attn_mma_max_fused_chunks() { return kMaxFusedChunks; }

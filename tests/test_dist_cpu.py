@@ -155,3 +155,41 @@ def test_split_kv_step_missing_rank_fails_fast(tmp_path, oracle):
     _, _, _, _, paths = _run(2, 1, tmp_path, oracle)
     assert os.path.exists(paths[0] + ".err"), "rank 0 should have seen the collective fail"
     assert not os.path.exists(paths[0])
+
+
+def _handle_worker(rank, world, port, result_path):
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "llm-inference-webgpu_b200"))
+    from b2a import dist as bdist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    try:
+        got = bdist.gather_handles(bytes([rank + 1]) * 64, world)
+        with open(result_path, "wb") as f:
+            f.write(got)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_handles_gathered_in_rank_order(tmp_path):
+    """PeerSplitKV's setup step: every rank's 64-byte exchange handle reaches
+    every rank, in rank order (gloo on CPU; NCCL on GPUs)."""
+    import multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    paths = [str(tmp_path / f"h{r}.bin") for r in range(world)]
+    procs = [ctx.Process(target=_handle_worker, args=(r, world, port, paths[r])) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            raise AssertionError("handle exchange hung")
+    want = bytes([1]) * 64 + bytes([2]) * 64
+    for path in paths:
+        with open(path, "rb") as f:
+            assert f.read() == want

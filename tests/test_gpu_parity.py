@@ -393,6 +393,56 @@ def test_split_kv_partials_combine_to_full_decode(ctx, rope, oracle):
         assert_parity(out[b].reshape(-1), ref, "f32", f"split seq {b}")
 
 
+def test_split_exchange_single_rank_matches_decode(ctx, rope, oracle):
+    """The in-kernel exchange path with one rank: the group partials go through
+    the exchange buffer and flags of this GPU only, and the output equals the
+    full decode (several steps, so both buffer parities are used)."""
+    batch, L, dtype = 4, 1500, "f16"
+    c = b2a.GpuKVCache(ctx, cfg(1), L + 1, batch=batch, dtype=dtype)
+    hk, hv = _fill_cache(ctx, c, oracle, [L] * batch, 1, dtype, 700)
+    q = oracle.round_to(oracle.normal_array(batch * H * D, 41), dtype).reshape(batch, H, D)
+    kn = oracle.round_to(oracle.normal_array(batch * KVH * D, 42), dtype).reshape(batch, KVH, D)
+    vn = oracle.round_to(oracle.normal_array(batch * KVH * D, 43), dtype).reshape(batch, KVH, D)
+    ex = b2a.Exchange(ctx, 1, 0, batch, H, KVH)
+    outs = []
+    for _ in range(3):
+        out = np.empty((batch, H, D), np.float32)
+        b2a.decodeSplit(ctx, c, rope, 0, oracle.to_bits(q, dtype), oracle.to_bits(kn, dtype),
+                        oracle.to_bits(vn, dtype), np.full(batch, L, np.int32), ex, out, H, dtype=dtype)
+        outs.append(out)
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+    for b in range(batch):
+        ref, _, _ = _oracle_decode(oracle, q[b], kn[b], vn[b], hk[b, 0], hv[b, 0], L, dtype)
+        assert_parity(outs[0][b].reshape(-1), ref, "f32", f"exchange seq {b}")
+    ex.close()
+
+
+def test_split_exchange_wait_gives_up_with_error(ctx, rope, oracle):
+    """A rank whose peer never arrives: rank 0 of a two-rank exchange whose
+    rank 1 is a second exchange object that no kernel ever serves. The kernel's
+    wait on rank 1's flag gives up after about a second, the call reports
+    B2A_ETIMEDOUT, and the context keeps working."""
+    import time
+    batch, L, dtype = 2, 300, "f16"
+    c = b2a.GpuKVCache(ctx, cfg(1), L + 1, batch=batch, dtype=dtype)
+    _fill_cache(ctx, c, oracle, [L] * batch, 1, dtype, 710)
+    q = oracle.to_bits(oracle.normal_array(batch * H * D, 44).reshape(batch, H, D), dtype)
+    ex0 = b2a.Exchange(ctx, 2, 0, batch, H, KVH)
+    ex1 = b2a.Exchange(ctx, 2, 1, batch, H, KVH)
+    ex0.connect_local(1, ex1)
+    out = np.empty((batch, H, D), np.float32)
+    t0 = time.monotonic()
+    with pytest.raises(b2a.B2AError) as err:
+        b2a.decodeSplit(ctx, c, rope, 0, q, None, None, np.full(batch, L, np.int32), ex0, out, H, dtype=dtype)
+    assert err.value.status == 6, err.value   # B2A_ETIMEDOUT
+    assert time.monotonic() - t0 < 30
+    ex0.close()
+    ex1.close()
+    # the context and cache still serve ordinary calls
+    o2 = np.empty((batch, 1, H, D), np.float32)
+    b2a.attentionDecode(ctx, c, rope, 0, q.reshape(batch, 1, H, D), None, None, o2, H, dtype=dtype)
+    assert np.isfinite(o2).all()
+
 
 def test_host_pipelined_decode_matches_device_path(ctx, rope, oracle):
     """The host-pointer decode splits the batch into groups whose uploads,
