@@ -194,7 +194,7 @@ def cpu_decode_sample(lengths: np.ndarray, target_s: float, threads: int = 0):
     t0 = time.perf_counter()
     _, used = o.batched_decode_f16(q, H * D, kb, vb, seq_stride, lengths, SEQS, cap, H, KVH, D, H * D, threads)
     t1 = time.perf_counter() - t0
-    n = max(1, min(LAYERS, int(target_s / max(t1, 1e-6))))
+    n = max(1, int(target_s / max(t1, 1e-6)))   # layers timed (the step has LAYERS; more repeat them)
     t0 = time.perf_counter()
     for _ in range(n):
         o.batched_decode_f16(q, H * D, kb, vb, seq_stride, lengths, SEQS, cap, H, KVH, D, H * D, threads)

@@ -1106,12 +1106,16 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* ro
 // ----------------------------------------------------------------- prefill --
 
 namespace {
-// B2A_PREFILL_TILES=1 selects the one-tile-per-CTA prefill kernel for f16
-// caches (the two-tile kernel is the default); read on every call so a
-// process can compare both.
-int prefill_tiles_per_cta() {
+// Query tiles per CTA of the f16-cache prefill: the two-tile kernel halves the
+// CTA count, which pays once there are at least two CTAs per SM to spread
+// (measured: one-tile faster at S <= 2048, two-tile faster at S >= 8192 for 14
+// heads). B2A_PREFILL_TILES=1 or 2 forces a kernel (read on every call, so a
+// process can compare both).
+int prefill_tiles_per_cta(const b2a_ctx* ctx, int count, int heads) {
   const char* v = std::getenv("B2A_PREFILL_TILES");
-  return (v != nullptr && v[0] == '1' && v[1] == 0) ? 1 : 2;
+  if (v != nullptr && (v[0] == '1' || v[0] == '2') && v[1] == 0) return v[0] - '0';
+  const int64_t ctas = static_cast<int64_t>((count + 127) / 128) * heads;
+  return ctas >= 2LL * ctx->sm_count ? 2 : 1;
 }
 }  // namespace
 
@@ -1178,7 +1182,7 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* r
     p.tmap_k = &c->tmap_k;
     p.tmap_v = &c->tmap_v;
   }
-  if (prefill_pair_supported(p) && prefill_tiles_per_cta() != 1) {
+  if (prefill_pair_supported(p) && prefill_tiles_per_cta(ctx, count, num_heads) == 2) {
     // tensor-core causal attention, two heads' 128-query tiles per CTA (f16 cache)
     {
       KernelTimer kt(ctx, K_PREFILL_PAIR);

@@ -266,12 +266,9 @@ def test_prefill_tensor_core(ctx, rope, oracle, monkeypatch, cache_dtype, splits
     """Causal prefill through the tcgen05 kernels: bf16 Q/K/V,
     K/V cached as f16 (bf16 values are exact in f16) or bf16; several calls in a
     row continue one sequence (chunked prefill, past > 0). tiles: query tiles per
-    CTA (the two-head kernel serves f16 caches; B2A_PREFILL_TILES=1 selects the
-    one-tile kernel)."""
-    if tiles == 1:
-        monkeypatch.setenv("B2A_PREFILL_TILES", "1")
-    else:
-        monkeypatch.delenv("B2A_PREFILL_TILES", raising=False)
+    CTA, forced with B2A_PREFILL_TILES (by default f16 caches take the two-head
+    kernel once there are two CTAs per SM, bf16 caches the one-tile kernel)."""
+    monkeypatch.setenv("B2A_PREFILL_TILES", str(tiles))
     n = sum(splits)
     q = oracle.round_to(oracle.normal_array(n * H * D, 71), "bf16").reshape(n, H * D)
     k = oracle.round_to(oracle.normal_array(n * KVH * D, 72), "bf16").reshape(n, KVH * D)
@@ -307,7 +304,7 @@ def test_prefill_tensor_core(ctx, rope, oracle, monkeypatch, cache_dtype, splits
 def test_prefill_pairs_over_group_shapes(ctx, rope, oracle, monkeypatch, nh, nkv, in_dt, out_dt, n):
     """The two-head prefill kernel pairs the query heads of each KV group (an odd
     group leaves one head alone): other group sizes, input and output dtypes."""
-    monkeypatch.delenv("B2A_PREFILL_TILES", raising=False)
+    monkeypatch.setenv("B2A_PREFILL_TILES", "2")
     q = oracle.normal_array(n * nh * D, 81).reshape(n, nh * D)
     k = oracle.normal_array(n * nkv * D, 82).reshape(n, nkv * D)
     v = oracle.normal_array(n * nkv * D, 83).reshape(n, nkv * D)
