@@ -234,9 +234,9 @@ b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, i
  * (b2a_exchange_open). Then every rank calls b2a_attention_decode_split once per
  * step, the same number of times: inside the attention kernel the last CTA of
  * each (sequence, KV head) stores the group's merged partial into every rank's
- * exchange buffer (peer stores over NVLink), raises a per-group flag there, waits
- * (at most ~1 s) for the group's partials from all ranks and writes the combined,
- * normalised output. A wait that gives up makes that call (host pointers) or the
+ * exchange buffer (peer stores over NVLink, each value tagged with the step
+ * number in the same 64-bit word), waits (at most ~1 s) until all ranks' words
+ * for the group carry the step and writes the combined, normalised output. A wait that gives up makes that call (host pointers) or the
  * next b2a_synchronize return B2A_ETIMEDOUT; recreate the exchange on every rank
  * after that. The cache's (sequence, KV head) groups must not outnumber the
  * CTAs that fit on the GPU at once (three per SM). */

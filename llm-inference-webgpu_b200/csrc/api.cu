@@ -12,13 +12,13 @@
 #include "b2a_internal.cuh"
 
 // A split-KV exchange (include/b2a.h): one device allocation holding the
-// partials [2 parities][world][rows][68] f32, the flags [2][world][groups] i32
-// and the step / done counters; peer[r] is rank r's allocation as mapped here.
+// partials [2 parities][world][rows][68] as 64-bit (value, step) words and the
+// step / done counters; peer[r] is rank r's allocation as mapped here.
 struct b2a_exchange {
   int device = 0;
   int world = 1, rank = 0, batch = 0, heads = 0, kv_heads = 0, rows = 0, groups = 0;
   void* base = nullptr;
-  size_t bytes = 0, f_off = 0, c_off = 0;
+  size_t bytes = 0, c_off = 0;
   void* peer[b2a::kMaxWorld] = {};
   bool opened[b2a::kMaxWorld] = {};   // peer[r] came from cudaIpcOpenMemHandle
 };
@@ -501,17 +501,14 @@ b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, 
   const b2a_dtype odt = ex ? out_dtype : B2A_F32;
   if (ex) {
     for (int r = 0; r < ex->world; r++) {
-      p.x_peer[r] = static_cast<float*>(ex->peer[r]);
-      p.f_peer[r] = reinterpret_cast<int32_t*>(static_cast<char*>(ex->peer[r]) + ex->f_off);
+      p.x_peer[r] = static_cast<uint64_t*>(ex->peer[r]);
     }
-    p.x_local = static_cast<const float*>(ex->base);
-    p.f_local = reinterpret_cast<const int32_t*>(static_cast<char*>(ex->base) + ex->f_off);
+    p.x_local = static_cast<const uint64_t*>(ex->base);
     p.x_epoch = reinterpret_cast<int32_t*>(static_cast<char*>(ex->base) + ex->c_off);
     p.x_done = p.x_epoch + 1;
     p.x_world = ex->world;
     p.x_rank = ex->rank;
     p.x_rows = ex->rows;
-    p.x_groups = ex->groups;
   }
   const size_t ies = dtype_size(in_dtype);
   const size_t q_bytes = static_cast<size_t>(c->batch) * num_heads * c->head_dim * ies;
@@ -1278,10 +1275,8 @@ b2a_status b2a_exchange_create(b2a_ctx* ctx, int world, int rank, int batch, int
   ex->kv_heads = num_kv_heads;
   ex->rows = batch * num_heads;
   ex->groups = batch * num_kv_heads;
-  const size_t x_bytes = 2ull * world * ex->rows * (64 + 4) * sizeof(float);
-  const size_t f_bytes = 2ull * world * ex->groups * sizeof(int32_t);
-  ex->f_off = (x_bytes + 255) & ~size_t(255);
-  ex->c_off = (ex->f_off + f_bytes + 255) & ~size_t(255);
+  const size_t x_bytes = 2ull * world * ex->rows * (64 + 4) * sizeof(uint64_t);
+  ex->c_off = (x_bytes + 255) & ~size_t(255);
   ex->bytes = ex->c_off + 256;
   cudaError_t e = cudaMalloc(&ex->base, ex->bytes);
   if (e == cudaSuccess) e = cudaMemset(ex->base, 0, ex->bytes);

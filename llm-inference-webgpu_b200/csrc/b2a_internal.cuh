@@ -147,18 +147,17 @@ struct AttnParams {
   int fuse_mode;
   int32_t* counters;
   // fuse_mode 2 (split-KV across ranks): each group's merged partial is stored
-  // into every rank's exchange buffer, x_peer[r] = [2][world][x_rows][D+4] f32,
-  // with a flag per (parity, source rank, group) in f_peer[r]; the group's last
-  // CTA then waits for all ranks' flags in its own buffer (x_local, f_local)
-  // and writes the combined output to fuse_out. x_epoch counts steps (bumped
-  // by the launch's last CTA, counted in x_done).
-  float* x_peer[kMaxWorld];
-  int32_t* f_peer[kMaxWorld];
-  const float* x_local;
-  const int32_t* f_local;
+  // into every rank's exchange buffer, x_peer[r] = [2 parities][world][x_rows]
+  // [D+4] words of 64 bits, each holding one f32 value in its low half and the
+  // step number in its high half (a reader spins on the words themselves, no
+  // separate flag); the group's last CTA then waits for all ranks' words in
+  // its own buffer (x_local) and writes the combined output to fuse_out.
+  // x_epoch counts steps (bumped by the launch's last CTA, counted in x_done).
+  uint64_t* x_peer[kMaxWorld];
+  const uint64_t* x_local;
   int32_t* x_epoch;
   int32_t* x_done;
-  int x_world, x_rank, x_rows, x_groups;
+  int x_world, x_rank, x_rows;
 };
 
 struct CombineParams {

@@ -186,10 +186,13 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ int ld_acquire_sys(const int32_t* f) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* a) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* a, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
 // fuse_mode 2: counts this CTA as finished; the launch's last CTA advances the
 // exchange's step counter (every CTA that reads it has done so before counting).
@@ -636,76 +639,103 @@ __global__ void __launch_bounds__(kThreads, 3)
   if (p.fuse_mode != 2) return;
 
   // ---- exchange across ranks: store this group's merged partial into every
-  // rank's buffer (peer stores over NVLink), raise this rank's flag there,
-  // wait for every rank's flag here, then combine in ascending rank order.
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  // rank's buffer (peer stores over NVLink) as 64-bit words (value, step), then
+  // read every rank's words here until all carry this step, and combine the
+  // ranks in ascending order. A 64-bit aligned store is seen whole or not at
+  // all, so the step half vouches for the value half: no flag, no fence.
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");   // xs complete
   const int epoch = __ldcg(p.x_epoch) + 1;
   const int parity = epoch & 1;
-  const int grp = (b * p.num_layers + l) * p.kv_heads + g;
-  constexpr int kRowVec = (kD + 4) / 4;
-  const int nvec = G * kRowVec;
-  const float4* xs4 = reinterpret_cast<const float4*>(xs);
-  for (int i = tid; i < p.x_world * nvec; i += kConsumerWarps * 32) {
-    const int r = i / nvec, k = i % nvec;
-    float4* dst = reinterpret_cast<float4*>(
-        p.x_peer[r] + ((static_cast<int64_t>(parity) * p.x_world + p.x_rank) * p.x_rows + row0) * (kD + 4));
-    dst[k] = xs4[k];
+  const uint64_t tag = static_cast<uint64_t>(static_cast<uint32_t>(epoch)) << 32;
+  const int nwords = G * (kD + 4);
+  for (int i = tid; i < p.x_world * nwords; i += kConsumerWarps * 32) {
+    const int r = i / nwords, k = i % nwords;
+    uint64_t* dst = p.x_peer[r] + ((static_cast<int64_t>(parity) * p.x_world + p.x_rank) * p.x_rows + row0) * (kD + 4) + k;
+    st_relaxed_sys(dst, tag | __float_as_uint(xs[k]));
   }
-  // the barrier orders all threads' peer stores before the flag stores, whose
-  // release at system scope makes them visible to the rank that acquires the flag
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  if (tid < p.x_world) {
-    int32_t* f = p.f_peer[tid] + (parity * p.x_world + p.x_rank) * p.x_groups + grp;
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
-    const int32_t* mine = p.f_local + (parity * p.x_world + tid) * p.x_groups + grp;
-    const unsigned long long t0 = globaltimer_ns();
-    while (ld_acquire_sys(mine) != epoch) {
-      if (globaltimer_ns() - t0 > kPeerWaitNs) {
-        atomicOr(p.err, kErrPeerTimeout);
-        break;
-      }
-      __nanosleep(100);
+  // read every rank's words until all carry this step: first each rank's
+  // (m, l) per head (a thread per (rank, head)), then each rank's outputs (a
+  // thread per (head, 4 dims)), every load of a pass in flight together
+  const unsigned long long t0 = globaltimer_ns();
+  bool gave_up = false;
+  auto timed_out = [&]() {
+    if (!gave_up && globaltimer_ns() - t0 > kPeerWaitNs) {
+      atomicOr(p.err, kErrPeerTimeout);
+      gave_up = true;
     }
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  // every rank's (m, l, 4 dims) for this thread's (head, 4 dims) in one round trip
-  for (int t = tid; t < G * (kD / 4); t += kConsumerWarps * 32) {
-    const int h = t / (kD / 4), d4 = t % (kD / 4);
+    return gave_up;
+  };
+  const int64_t rank_stride = static_cast<int64_t>(p.x_rows) * (kD + 4);   // words between ranks' slots
+  const uint64_t* slot0 = p.x_local + (static_cast<int64_t>(parity) * p.x_world * p.x_rows + row0) * (kD + 4);
+  float* mlx = xs + 16 * (kD + 4);   // [world][G] weights 2^(m_r - m*) of head h, then 1/L per head
+  if (tid < G) {
+    const uint64_t* src = slot0 + tid * (kD + 4);
     float mr[kMaxWorld], lr[kMaxWorld];
-    float4 vr[kMaxWorld];
-    float mx = -CUDART_INF_F;
+    while (true) {
+      bool ready = true;
 #pragma unroll
-    for (int r = 0; r < kMaxWorld; r++) {
-      mr[r] = -CUDART_INF_F;
-      lr[r] = 0.f;
-      vr[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < p.x_world) {
-        const float* xr = p.x_local + ((static_cast<int64_t>(parity) * p.x_world + r) * p.x_rows + row0 + h) * (kD + 4);
-        mr[r] = __ldcg(xr + kD);
-        lr[r] = __ldcg(xr + kD + 1);
-        vr[r] = __ldcg(reinterpret_cast<const float4*>(xr) + d4);
+      for (int r = 0; r < kMaxWorld; r++) {
+        mr[r] = -CUDART_INF_F;
+        lr[r] = 0.f;
+        if (r < p.x_world) {
+          const uint64_t wm = ld_relaxed_sys(src + r * rank_stride + kD);
+          const uint64_t wl = ld_relaxed_sys(src + r * rank_stride + kD + 1);
+          ready &= static_cast<uint32_t>(wm >> 32) == static_cast<uint32_t>(epoch) &&
+                   static_cast<uint32_t>(wl >> 32) == static_cast<uint32_t>(epoch);
+          mr[r] = __uint_as_float(static_cast<uint32_t>(wm));
+          lr[r] = __uint_as_float(static_cast<uint32_t>(wl));
+        }
       }
+      if (ready || timed_out()) break;
+      __nanosleep(64);
     }
+    float mx = -CUDART_INF_F;
 #pragma unroll
     for (int r = 0; r < kMaxWorld; r++)
       if (lr[r] > 0.f) mx = fmaxf(mx, mr[r]);
     float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < kMaxWorld; r++) {
-      if (lr[r] > 0.f) {
-        const float w = exp2f(mr[r] - mx);
-        L = fmaf(w, lr[r], L);
-        acc.x = fmaf(w, vr[r].x, acc.x);
-        acc.y = fmaf(w, vr[r].y, acc.y);
-        acc.z = fmaf(w, vr[r].z, acc.z);
-        acc.w = fmaf(w, vr[r].w, acc.w);
+      const float w = lr[r] > 0.f ? exp2f(mr[r] - mx) : 0.f;
+      if (r < p.x_world) mlx[r * G + tid] = w;
+      L = fmaf(w, lr[r], L);
+    }
+    mlx[kMaxWorld * G + tid] = 1.f / L;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  for (int t = tid; t < G * (kD / 4); t += kConsumerWarps * 32) {
+    const int h = t / (kD / 4), d4 = t % (kD / 4);
+    const uint64_t* src = slot0 + h * (kD + 4) + 4 * d4;
+    float ov[kMaxWorld][4];
+    while (true) {
+      bool ready = true;
+#pragma unroll
+      for (int r = 0; r < kMaxWorld; r++) {
+        ov[r][0] = ov[r][1] = ov[r][2] = ov[r][3] = 0.f;
+        if (r < p.x_world) {
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const uint64_t wd = ld_relaxed_sys(src + r * rank_stride + e);
+            ready &= static_cast<uint32_t>(wd >> 32) == static_cast<uint32_t>(epoch);
+            ov[r][e] = __uint_as_float(static_cast<uint32_t>(wd));
+          }
+        }
+      }
+      if (ready || timed_out()) break;
+      __nanosleep(64);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; r++) {
+      if (r < p.x_world) {
+        const float w = mlx[r * G + h];
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[e] = fmaf(w, ov[r][e], acc[e]);
       }
     }
-    const float inv = 1.f / L;
-    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+    const float inv = mlx[kMaxWorld * G + h];
 #pragma unroll
-    for (int e = 0; e < 4; e++) st_from_f32(p.fuse_out, (row0 + h) * kD + 4 * d4 + e, p.fuse_dtype, a4[e] * inv);
+    for (int e = 0; e < 4; e++) st_from_f32(p.fuse_out, (row0 + h) * kD + 4 * d4 + e, p.fuse_dtype, acc[e] * inv);
   }
   if (tid == 0) exchange_done(p);
 }
