@@ -222,6 +222,31 @@ b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* cache, const 
 b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch,
                            int num_heads, int head_dim, void* out, b2a_dtype out_dtype, int flags);
 
+/* ---- projections either side of attention: int8 weights, per-row scales -----
+ * The Qwen2.5 layer's q/k/v and output projections (src/cpu/model.js:98-101,
+ * 125-128) over matVec (src/core/ops.js:33-41) with the reference's symmetric
+ * per-channel int8 weights (src/core/quantize.js:36-67). */
+/* Host, no device: quantizeInt8PerChannel. scales[r] = max|w[r][:]| / 127 (f32),
+ * codes = round-half-away-from-zero(w / scale) clamped to [-127, 127]; an
+ * all-zero row gets scale 0 and zero codes. */
+b2a_status b2a_quantize_int8_per_channel(const float* w, int rows, int cols, int8_t* codes, float* scales);
+/* out[t][r] = residual[t][r] + scales[r] * sum_c codes[r][c] * x[t][c] + bias[r],
+ * t < tokens: codes [rows][cols] (cols a multiple of 16; 16-byte aligned on the
+ * device), scales and bias [rows] in their dtypes (bias, residual may be NULL),
+ * x [tokens][cols] (16-byte aligned rows on the device), out and residual
+ * [tokens][rows] in out_dtype. The residual add is o_proj's x += W·a. */
+b2a_status b2a_linear_int8(b2a_ctx* ctx, const int8_t* codes, const void* scales, b2a_dtype scale_dtype,
+                           const void* bias, b2a_dtype bias_dtype, const void* x, b2a_dtype x_dtype, int rows,
+                           int cols, int tokens, const void* residual, void* out, b2a_dtype out_dtype, int flags);
+/* The fused q/k/v projection: codes/scales/bias hold the q rows (q_rows =
+ * num_heads*head_dim), then the k rows, then the v rows (kv_rows each);
+ * q_out [tokens][q_rows], k_out and v_out [tokens][kv_rows] in out_dtype, the
+ * layouts b2a_attention_decode / _prefill take for q, k_new and v_new. */
+b2a_status b2a_qkv_int8(b2a_ctx* ctx, const int8_t* codes, const void* scales, b2a_dtype scale_dtype,
+                        const void* bias, b2a_dtype bias_dtype, const void* x, b2a_dtype x_dtype, int hidden,
+                        int q_rows, int kv_rows, int tokens, void* q_out, void* k_out, void* v_out,
+                        b2a_dtype out_dtype, int flags);
+
 /* ---- split-KV decode with the exchange fused into the attention kernel ------
  * No reference counterpart (the reference runs on one device). The merge is the
  * log-sum-exp combine of b2a_lse_combine, in ascending rank order, so every rank

@@ -8,5 +8,6 @@ library, or without a CUDA device, calls raise.
 """
 from ._lib import B2AError, BusyError, RangeError, load, lib_path  # noqa: F401
 from .attention import (appendRope, attentionDecode, attentionPrefill, decodePartial, decodeSplit,  # noqa: F401
-                        default_context, groupedAttention, kvHeadFor, lseCombine, ropeFrequencies, ropeTables)
+                        default_context, groupedAttention, kvHeadFor, linearInt8, lseCombine, qkvInt8,
+                        quantizeInt8PerChannel, ropeFrequencies, ropeTables)
 from .runtime import CacheConfig, Context, Exchange, GpuKVCache, RopeTable  # noqa: F401

@@ -55,6 +55,9 @@ SIGNATURES = {
     "b2a_grouped_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i]),
     "b2a_attention_decode_partial": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i]),
     "b2a_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _i, _i]),
+    "b2a_quantize_int8_per_channel": (_i, [_vp, _i, _i, _vp, _vp]),
+    "b2a_linear_int8": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp, _i, _i]),
+    "b2a_qkv_int8": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i]),
     "b2a_exchange_create": (_i, [_vp, _i, _i, _i, _i, _i, _pp]),
     "b2a_exchange_handle": (_i, [_vp, _vp]),
     "b2a_exchange_open": (_i, [_vp, _vp]),

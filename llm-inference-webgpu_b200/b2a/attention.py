@@ -153,3 +153,59 @@ def lseCombine(ctx: Context, partials, numParts: int, batch: int, numHeads: int,
     pa, oa = _arg(partials), _arg(out, out_dtype, writable=True)
     check(load().b2a_lse_combine(ctx.handle, pa.ptr, numParts, batch, numHeads, headDim, oa.ptr, DTYPES[oa.dtype],
                                  _where(pa, oa)))
+
+
+# ------------------------------------------------------------- projections --
+
+def quantizeInt8PerChannel(W, rows: int, cols: int) -> dict:
+    """quantizeInt8PerChannel (src/core/quantize.js:36-58), on the host:
+    {'q': int8 [rows, cols], 'scales': f32 [rows], 'rows', 'cols', 'scheme'}."""
+    w = np.ascontiguousarray(np.asarray(W, np.float32).reshape(-1))
+    if w.size != rows * cols:
+        raise ValueError(f"expected {rows * cols} weights, got {w.size}")
+    q = np.zeros(rows * cols, np.int8)
+    scales = np.zeros(rows, np.float32)
+    check(load().b2a_quantize_int8_per_channel(w.ctypes.data, rows, cols, q.ctypes.data, scales.ctypes.data))
+    return {"q": q.reshape(rows, cols), "scales": scales, "rows": rows, "cols": cols, "scheme": "int8-per-channel"}
+
+
+def linearInt8(ctx: Context, codes, scales, bias, x, out, rows: int, cols: int, tokens: int, residual=None,
+               x_dtype: str | None = None, out_dtype: str | None = None, scale_dtype: str | None = None) -> None:
+    """out[t] = residual[t] + scales * (codes @ x[t]) + bias (matVec, src/core/ops.js:33-41, with int8
+    per-row weights); codes int8 [rows, cols], x [tokens, cols], out [tokens, rows]. 16-bit arrays
+    given as uint16 bits name their dtype ("f16"/"bf16")."""
+    ca, sa, ba = _arg_i8(codes), _arg(scales, scale_dtype), _arg(bias)
+    xa = _arg(x, x_dtype)
+    oa = _arg(out, out_dtype, writable=True)
+    ra = _arg(residual, out_dtype)
+    where = _where(ca, sa, ba, xa, oa, ra)
+    check(load().b2a_linear_int8(ctx.handle, ca.ptr, sa.ptr, DTYPES[sa.dtype], ba.ptr if ba else None,
+                                 DTYPES[ba.dtype] if ba else 0, xa.ptr, DTYPES[xa.dtype], rows, cols, tokens,
+                                 ra.ptr if ra else None, oa.ptr, DTYPES[oa.dtype], where))
+
+
+def qkvInt8(ctx: Context, codes, scales, bias, x, q_out, k_out, v_out, hidden: int, q_rows: int, kv_rows: int,
+            tokens: int, x_dtype: str | None = None, out_dtype: str | None = None,
+            scale_dtype: str | None = None) -> None:
+    """The q/k/v projections of src/cpu/model.js:98-101 in one launch: codes hold the q, k and v rows
+    (q_rows, kv_rows, kv_rows); q_out [tokens, q_rows], k_out/v_out [tokens, kv_rows]."""
+    ca, sa, ba = _arg_i8(codes), _arg(scales, scale_dtype), _arg(bias)
+    xa = _arg(x, x_dtype)
+    qa = _arg(q_out, out_dtype, writable=True)
+    ka = _arg(k_out, out_dtype, writable=True)
+    va = _arg(v_out, out_dtype, writable=True)
+    where = _where(ca, sa, ba, xa, qa, ka, va)
+    check(load().b2a_qkv_int8(ctx.handle, ca.ptr, sa.ptr, DTYPES[sa.dtype], ba.ptr if ba else None,
+                              DTYPES[ba.dtype] if ba else 0, xa.ptr, DTYPES[xa.dtype], hidden, q_rows, kv_rows, tokens,
+                              qa.ptr, ka.ptr, va.ptr, DTYPES[_same_dtype(qa, ka, va)], where))
+
+
+def _arg_i8(x):
+    """int8 codes: a numpy int8 array (host) or a torch int8 CUDA tensor (device)."""
+    from .runtime import _Arg, torch as _torch
+    if _torch is not None and isinstance(x, _torch.Tensor):
+        if x.dtype != _torch.int8 or not x.is_contiguous():
+            raise ValueError("codes must be a contiguous int8 tensor")
+        return _Arg(x.data_ptr(), _lib.B2A_DEVICE if x.is_cuda else _lib.B2A_HOST, "i8", x.numel(), x)
+    a = np.ascontiguousarray(x, np.int8)
+    return _Arg(a.ctypes.data, _lib.B2A_HOST, "i8", a.nbytes, a)

@@ -43,7 +43,7 @@ b2a_status cuda_fail(cudaError_t e, const char* what) {
 
 const char* const kKernelNames[K_NUM_KINDS] = {"attention_simt", "attention_mma", "combine", "rope_append",
                                                "write_at", "grouped_generic", "prefill_tc",
-                                               "prefill_pair"};
+                                               "prefill_pair", "linear_int8"};
 
 namespace {
 cudaEvent_t take_event(b2a_ctx* ctx) {
@@ -535,6 +535,86 @@ b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, 
   }
   if ((s = run_split_kv(ctx, c, p, max_keys, dout, static_cast<int>(odt), mode)) != B2A_OK) return s;
   if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
+  return B2A_OK;
+}
+
+
+// Shared body of b2a_linear_int8 / b2a_qkv_int8: validation, staging of host
+// pointers, launch. seg_end lists the cumulative rows of each output.
+b2a_status linear_int8(b2a_ctx* ctx, const int8_t* codes, const void* scales, b2a_dtype scale_dtype, const void* bias,
+                       b2a_dtype bias_dtype, const void* x, b2a_dtype x_dtype, int rows, int cols, int tokens,
+                       const void* residual, void* const* outs, const int* seg_end, int nseg, b2a_dtype out_dtype,
+                       int flags) {
+  if (ctx == nullptr || codes == nullptr || scales == nullptr || x == nullptr) return fail(B2A_EINVAL, "null argument");
+  for (int s = 0; s < nseg; s++)
+    if (outs[s] == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (!valid_dtype(scale_dtype) || !valid_dtype(bias_dtype) || !valid_dtype(x_dtype) || !valid_dtype(out_dtype)) {
+    return fail(B2A_EINVAL, "unknown dtype");
+  }
+  if (rows < 1 || cols < 16 || cols % 16 != 0 || tokens < 0) {
+    return fail(B2A_EINVAL, "linear shape: rows %d, cols %d (a positive multiple of 16), tokens %d", rows, cols, tokens);
+  }
+  if (tokens == 0) return B2A_OK;
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const size_t w_bytes = static_cast<size_t>(rows) * cols;
+  const size_t sc_bytes = static_cast<size_t>(rows) * dtype_size(scale_dtype);
+  const size_t b_bytes = bias ? static_cast<size_t>(rows) * dtype_size(bias_dtype) : 0;
+  const size_t x_bytes = static_cast<size_t>(tokens) * cols * dtype_size(x_dtype);
+  LinearParams p{};
+  p.w = codes;
+  p.scale = scales;
+  p.scale_dtype = static_cast<int>(scale_dtype);
+  p.bias = bias;
+  p.bias_dtype = static_cast<int>(bias_dtype);
+  p.x = x;
+  p.x_dtype = static_cast<int>(x_dtype);
+  p.rows = rows;
+  p.cols = cols;
+  p.tokens = tokens;
+  p.nseg = nseg;
+  p.out_dtype = static_cast<int>(out_dtype);
+  p.residual = residual;
+  size_t out_bytes[3] = {0, 0, 0};
+  for (int s = 0; s < nseg; s++) {
+    p.seg_end[s] = seg_end[s];
+    p.out[s] = outs[s];
+    out_bytes[s] = static_cast<size_t>(tokens) * (seg_end[s] - (s ? seg_end[s - 1] : 0)) * dtype_size(out_dtype);
+  }
+  b2a_status st;
+  if (flags == B2A_HOST) {
+    Stage sg;
+    int iw = sg.add(w_bytes), is = sg.add(sc_bytes), ib = sg.add(b_bytes), ix = sg.add(x_bytes),
+        ir = sg.add(residual ? out_bytes[0] : 0);
+    int io[3] = {sg.add(out_bytes[0]), sg.add(out_bytes[1]), sg.add(out_bytes[2])};
+    if ((st = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, sg.total, "allocating staging")) != B2A_OK) return st;
+    if ((st = h2d(ctx, sg.ptr(ctx, iw), codes, w_bytes)) != B2A_OK) return st;
+    if ((st = h2d(ctx, sg.ptr(ctx, is), scales, sc_bytes)) != B2A_OK) return st;
+    if (bias && (st = h2d(ctx, sg.ptr(ctx, ib), bias, b_bytes)) != B2A_OK) return st;
+    if ((st = h2d(ctx, sg.ptr(ctx, ix), x, x_bytes)) != B2A_OK) return st;
+    if (residual && (st = h2d(ctx, sg.ptr(ctx, ir), residual, out_bytes[0])) != B2A_OK) return st;
+    p.w = static_cast<const int8_t*>(sg.ptr(ctx, iw));
+    p.scale = sg.ptr(ctx, is);
+    p.bias = bias ? sg.ptr(ctx, ib) : nullptr;
+    p.x = sg.ptr(ctx, ix);
+    p.residual = residual ? sg.ptr(ctx, ir) : nullptr;
+    for (int s = 0; s < nseg; s++) p.out[s] = sg.ptr(ctx, io[s]);
+  } else if ((reinterpret_cast<uintptr_t>(codes) & 15) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) {
+    return fail(B2A_EINVAL, "device codes and activations must start on a 16-byte boundary");
+  }
+  cudaError_t e;
+  {
+    KernelTimer kt(ctx, K_LINEAR);
+    e = launch_linear_int8(p, ctx->stream);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "launching the int8 projection");
+  if (flags == B2A_HOST) {
+    for (int s = 0; s < nseg; s++) {
+      B2A_CUDA(cudaMemcpyAsync(outs[s], p.out[s], out_bytes[s], cudaMemcpyDeviceToHost, ctx->stream),
+               "copying results to the host");
+    }
+    return d2h_sync(ctx, nullptr, nullptr, 0);
+  }
   return B2A_OK;
 }
 
@@ -1251,6 +1331,51 @@ b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* c, const b2a_
   if (partial == nullptr) return fail(B2A_EINVAL, "null argument");
   return decode_positions(ctx, c, rope, layer, num_heads, q, k_new, v_new, in_dtype, q_positions, nullptr, partial,
                           B2A_F32, flags);
+}
+
+b2a_status b2a_quantize_int8_per_channel(const float* w, int rows, int cols, int8_t* codes, float* scales) {
+  if (w == nullptr || codes == nullptr || scales == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (rows < 0 || cols < 0) return fail(B2A_EINVAL, "bad shape %d x %d", rows, cols);
+  // src/core/quantize.js:36-58: the row peak over 127 in f64, stored f32; the
+  // codes divide by the f64 scale and round half away from zero (C's round)
+  for (int r = 0; r < rows; r++) {
+    const float* row = w + static_cast<size_t>(r) * cols;
+    double peak = 0.0;
+    for (int c = 0; c < cols; c++) peak = std::max(peak, std::fabs(static_cast<double>(row[c])));
+    const double scale = peak / 127.0;
+    scales[r] = static_cast<float>(scale);
+    int8_t* out = codes + static_cast<size_t>(r) * cols;
+    if (scale == 0.0) {
+      std::memset(out, 0, static_cast<size_t>(cols));
+      continue;
+    }
+    const double inverse = 1.0 / scale;
+    for (int c = 0; c < cols; c++) {
+      const double level = std::round(static_cast<double>(row[c]) * inverse);
+      out[c] = static_cast<int8_t>(std::min(127.0, std::max(-127.0, level)));
+    }
+  }
+  return B2A_OK;
+}
+
+b2a_status b2a_linear_int8(b2a_ctx* ctx, const int8_t* codes, const void* scales, b2a_dtype scale_dtype,
+                           const void* bias, b2a_dtype bias_dtype, const void* x, b2a_dtype x_dtype, int rows,
+                           int cols, int tokens, const void* residual, void* out, b2a_dtype out_dtype, int flags) {
+  void* outs[1] = {out};
+  const int seg_end[1] = {rows};
+  return linear_int8(ctx, codes, scales, scale_dtype, bias, bias_dtype, x, x_dtype, rows, cols, tokens, residual,
+                     outs, seg_end, 1, out_dtype, flags);
+}
+
+b2a_status b2a_qkv_int8(b2a_ctx* ctx, const int8_t* codes, const void* scales, b2a_dtype scale_dtype,
+                        const void* bias, b2a_dtype bias_dtype, const void* x, b2a_dtype x_dtype, int hidden,
+                        int q_rows, int kv_rows, int tokens, void* q_out, void* k_out, void* v_out,
+                        b2a_dtype out_dtype, int flags) {
+  if (q_rows < 1 || kv_rows < 1) return fail(B2A_EINVAL, "q rows %d and kv rows %d must be positive", q_rows, kv_rows);
+  void* outs[3] = {q_out, k_out, v_out};
+  const int seg_end[3] = {q_rows, q_rows + kv_rows, q_rows + 2 * kv_rows};
+  return linear_int8(ctx, codes, scales, scale_dtype, bias, bias_dtype, x, x_dtype, q_rows + 2 * kv_rows, hidden,
+                     tokens, nullptr, outs, seg_end, 3, out_dtype, flags);
 }
 
 b2a_status b2a_exchange_create(b2a_ctx* ctx, int world, int rank, int batch, int num_heads, int num_kv_heads,

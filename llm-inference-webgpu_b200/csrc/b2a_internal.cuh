@@ -46,7 +46,7 @@ struct b2a_ctx {
 namespace b2a {
 // Kernel kinds reported by b2a_timing_read.
 enum KernelKind { K_ATTN_SIMT = 0, K_ATTN_MMA, K_COMBINE, K_ROPE_APPEND, K_WRITE_AT, K_GROUPED, K_PREFILL_TC,
-                  K_PREFILL_PAIR, K_NUM_KINDS };
+                  K_PREFILL_PAIR, K_LINEAR, K_NUM_KINDS };
 extern const char* const kKernelNames[K_NUM_KINDS];
 
 // Brackets one launch with events on the context's stream while timing is on.
@@ -160,6 +160,26 @@ struct AttnParams {
   int x_world, x_rank, x_rows;
 };
 
+// Projection with int8 weights (k_linear.cu): out[t][r] = residual[t][r] +
+// scale[r] * sum_c w[r][c] x[t][c] + bias[r]. Output rows are split into up to
+// three segments (q, k, v of a fused QKV weight): rows [seg_end[s-1], seg_end[s])
+// go to out[s] as [tokens][rows of the segment].
+struct LinearParams {
+  const int8_t* w;            // [rows][cols], cols a multiple of 16
+  const void* scale;          // [rows]
+  int scale_dtype;
+  const void* bias;           // [rows] or null
+  int bias_dtype;
+  const void* x;              // [tokens][cols]
+  int x_dtype;
+  int rows, cols, tokens;
+  void* out[3];
+  int seg_end[3];
+  int nseg;
+  int out_dtype;
+  const void* residual;       // one segment only: [tokens][rows] in out_dtype, or null
+};
+
 struct CombineParams {
   const float* partial;       // chunked: [rows][nchunks][D+4]; cross-rank: [nchunks][rows][D+4]
   int64_t rows;
@@ -195,6 +215,7 @@ bool prefill_tc_supported(const AttnParams& p);
 cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cudaStream_t st);
 bool prefill_pair_supported(const AttnParams& p);
 cudaError_t launch_prefill_pair(const AttnParams& p, void* out, int out_dtype, cudaStream_t st);
+cudaError_t launch_linear_int8(const LinearParams& p, cudaStream_t st);
 cudaError_t launch_grouped_generic(const float* q, const float* k, const float* v, float* out, int seq,
                                    int past, int heads, int kv_heads, int head_dim, cudaStream_t st);
 

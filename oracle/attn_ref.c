@@ -520,3 +520,47 @@ int or_batched_decode_f16(const float* q, size_t q_stride, const uint16_t* kcach
   }
   return used;
 }
+
+/* ------------------------------------------------------------------ projections */
+
+/* src/core/quantize.js:25-27: round half away from zero (C's round). */
+void or_quantize_int8_per_channel(const float* w, int rows, int cols, int8_t* codes, float* scales) {
+  for (int r = 0; r < rows; r++) {
+    const float* row = w + (size_t)r * cols;
+    double peak = 0.0;
+    for (int c = 0; c < cols; c++) {
+      const double m = fabs((double)row[c]);
+      if (m > peak) peak = m;
+    }
+    const double scale = peak / 127.0;            /* a JS number: f64 */
+    scales[r] = (float)scale;                     /* Float32Array store */
+    int8_t* out = codes + (size_t)r * cols;
+    if (scale == 0.0) {
+      memset(out, 0, (size_t)cols);
+      continue;
+    }
+    const double inverse = 1.0 / scale;
+    for (int c = 0; c < cols; c++) {
+      double level = round((double)row[c] * inverse);
+      if (level > 127.0) level = 127.0;
+      if (level < -127.0) level = -127.0;
+      out[c] = (int8_t)level;
+    }
+  }
+}
+
+void or_dequantize_int8_per_channel(const int8_t* codes, const float* scales, int rows, int cols, float* out) {
+  for (int r = 0; r < rows; r++) {
+    const double s = (double)scales[r];
+    for (int c = 0; c < cols; c++) out[(size_t)r * cols + c] = (float)((double)codes[(size_t)r * cols + c] * s);
+  }
+}
+
+void or_matvec(const float* w, const float* x, int rows, int cols, const float* bias, float* out) {
+  for (int r = 0; r < rows; r++) {
+    double acc = bias ? (double)bias[r] : 0.0;
+    const float* row = w + (size_t)r * cols;
+    for (int c = 0; c < cols; c++) acc += (double)row[c] * (double)x[c];
+    out[r] = (float)acc;
+  }
+}

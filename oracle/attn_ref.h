@@ -130,6 +130,17 @@ int or_batched_decode_f16(const float* q, size_t q_stride, const uint16_t* kcach
                           int batch, int cap, int num_heads, int num_kv_heads, int head_dim,
                           float* out, size_t out_stride, int threads);
 
+
+/* ---- projections (the layer's neighbours of attention) ---------------------- */
+/* quantize.js:36-58: symmetric int8 per output row; scale = peak/127 stored as
+ * f32, codes = roundHalfAwayFromZero(w / scale) (the division by the f64 scale)
+ * clamped to [-127, 127]; an all-zero row gets scale 0 and zero codes. */
+void or_quantize_int8_per_channel(const float* w, int rows, int cols, int8_t* codes, float* scales);
+/* quantize.js:60-67: codes * scale, stored f32. */
+void or_dequantize_int8_per_channel(const int8_t* codes, const float* scales, int rows, int cols, float* out);
+/* ops.js:33-41: out[r] = bias[r] + sum_c W[r][c] x[c], f64 accumulation, f32 store. */
+void or_matvec(const float* w, const float* x, int rows, int cols, const float* bias, float* out);
+
 #ifdef __cplusplus
 }
 #endif

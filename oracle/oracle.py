@@ -90,6 +90,13 @@ def lib():
         L.or_batched_decode_f16.argtypes = [_f32p, ctypes.c_size_t, _u16p, _u16p, ctypes.c_size_t, _i32p,
                                             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             _f32p, ctypes.c_size_t, ctypes.c_int]
+        _i8p = ctypes.POINTER(ctypes.c_int8)
+        L.or_quantize_int8_per_channel.restype = None
+        L.or_quantize_int8_per_channel.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, _i8p, _f32p]
+        L.or_dequantize_int8_per_channel.restype = None
+        L.or_dequantize_int8_per_channel.argtypes = [_i8p, _f32p, ctypes.c_int, ctypes.c_int, _f32p]
+        L.or_matvec.restype = None
+        L.or_matvec.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
     return _lib
 
 
@@ -351,6 +358,47 @@ class OracleKVCache:
 
 
 # ---- generators ---------------------------------------------------------------------
+
+def quantize_int8(w, rows: int, cols: int):
+    """quantizeInt8PerChannel (src/core/quantize.js:36-58): (codes int8 [rows, cols], scales f32 [rows])."""
+    w = np.ascontiguousarray(f32(w).reshape(-1))
+    codes = np.zeros(rows * cols, np.int8)
+    scales = np.zeros(rows, np.float32)
+    lib().or_quantize_int8_per_channel(_p(w, ctypes.c_float), rows, cols, _p(codes, ctypes.c_int8),
+                                       _p(scales, ctypes.c_float))
+    return codes.reshape(rows, cols), scales
+
+
+def dequantize_int8(codes, scales, rows: int, cols: int) -> np.ndarray:
+    """dequantizeInt8PerChannel (src/core/quantize.js:60-67)."""
+    codes = np.ascontiguousarray(codes, np.int8).reshape(-1)
+    scales = np.ascontiguousarray(f32(scales))
+    out = np.zeros(rows * cols, np.float32)
+    lib().or_dequantize_int8_per_channel(_p(codes, ctypes.c_int8), _p(scales, ctypes.c_float), rows, cols,
+                                         _p(out, ctypes.c_float))
+    return out.reshape(rows, cols)
+
+
+def matvec(w, x, rows: int, cols: int, bias=None) -> np.ndarray:
+    """matVec (src/core/ops.js:33-41): f64 accumulation, f32 result."""
+    w = np.ascontiguousarray(f32(w).reshape(-1))
+    x = np.ascontiguousarray(f32(x).reshape(-1))
+    out = np.zeros(rows, np.float32)
+    b = None if bias is None else np.ascontiguousarray(f32(bias).reshape(-1))
+    lib().or_matvec(_p(w, ctypes.c_float), _p(x, ctypes.c_float), rows, cols,
+                    None if b is None else _p(b, ctypes.c_float), _p(out, ctypes.c_float))
+    return out
+
+
+def quantize_test_rand(n: int, seed: int) -> np.ndarray:
+    """test/quantize.test.js:10-18: LCG s = s*1664525 + 1013904223 (mod 2^32), a = s/0xffffffff*2 - 1, f32."""
+    s = seed & 0xffffffff
+    out = np.empty(n, np.float32)
+    for i in range(n):
+        s = (s * 1664525 + 1013904223) & 0xffffffff
+        out[i] = np.float32(s / 0xffffffff * 2 - 1)
+    return out
+
 
 def random_array(n: int, seed: int) -> np.ndarray:
     """test/attention.test.js:60-69."""
