@@ -338,6 +338,8 @@ def run_ours(args) -> None:
         line["split_kv"] = bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args)
     if world == 1 and not args.no_prefill:
         line["prefill"] = bench_prefill(torch, b2a, ctx, stream, dev, pk, args)
+    if world == 1 and not args.no_layer:
+        line["layer"] = bench_layer(torch, b2a, ctx, stream, dev, args)
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, used, sample = cpu_decode_sample(lengths, target_s=args.cpu_seconds)
         # the reference itself is single-threaded JavaScript: the same restatement on one thread beside it
@@ -478,6 +480,80 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
                        if world > 1 else "none (b2a_attention_decode: chunks merged inside the kernel)"}}
 
 
+def bench_layer(torch, b2a, ctx, stream, dev, args) -> dict:
+    """SURVEY 8(f)1, the attention block's neighbours: one decode step of one Qwen2.5 layer's
+    attention block through the library - fused int8 q/k/v projection (bias, f16 row scales),
+    RoPE + append + attention over the cache, int8 o_proj with the residual add - replayed from a
+    CUDA graph. Two shapes: BASELINE config 4 (one sequence, ~128 cached positions, the
+    generation loop's per-layer step) and config 3 (64 sequences, lengths U{256..4096})."""
+    hidden, rows = H * D, H * D + 2 * KVH * D
+    g = torch.Generator(device=dev)
+    g.manual_seed(31)
+
+    def codes(r, c):
+        return torch.randint(-127, 128, (r, c), generator=g, device=dev, dtype=torch.int8)
+
+    with torch.cuda.stream(stream):
+        wqkv, wo = codes(rows, hidden), codes(hidden, hidden)
+        sqkv = (torch.rand(rows, generator=g, device=dev) * 1e-3).half()
+        so = (torch.rand(hidden, generator=g, device=dev) * 1e-3).half()
+        bias = torch.randn(rows, generator=g, device=dev) * 0.1
+    res = {"metric": "attention-block decode step", "unit": "us/layer", "weights": "int8 per-row, f16 scales",
+           "kernels_per_layer": 3, "shapes": {}}
+    weight_bytes = rows * hidden + hidden * hidden
+    for name, batch, lens in (("config4-generation", 1, [128]),
+                              ("config3-batch64", SEQS, [int(x) for x in config3_lengths(0)])):
+        with torch.cuda.stream(stream):
+            cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(1, KVH, D, H), max(lens) + 1, batch=batch, dtype="f16")
+            rope = b2a.RopeTable(ctx, D, THETA, max(lens) + 1)
+            cache.setLengths(lens)
+            x = torch.randn(batch, hidden, generator=g, device=dev)
+            q = torch.empty(batch, H * D, device=dev, dtype=torch.float16)
+            kn = torch.empty(batch, KVH * D, device=dev, dtype=torch.float16)
+            vn = torch.empty(batch, KVH * D, device=dev, dtype=torch.float16)
+            att = torch.empty(batch, H * D, device=dev)
+            xo = torch.empty(batch, hidden, device=dev)
+
+            def step():
+                b2a.qkvInt8(ctx, wqkv, sqkv, bias, x, q, kn, vn, hidden, H * D, KVH * D, batch)
+                b2a.attentionDecode(ctx, cache, rope, 0, q.view(batch, 1, H, D), kn.view(batch, 1, KVH, D),
+                                    vn.view(batch, 1, KVH, D), att.view(batch, 1, H, D), H)
+                b2a.linearInt8(ctx, wo, so, None, att, xo, hidden, hidden, batch, residual=x)
+            for _ in range(5):
+                step()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        n = 200
+        with torch.cuda.stream(stream):
+            for _ in range(5):
+                graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) / n * 1e3
+        # per-kernel device times from eager steps with the library's event timing
+        with torch.cuda.stream(stream):
+            ctx.enable_timing(True)
+            for _ in range(20):
+                step()
+            kt = ctx.read_timing()
+            ctx.enable_timing(False)
+        kv_bytes = sum(lens) * KVH * D * 2 * 2
+        res["shapes"][name] = {"batch": batch, "kv_positions": int(sum(lens)), "us_per_layer": round(us, 2),
+                               "bytes_per_layer": int(weight_bytes + kv_bytes),
+                               "gb_s": round((weight_bytes + kv_bytes) / (us * 1e-6) / 1e9, 1),
+                               "kernels_us": {k: round(v[1] / v[0] * 1e3, 2) for k, v in kt.items()}}
+        del graph
+        cache.close()
+        rope.close()
+    return res
+
+
 def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
     """causal prefill, bf16 Q/K/V, RoPE at 0..S-1, fused append, bf16 out."""
     res = {"metric": "prefill-attn TFLOPS", "unit": "TFLOPS", "dtype": "bf16", "sweep": {}}
@@ -601,6 +677,7 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-splitkv", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-layer", action="store_true", help="skip the attention-block (projections) measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192, 16384])
     ap.add_argument("--prefill-cache", choices=["f16", "bf16"], default="f16",

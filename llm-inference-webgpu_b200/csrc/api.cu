@@ -231,6 +231,10 @@ b2a_status check_cache_shape(const b2a_kvcache* c, const b2a_rope* rope, int num
   return B2A_OK;
 }
 
+// The shortest split-KV chunk, in 64-position tiles: below it the per-chunk
+// merge costs more than the parallelism gains.
+constexpr int64_t kMinChunkTiles = 4;
+
 AttnParams base_params(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope) {
   AttnParams p{};
   p.kc = c->d_k;
@@ -301,20 +305,25 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
       }
       const int64_t tiles = (std::max(max_nk, 1) + 63) / 64;
       const int64_t n = std::min<int64_t>(per_group, attn_mma_max_fused_chunks());
-      p.chunk = static_cast<int>(64 * ((tiles + n - 1) / n));
+      p.chunk = static_cast<int>(64 * std::max<int64_t>(kMinChunkTiles, (tiles + n - 1) / n));
       items = attn_mma_items(p, c->len.data());
     } else if (per_group >= 2 && max_nk > 0 &&
                static_cast<int64_t>(min_nk) * 8 >= static_cast<int64_t>(max_nk) * 7) {
       const int64_t tiles = (max_nk + 63) / 64;
-      p.chunk = static_cast<int>(64 * ((tiles + per_group - 1) / per_group));
+      p.chunk = static_cast<int>(64 * std::max<int64_t>(kMinChunkTiles, (tiles + per_group - 1) / per_group));
       items = attn_mma_items(p, c->len.data());
     } else {
-      const int64_t want = 8LL * ctx->sm_count;
-      for (int chunk : {4096, 2048, 1024, 512, 256}) {
-        p.chunk = chunk;
-        items = attn_mma_items(p, c->len.data());
-        if (items >= want) break;
+      // about two waves of the resident CTAs over all the key tiles, in chunks
+      // of 4..64 tiles: short work keeps whole groups in one chunk (no merge),
+      // a long multi-layer batch gets whole 4096-position chunks
+      int64_t total_tiles = 0;
+      for (int b = 0; b < p.batch; b++) {
+        total_tiles += (static_cast<int64_t>(c->len[p.seq_begin + b]) + p.horizon_extra + 63) / 64;
       }
+      total_tiles *= static_cast<int64_t>(p.num_layers) * p.kv_heads;
+      const int64_t per_item = (total_tiles + 2 * slots - 1) / (2 * slots);
+      p.chunk = static_cast<int>(64 * std::min<int64_t>(64, std::max<int64_t>(kMinChunkTiles, per_item)));
+      items = attn_mma_items(p, c->len.data());
     }
   }
   p.nchunks = max_keys > 0 ? (max_keys + p.chunk - 1) / p.chunk : 1;

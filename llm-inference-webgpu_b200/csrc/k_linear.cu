@@ -7,11 +7,13 @@
 // Tensor cores (mma.sync m16n8k16, f16 in, f32 accumulate): an int8 code is
 // exact in f16, so A = the codes of 16 rows and the row scale is applied in the
 // epilogue; B = the activations, split into an f16 high part and an f16
-// residual (two MMAs) so the product keeps ~f32 precision. A CTA of four warps
-// owns 64 rows x 32 tokens and stages its weight rows (int8) and the tokens'
-// activations (as given: f32, f16 or bf16) in shared memory for up to 1024
-// columns at a time with asynchronous 16-byte copies, all in flight at once;
-// the activations are split while the MMA fragments are built. Weight reads dominate the bytes
+// residual (two MMAs) so the product keeps ~f32 precision. A CTA of eight warps
+// owns 16 rows x 32 tokens (so a 1152-row projection spreads over 72 CTAs even
+// for one token) and stages its weight rows (int8) and the tokens' activations
+// (as given: f32, f16 or bf16) in shared memory for up to 1024 columns at a
+// time with asynchronous 16-byte copies, all in flight at once. The eight warps
+// split the columns, MMA only the 8-token tiles that hold tokens, and add their
+// partial sums through shared memory. Weight reads dominate the bytes
 // (HBM-bound for large matrices; latency-bound at the Qwen2.5-0.5B sizes).
 #include <cuda_fp16.h>
 
@@ -22,12 +24,14 @@ namespace b2a {
 
 namespace {
 
-constexpr int kRowsPerCta = 64;
+constexpr int kRowsPerCta = 16;
 constexpr int kTokPerCta = 32;
 constexpr int kMaxKc = 1024;                    // columns staged per pass
 constexpr int kWPitch = kMaxKc + 16;            // bytes per staged weight row (bank spread)
 constexpr int kXPitch = kMaxKc * 4 + 16;        // bytes per staged token row (f32 or 16-bit)
-constexpr int kSmem = kRowsPerCta * kWPitch + kTokPerCta * kXPitch;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kSmem = kRowsPerCta * kWPitch + kTokPerCta * kXPitch + kWarps * kRowsPerCta * kTokPerCta * 4;
 
 // 16-byte asynchronous copy global -> shared; src_bytes 0 fills zeros
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
@@ -56,17 +60,27 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
 
 }  // namespace
 
-__global__ void __launch_bounds__(128) k_linear_int8(LinearParams p) {
+__global__ void __launch_bounds__(kThreads) k_linear_int8(LinearParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* ws = smem;                                   // [64][kWPitch] int8 codes
-  unsigned char* xs = smem + kRowsPerCta * kWPitch;           // [32][kXPitch] activations as given
+  unsigned char* ws = smem;                                                 // [16][kWPitch] int8 codes
+  unsigned char* xs = smem + kRowsPerCta * kWPitch;                         // [32][kXPitch] activations as given
+  float* part = reinterpret_cast<float*>(xs + kTokPerCta * kXPitch);       // [8 warps][16 rows][32 tokens]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;
   const int r0 = blockIdx.x * kRowsPerCta;
   const int t0 = blockIdx.y * kTokPerCta;
   const int nrows = min(kRowsPerCta, p.rows - r0);
   const int ntok = min(kTokPerCta, p.tokens - t0);
+  const int ntiles = (ntok + 7) / 8;             // 8-token MMA tiles that hold tokens
   const int esz = p.x_dtype == DT_F32 ? 4 : 2;
+
+  // the rows' scales and biases, loaded while the tiles stream in
+  __shared__ float rsc[kRowsPerCta], rbi[kRowsPerCta];
+  if (tid < kRowsPerCta) {
+    const int r = r0 + tid;
+    rsc[tid] = tid < nrows ? ld_as_f32(p.scale, r, p.scale_dtype) : 0.f;
+    rbi[tid] = (tid < nrows && p.bias) ? ld_as_f32(p.bias, r, p.bias_dtype) : 0.f;
+  }
 
   float acc[4][4];
 #pragma unroll
@@ -78,31 +92,35 @@ __global__ void __launch_bounds__(128) k_linear_int8(LinearParams p) {
     const int kc = min(kMaxKc, p.cols - c0);   // a multiple of 16
     if (c0 > 0) __syncthreads();                 // the previous pass is done with the tiles
     const int wvec = kc / 16;
-    for (int i = tid; i < kRowsPerCta * wvec; i += 128) {
+    for (int i = tid; i < kRowsPerCta * wvec; i += kThreads) {
       const int r = i / wvec, v = i % wvec;
       const bool in = r < nrows;
       cp_async16(ws + r * kWPitch + 16 * v, p.w + (in ? static_cast<int64_t>(r0 + r) * p.cols + c0 + 16 * v : 0),
                  in ? 16 : 0);
     }
+    // only the tokens that exist (the rest of a tile reads stale shared
+    // memory, which only reaches that tile's unused output columns)
     const int xvec = kc * esz / 16;
-    for (int i = tid; i < kTokPerCta * xvec; i += 128) {
+    for (int i = tid; i < ntok * xvec; i += kThreads) {
       const int t = i / xvec, v = i % xvec;
-      const bool in = t < ntok;
-      const unsigned char* src = static_cast<const unsigned char*>(p.x) +
-                                 (in ? (static_cast<int64_t>(t0 + t) * p.cols + c0) * esz + 16 * v : 0);
-      cp_async16(xs + t * kXPitch + 16 * v, src, in ? 16 : 0);
+      cp_async16(xs + t * kXPitch + 16 * v,
+                 static_cast<const unsigned char*>(p.x) + (static_cast<int64_t>(t0 + t) * p.cols + c0) * esz + 16 * v, 16);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    const unsigned char* wr0 = ws + (warp * 16 + gq) * kWPitch;
+    const unsigned char* wr0 = ws + gq * kWPitch;
     const unsigned char* wr1 = wr0 + 8 * kWPitch;
-    for (int k = 0; k < kc; k += 16) {
+    // this warp's eighth of the staged columns, in 16-column steps
+    const int steps = kc / 16;
+    const int k_begin = 16 * ((steps * warp) / kWarps), k_end = 16 * ((steps * (warp + 1)) / kWarps);
+    for (int k = k_begin; k < k_end; k += 16) {
       const uint32_t a0 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(wr0 + k + 2 * tq));
       const uint32_t a1 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(wr1 + k + 2 * tq));
       const uint32_t a2 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(wr0 + k + 8 + 2 * tq));
       const uint32_t a3 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(wr1 + k + 8 + 2 * tq));
 #pragma unroll
       for (int n = 0; n < 4; n++) {
+        if (n >= ntiles) break;
         const unsigned char* xr = xs + (8 * n + gq) * kXPitch;
         float v[4];   // x[t][k+2tq], x[t][k+2tq+1], x[t][k+8+2tq], x[t][k+9+2tq]
         if (esz == 4) {
@@ -127,30 +145,45 @@ __global__ void __launch_bounds__(128) k_linear_int8(LinearParams p) {
     }
   }
 
-  // epilogue: C fragment (row gq / gq+8 of the warp's 16, tokens 2tq, 2tq+1 of each n tile)
+  // the warps' partial sums: C fragment (rows gq / gq+8, tokens 2tq, 2tq+1 of
+  // each tile) -> part[warp][row][token], then a thread per (row, token)
 #pragma unroll
-  for (int hr = 0; hr < 2; hr++) {
-    const int r = r0 + warp * 16 + gq + 8 * hr;
-    if (r >= p.rows) continue;
-    const float sc = ld_as_f32(p.scale, r, p.scale_dtype);
-    const float bi = p.bias ? ld_as_f32(p.bias, r, p.bias_dtype) : 0.f;
+  for (int n = 0; n < 4; n++) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int row = gq + 8 * (e >> 1), tok = 8 * n + 2 * tq + (e & 1);
+      part[(warp * kRowsPerCta + row) * kTokPerCta + tok] = acc[n][e];
+    }
+  }
+  __syncthreads();
+  // two (row, token) outputs per thread: every global load first, then the math
+  constexpr int kPer = kRowsPerCta * kTokPerCta / kThreads;
+  float res[kPer];
+#pragma unroll
+  for (int u = 0; u < kPer; u++) {
+    const int i = tid + kThreads * u, row = i / kTokPerCta, tok = i % kTokPerCta;
+    res[u] = 0.f;
+    if (p.residual && row < nrows && tok < ntok) {
+      const int r = r0 + row;
+      const int seg_rows = p.seg_end[0];   // the residual comes with one segment
+      res[u] = ld_as_f32(p.residual, static_cast<int64_t>(t0 + tok) * seg_rows + r, p.out_dtype);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kPer; u++) {
+    const int i = tid + kThreads * u, row = i / kTokPerCta, tok = i % kTokPerCta;
+    const int r = r0 + row, t = t0 + tok;
+    float sum = 0.f;
+#pragma unroll
+    for (int w8 = 0; w8 < kWarps; w8++) sum += part[(w8 * kRowsPerCta + row) * kTokPerCta + tok];
+    if (row >= nrows || tok >= ntok) continue;
     // the output segment of row r (selects, not indexing, keep the parameters in registers)
     const int seg = (p.nseg > 1 && r >= p.seg_end[0]) + (p.nseg > 2 && r >= p.seg_end[1]);
     const int seg_begin = seg == 0 ? 0 : (seg == 1 ? p.seg_end[0] : p.seg_end[1]);
     const int seg_rows = (seg == 0 ? p.seg_end[0] : (seg == 1 ? p.seg_end[1] : p.seg_end[2])) - seg_begin;
     void* out = seg == 0 ? p.out[0] : (seg == 1 ? p.out[1] : p.out[2]);
-#pragma unroll
-    for (int n = 0; n < 4; n++) {
-#pragma unroll
-      for (int e = 0; e < 2; e++) {
-        const int t = t0 + 8 * n + 2 * tq + e;
-        if (t >= p.tokens) continue;
-        const int64_t o = static_cast<int64_t>(t) * seg_rows + (r - seg_begin);
-        float v = fmaf(acc[n][2 * hr + e], sc, bi);
-        if (p.residual) v += ld_as_f32(p.residual, o, p.out_dtype);
-        st_from_f32(out, o, p.out_dtype, v);
-      }
-    }
+    const int64_t o = static_cast<int64_t>(t) * seg_rows + (r - seg_begin);
+    st_from_f32(out, o, p.out_dtype, fmaf(sum, rsc[row], rbi[row]) + res[u]);
   }
 }
 
@@ -165,7 +198,7 @@ cudaError_t launch_linear_int8(const LinearParams& p, cudaStream_t st) {
     attr[dev] = true;
   }
   const dim3 grid((p.rows + kRowsPerCta - 1) / kRowsPerCta, (p.tokens + kTokPerCta - 1) / kTokPerCta);
-  k_linear_int8<<<grid, 128, kSmem, st>>>(p);
+  k_linear_int8<<<grid, kThreads, kSmem, st>>>(p);
   return cudaGetLastError();
 }
 
