@@ -222,6 +222,13 @@ __global__ void __launch_bounds__(kThreads, 3)
   uint64_t* empty = full + kStages;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Programmatic dependent launch: the next kernel in the stream may begin its
+  // prologue once every CTA of this grid is resident, and this grid's own
+  // reads of anything an earlier kernel writes (lengths, q, k/v, the cache)
+  // wait for that kernel to finish. With lengths passed by value the work-item
+  // lookup below runs before the wait.
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (p.n_len_inline == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- which work item: items are numbered sequence-major, each sequence
   // contributing num_layers * kv_heads * chunks(b) of them.
@@ -266,6 +273,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (p.n_len_inline != 0) asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
   const int b = ms.item[0];
   if (b < 0) return;   // grid larger than the item count (cannot happen with the host's count)
@@ -766,19 +774,25 @@ cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st)
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr_f16[64] = {}, attr_bf16[64] = {};
-  if (p.cache_dtype == DT_F16) {
-    if (dev < 64 && !attr_f16[dev]) {
-      cudaFuncSetAttribute(k_decode_mma<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
-      attr_f16[dev] = true;
-    }
-    k_decode_mma<__half><<<static_cast<unsigned>(items), kThreads, kSmemTotal, st>>>(*mk, *mv, p);
-  } else {
-    if (dev < 64 && !attr_bf16[dev]) {
-      cudaFuncSetAttribute(k_decode_mma<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
-      attr_bf16[dev] = true;
-    }
-    k_decode_mma<__nv_bfloat16><<<static_cast<unsigned>(items), kThreads, kSmemTotal, st>>>(*mk, *mv, p);
+  const bool f16 = p.cache_dtype == DT_F16;
+  void (*kern)(const CUtensorMap, const CUtensorMap, AttnParams) = f16 ? k_decode_mma<__half> : k_decode_mma<__nv_bfloat16>;
+  bool* attr = f16 ? attr_f16 : attr_bf16;
+  if (dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+    attr[dev] = true;
   }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(items));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemTotal;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *mk, *mv, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -74,6 +74,12 @@ __global__ void __launch_bounds__(kThreads) k_linear_int8(LinearParams p) {
   const int ntiles = (ntok + 7) / 8;             // 8-token MMA tiles that hold tokens
   const int esz = p.x_dtype == DT_F32 ? 4 : 2;
 
+  // Programmatic dependent launch: the next kernel may start its prologue
+  // once every CTA of this grid is resident; this grid reads nothing from
+  // global memory before the kernel ahead of it (which may have written the
+  // weights, scales or activations) has finished.
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // the rows' scales and biases, loaded while the tiles stream in
   __shared__ float rsc[kRowsPerCta], rbi[kRowsPerCta];
   if (tid < kRowsPerCta) {
@@ -198,8 +204,17 @@ cudaError_t launch_linear_int8(const LinearParams& p, cudaStream_t st) {
     attr[dev] = true;
   }
   const dim3 grid((p.rows + kRowsPerCta - 1) / kRowsPerCta, (p.tokens + kTokPerCta - 1) / kTokPerCta);
-  k_linear_int8<<<grid, kThreads, kSmem, st>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_linear_int8, p);
 }
 
 }  // namespace b2a
