@@ -285,6 +285,77 @@ b2a_status b2a_attention_decode_split(b2a_ctx* ctx, b2a_kvcache* cache, const b2
                                       b2a_dtype in_dtype, const int32_t* q_positions, b2a_exchange* ex,
                                       void* out, b2a_dtype out_dtype, int flags);
 
+/* ---- the Qwen2 decoder around the attention path ------------------------------
+ * ReferenceModel.forward / generate (src/cpu/model.js:55-187) and
+ * GpuModel.forward (src/gpu/model.js:227-400) over int8 weights with one scale
+ * per output row. One layer, in the order it runs:
+ *   h = x + O(attn(RoPE(Q(rms(x))), RoPE(K(rms(x))), V(rms(x))))
+ *   y = h + Down(silu(Gate(rms(h))) * Up(rms(h)))
+ * then the final RMSNorm and the tied output projection (the embedding rows).
+ * A model owns its weights on the device, a one-sequence f16 KV cache of
+ * `capacity` positions, the RoPE table (max_positions entries) and its
+ * activations; q/k/v reach attention as f16, everything else is f32. */
+typedef struct b2a_model b2a_model;
+typedef struct b2a_model_config {
+  int hidden_size;         /* num_heads * 64                                   */
+  int intermediate_size;   /* a multiple of 16                                 */
+  int num_layers;
+  int num_heads;
+  int num_kv_heads;        /* divides num_heads, at most 8 query heads each    */
+  int vocab_size;
+  int max_positions;       /* max_position_embeddings: RoPE table entries      */
+  double rope_theta;
+  double rms_norm_eps;
+  b2a_dtype scale_dtype;   /* dtype of every per-row scale: B2A_F16 or B2A_F32 */
+} b2a_model_config;
+/* One decoder layer's tensors (row-major, [out_features][in_features]). */
+typedef struct b2a_layer_weights {
+  const float* input_norm;       /* [hidden]                                          */
+  const float* post_attn_norm;   /* [hidden]                                          */
+  const int8_t* qkv;             /* [hidden + 2*kv_dim][hidden]: q rows, k rows, v rows */
+  const void* qkv_scales;        /* [hidden + 2*kv_dim] in scale_dtype                */
+  const float* qkv_bias;         /* [hidden + 2*kv_dim]                               */
+  const int8_t* o;               /* [hidden][hidden]                                  */
+  const void* o_scales;
+  const int8_t* gate;            /* [intermediate][hidden]                            */
+  const void* gate_scales;
+  const int8_t* up;              /* [intermediate][hidden]                            */
+  const void* up_scales;
+  const int8_t* down;            /* [hidden][intermediate]                            */
+  const void* down_scales;
+} b2a_layer_weights;
+b2a_status b2a_model_create(b2a_ctx* ctx, const b2a_model_config* cfg, int capacity, b2a_model** out);
+b2a_status b2a_model_destroy(b2a_model* model);
+/* Copies weights in from host (B2A_HOST) or device (B2A_DEVICE) memory. Every
+ * layer, the embedding and the final norm must be loaded before a forward. */
+b2a_status b2a_model_load_layer(b2a_model* model, int layer, const b2a_layer_weights* w, int flags);
+/* The tied embedding, codes [vocab][hidden] and scales [vocab]: the input
+ * lookup dequantizes one row per token, the output projection is the int8
+ * product with every row. */
+b2a_status b2a_model_load_embedding(b2a_model* model, const int8_t* codes, const void* scales, int flags);
+b2a_status b2a_model_load_final_norm(b2a_model* model, const float* weight, int flags);
+/* ReferenceModel.forward(tokenIds, {cache}): runs `seq` tokens at positions
+ * length..length+seq-1 of the model's cache, then commits them. logits
+ * ([vocab] f32, the last position's; may be NULL) and next_token (the first
+ * index of the largest logit; may be NULL) in the memory `flags` names, like
+ * tokens. Errors as the reference: B2A_EINVAL "forward: need at least one
+ * token", B2A_ERANGE for a token outside the vocabulary or a full cache. */
+b2a_status b2a_model_forward(b2a_model* model, const int32_t* tokens, int seq, float* logits, int32_t* next_token,
+                             int flags);
+/* ReferenceModel.generate(promptIds, {maxTokens, stopTokens}), greedy, from an
+ * empty cache: the prompt in one pass, then one pass per new token, each
+ * token chosen and fed back on the device. Host arrays: tokens_out and
+ * best_logits [max_tokens] (the chosen token's logit); *n_generated stops
+ * short of max_tokens after a stop token (which is included). */
+b2a_status b2a_model_generate(b2a_model* model, const int32_t* prompt, int n_prompt, int max_tokens,
+                              const int32_t* stop_tokens, int n_stop, int32_t* tokens_out, float* best_logits,
+                              int* n_generated);
+b2a_status b2a_model_reset(b2a_model* model);
+b2a_status b2a_model_length(const b2a_model* model, int* length);
+/* The model's KV cache (layers x kv heads x capacity, f16), for reading the
+ * present keys and values with b2a_kvcache_read. Owned by the model. */
+b2a_status b2a_model_cache(b2a_model* model, b2a_kvcache** cache);
+
 #ifdef __cplusplus
 }
 #endif

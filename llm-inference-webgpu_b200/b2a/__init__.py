@@ -10,4 +10,5 @@ from ._lib import B2AError, BusyError, RangeError, load, lib_path  # noqa: F401
 from .attention import (appendRope, attentionDecode, attentionPrefill, decodePartial, decodeSplit,  # noqa: F401
                         default_context, groupedAttention, kvHeadFor, linearInt8, lseCombine, qkvInt8,
                         quantizeInt8PerChannel, ropeFrequencies, ropeTables)
+from .model import Model, ModelConfig  # noqa: F401
 from .runtime import CacheConfig, Context, Exchange, GpuKVCache, RopeTable  # noqa: F401

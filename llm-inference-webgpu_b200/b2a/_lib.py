@@ -64,6 +64,16 @@ SIGNATURES = {
     "b2a_exchange_connect_local": (_i, [_vp, _i, _vp]),
     "b2a_exchange_destroy": (_i, [_vp]),
     "b2a_attention_decode_split": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
+    "b2a_model_create": (_i, [_vp, _vp, _i, _pp]),
+    "b2a_model_destroy": (_i, [_vp]),
+    "b2a_model_load_layer": (_i, [_vp, _i, _vp, _i]),
+    "b2a_model_load_embedding": (_i, [_vp, _vp, _vp, _i]),
+    "b2a_model_load_final_norm": (_i, [_vp, _vp, _i]),
+    "b2a_model_forward": (_i, [_vp, _vp, _i, _vp, _vp, _i]),
+    "b2a_model_generate": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp, _vp, _ip]),
+    "b2a_model_reset": (_i, [_vp]),
+    "b2a_model_length": (_i, [_vp, _ip]),
+    "b2a_model_cache": (_i, [_vp, _pp]),
 }
 EXCHANGE_HANDLE_BYTES = 64
 

@@ -43,7 +43,8 @@ b2a_status cuda_fail(cudaError_t e, const char* what) {
 
 const char* const kKernelNames[K_NUM_KINDS] = {"attention_simt", "attention_mma", "combine", "rope_append",
                                                "write_at", "grouped_generic", "prefill_tc",
-                                               "prefill_pair", "linear_int8"};
+                                               "prefill_pair", "linear_int8", "embed_int8", "rmsnorm",
+                                               "swiglu", "argmax"};
 
 namespace {
 cudaEvent_t take_event(b2a_ctx* ctx) {
@@ -200,6 +201,10 @@ b2a_status check_device_error(b2a_ctx* ctx) {
     cudaMemset(ctx->d_err, 0, sizeof(err));
     // a kernel that gave up may have left merge counters non-zero
     if (ctx->d_counters) cudaMemset(ctx->d_counters, 0, ctx->d_counters_bytes);
+    if (err == kErrBadToken) {
+      // src/cpu/model.js:203-205
+      return fail(B2A_ERANGE, "a token on the device is outside the vocabulary; results of that call are invalid");
+    }
     return fail(B2A_ETIMEDOUT, "a device-side wait gave up (error word 0x%x); results of that call are invalid", err);
   }
   return B2A_OK;
@@ -628,6 +633,21 @@ b2a_status linear_int8(b2a_ctx* ctx, const int8_t* codes, const void* scales, b2
 }
 
 }  // namespace
+
+namespace b2a {
+bool ctx_acquire(b2a_ctx* ctx) {
+  int expected = 0;
+  if (ctx == nullptr || !ctx->busy.compare_exchange_strong(expected, 1)) return false;
+  cudaSetDevice(ctx->device);
+  return true;
+}
+void ctx_release(b2a_ctx* ctx) { ctx->busy.store(0); }
+b2a_status busy_fail(b2a_ctx* ctx) {
+  if (ctx == nullptr) return fail(B2A_EINVAL, "null context");
+  return fail(B2A_EBUSY, "a call is already running on this context; wait for it first");
+}
+b2a_status stream_sync_check(b2a_ctx* ctx) { return d2h_sync(ctx, nullptr, nullptr, 0); }
+}  // namespace b2a
 
 extern "C" {
 
@@ -1189,6 +1209,35 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* ro
   return run_split_kv(ctx, c, p, max_keys, dout, static_cast<int>(out_dtype), 0);
 }
 
+}  // extern "C"
+
+namespace b2a {
+
+b2a_status attn_decode_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_heads,
+                              const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype, void* out,
+                              b2a_dtype out_dtype) {
+  int max_keys = 0;
+  for (int b = 0; b < c->batch; b++) max_keys = std::max(max_keys, c->len[b] + 1);
+  AttnParams p = base_params(ctx, c, rope);
+  p.seq_begin = 0;
+  p.batch = c->batch;
+  p.num_layers = 1;
+  p.layer_begin = layer;
+  p.tokens = 1;
+  p.heads = num_heads;
+  p.group = num_heads / c->kv_heads;
+  p.in_dtype = static_cast<int>(in_dtype);
+  p.q = q;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.horizon_extra = 1;
+  return run_split_kv(ctx, c, p, max_keys, out, static_cast<int>(out_dtype), 0);
+}
+
+}  // namespace b2a
+
+extern "C" {
+
 // ----------------------------------------------------------------- prefill --
 
 namespace {
@@ -1228,6 +1277,36 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* r
   const size_t q_bytes = static_cast<size_t>(count) * num_heads * c->head_dim * ies;
   const size_t kv_bytes = static_cast<size_t>(count) * c->kv_heads * c->head_dim * ies;
   const size_t out_bytes = static_cast<size_t>(count) * num_heads * c->head_dim * dtype_size(out_dtype);
+  void* dout = out;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int iq = st.add(q_bytes), ik = st.add(kv_bytes), iv = st.add(kv_bytes), io = st.add(out_bytes);
+    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, ik), k, kv_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iv), v, kv_bytes)) != B2A_OK) return s;
+    q = st.ptr(ctx, iq);
+    k = st.ptr(ctx, ik);
+    v = st.ptr(ctx, iv);
+    dout = st.ptr(ctx, io);
+  }
+  if ((s = attn_prefill_device(ctx, c, rope, layer, seq_idx, num_heads, q, k, v, in_dtype, count, dout, out_dtype)) !=
+      B2A_OK) {
+    return s;
+  }
+  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
+  return B2A_OK;
+}
+
+}  // extern "C"
+
+namespace b2a {
+
+b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx,
+                               int num_heads, const void* q, const void* k, const void* v, b2a_dtype in_dtype,
+                               int count, void* dout, b2a_dtype out_dtype) {
+  b2a_status s;
+  const int past = c->len[seq_idx];
   AttnParams p = base_params(ctx, c, rope);
   p.seq_begin = seq_idx;
   p.batch = 1;
@@ -1241,19 +1320,6 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* r
   p.k_new = k;
   p.v_new = v;
   p.horizon_extra = 1;
-  void* dout = out;
-  if (flags == B2A_HOST) {
-    Stage st;
-    int iq = st.add(q_bytes), ik = st.add(kv_bytes), iv = st.add(kv_bytes), io = st.add(out_bytes);
-    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
-    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
-    if ((s = h2d(ctx, st.ptr(ctx, ik), k, kv_bytes)) != B2A_OK) return s;
-    if ((s = h2d(ctx, st.ptr(ctx, iv), v, kv_bytes)) != B2A_OK) return s;
-    p.q = st.ptr(ctx, iq);
-    p.k_new = st.ptr(ctx, ik);
-    p.v_new = st.ptr(ctx, iv);
-    dout = st.ptr(ctx, io);
-  }
   // RoPE(K) + append first (src/cpu/model.js:116 writes before attending), then
   // causal attention over past+count with RoPE(Q) fused into the Q load.
   cudaError_t e;
@@ -1285,9 +1351,12 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* r
   } else if ((s = run_split_kv(ctx, c, p, past + count, dout, static_cast<int>(out_dtype), 0)) != B2A_OK) {
     return s;
   }
-  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
   return B2A_OK;
 }
+
+}  // namespace b2a
+
+extern "C" {
 
 // ----------------------------------------------------- groupedAttention drop-in --
 

@@ -46,7 +46,7 @@ struct b2a_ctx {
 namespace b2a {
 // Kernel kinds reported by b2a_timing_read.
 enum KernelKind { K_ATTN_SIMT = 0, K_ATTN_MMA, K_COMBINE, K_ROPE_APPEND, K_WRITE_AT, K_GROUPED, K_PREFILL_TC,
-                  K_PREFILL_PAIR, K_LINEAR, K_NUM_KINDS };
+                  K_PREFILL_PAIR, K_LINEAR, K_EMBED, K_RMSNORM, K_SWIGLU, K_ARGMAX, K_NUM_KINDS };
 extern const char* const kKernelNames[K_NUM_KINDS];
 
 // Brackets one launch with events on the context's stream while timing is on.
@@ -218,5 +218,37 @@ cudaError_t launch_prefill_pair(const AttnParams& p, void* out, int out_dtype, c
 cudaError_t launch_linear_int8(const LinearParams& p, cudaStream_t st);
 cudaError_t launch_grouped_generic(const float* q, const float* k, const float* v, float* out, int seq,
                                    int past, int heads, int kv_heads, int head_dim, cudaStream_t st);
+
+// ---- the decoder around attention (k_model.cu, model.cu) -----------------------
+constexpr int kErrBadToken = 16;   // error word: a device token outside the vocabulary
+// x[t][:] = codes[tokens[t]][:] * scales[tokens[t]] (f32)
+cudaError_t launch_embed_int8(const int32_t* tokens, int count, const int8_t* codes, const void* scales,
+                              int scale_dtype, int hidden, int vocab, float* x, int32_t* err, cudaStream_t st);
+// out[r][:] = RMSNorm(x[r][:]) * w, rows of `hidden` f32
+cudaError_t launch_rmsnorm(const float* x, const float* w, double eps, int rows, int hidden, float* out,
+                           cudaStream_t st);
+// gate[i] = silu(gate[i]) * up[i]
+cudaError_t launch_swiglu(float* gate, const float* up, int64_t n, cudaStream_t st);
+// the first index of the largest of logits[0..n) -> *token (and its value ->
+// *value); scratch: kArgmaxScratchBytes, its counter word zeroed once at
+// allocation (the kernel leaves it zeroed)
+constexpr size_t kArgmaxScratchBytes = 8192;
+cudaError_t launch_argmax(const float* logits, int n, int32_t* token, float* value, void* scratch,
+                          cudaStream_t st);
+
+// Device-pointer bodies of b2a_attention_decode (one layer) and
+// b2a_attention_prefill: the caller validated the shapes and holds the context.
+b2a_status attn_decode_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_heads,
+                              const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype, void* out,
+                              b2a_dtype out_dtype);
+b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx,
+                               int num_heads, const void* q, const void* k, const void* v, b2a_dtype in_dtype,
+                               int count, void* out, b2a_dtype out_dtype);
+// the context's busy flag (one call at a time, src/gpu/model.js:231)
+bool ctx_acquire(b2a_ctx* ctx);
+void ctx_release(b2a_ctx* ctx);
+b2a_status busy_fail(b2a_ctx* ctx);
+// waits for the stream, then reads and clears the device error word
+b2a_status stream_sync_check(b2a_ctx* ctx);
 
 }  // namespace b2a

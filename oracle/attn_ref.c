@@ -564,3 +564,217 @@ void or_matvec(const float* w, const float* x, int rows, int cols, const float* 
     out[r] = (float)acc;
   }
 }
+
+/* ------------------------------------------------ the decoder around attention -- */
+
+/* src/core/ops.js:17-24: f64 sum of squares, scale = 1/sqrt(ss/n + eps), out = x*scale*w. */
+void or_rmsnorm(const float* x, const float* weight, double eps, int n, float* out) {
+  double sum_squares = 0.0;
+  for (int i = 0; i < n; i++) sum_squares += (double)x[i] * (double)x[i];
+  const double scale = 1.0 / sqrt(sum_squares / n + eps);
+  for (int i = 0; i < n; i++) out[i] = (float)((double)x[i] * scale * (double)weight[i]);
+}
+
+/* src/core/ops.js:81-83 */
+double or_silu(double x) { return x / (1.0 + exp(-x)); }
+
+/* src/core/ops.js:88-91 */
+void or_swiglu_inplace(float* gate, const float* up, int n) {
+  for (int i = 0; i < n; i++) gate[i] = (float)(or_silu((double)gate[i]) * (double)up[i]);
+}
+
+/* src/cpu/model.js:181-183: the first index of the largest value. */
+int or_argmax(const float* logits, int n) {
+  int best = 0;
+  for (int i = 1; i < n; i++)
+    if (logits[i] > logits[best]) best = i;
+  return best;
+}
+
+/* matVec (ops.js:33-41) over an int8 matrix widened per element exactly as
+ * or_dequantize_int8_per_channel does (quantize.js:60-67), rows split over
+ * `threads` OpenMP threads (each row's sum is the same either way). */
+static void matvec_int8(const int8_t* codes, const float* scales, const float* x, int rows, int cols,
+                        const float* bias, float* out, int threads) {
+#pragma omp parallel for schedule(static) num_threads(threads) if (threads > 1)
+  for (int r = 0; r < rows; r++) {
+    const double s = (double)scales[r];
+    const int8_t* row = codes + (size_t)r * cols;
+    double acc = bias ? (double)bias[r] : 0.0;
+    for (int c = 0; c < cols; c++) acc += (double)(float)((double)row[c] * s) * (double)x[c];
+    out[r] = (float)acc;
+  }
+}
+
+typedef struct {
+  const float *in_norm, *post_norm, *qkv_scales, *qkv_bias, *o_scales, *gate_scales, *up_scales, *down_scales;
+  const int8_t *qkv, *o, *gate, *up, *down;
+} or_layer;
+
+struct or_model {
+  int hidden, inter, layers, heads, kv_heads, vocab, head_dim, threads;
+  double eps;
+  double* inv_freq;
+  const int8_t* emb;
+  const float* emb_scales;
+  const float* final_norm;
+  or_layer* w;
+  or_kvcache* cache;
+};
+
+or_model* or_model_new(int hidden, int inter, int layers, int heads, int kv_heads, int vocab, double theta,
+                       double eps, int capacity, int threads) {
+  or_model* m = (or_model*)calloc(1, sizeof(or_model));
+  m->hidden = hidden;
+  m->inter = inter;
+  m->layers = layers;
+  m->heads = heads;
+  m->kv_heads = kv_heads;
+  m->vocab = vocab;
+  m->head_dim = hidden / heads;
+  m->eps = eps;
+  m->threads = threads > 0 ? threads : 1;
+  m->inv_freq = (double*)malloc(sizeof(double) * (size_t)(m->head_dim / 2));
+  or_rope_frequencies(m->head_dim, theta, m->inv_freq);
+  m->w = (or_layer*)calloc((size_t)layers, sizeof(or_layer));
+  m->cache = or_kvcache_new(layers, kv_heads * m->head_dim, capacity, NULL, 0);
+  return m;
+}
+
+void or_model_free(or_model* m) {
+  if (!m) return;
+  or_kvcache_free(m->cache);
+  free(m->inv_freq);
+  free(m->w);
+  free(m);
+}
+
+void or_model_set_layer(or_model* m, int layer, const float* in_norm, const float* post_norm, const int8_t* qkv,
+                        const float* qkv_scales, const float* qkv_bias, const int8_t* o, const float* o_scales,
+                        const int8_t* gate, const float* gate_scales, const int8_t* up, const float* up_scales,
+                        const int8_t* down, const float* down_scales) {
+  or_layer* w = &m->w[layer];
+  w->in_norm = in_norm;
+  w->post_norm = post_norm;
+  w->qkv = qkv;
+  w->qkv_scales = qkv_scales;
+  w->qkv_bias = qkv_bias;
+  w->o = o;
+  w->o_scales = o_scales;
+  w->gate = gate;
+  w->gate_scales = gate_scales;
+  w->up = up;
+  w->up_scales = up_scales;
+  w->down = down;
+  w->down_scales = down_scales;
+}
+
+void or_model_set_embedding(or_model* m, const int8_t* codes, const float* scales, const float* final_norm) {
+  m->emb = codes;
+  m->emb_scales = scales;
+  m->final_norm = final_norm;
+}
+
+int or_model_length(const or_model* m) { return or_kvcache_length(m->cache); }
+void or_model_reset(or_model* m) { or_kvcache_reset(m->cache); }
+
+void or_model_present(const or_model* m, int layer, float* key_out, float* value_out) {
+  or_kvcache_present(m->cache, layer, m->kv_heads, m->head_dim, key_out, value_out);
+}
+
+static float round_f16(float x) { return or_f16_to_f32(or_f32_to_f16(x)); }
+
+/* ReferenceModel.forward (src/cpu/model.js:55-161) over the int8 weights,
+ * with the device path's dtype boundaries restated: q/k/v are rounded to f16
+ * after their projection (the attention kernels take 16-bit inputs) and the
+ * cache keeps RoPE(k) and v rounded to f16 (the f16 cache). Everything else is
+ * the reference's f32 storage with f64 reductions. Returns the greedy pick of
+ * the last position's logits ([vocab], may be NULL) or -1 with err filled. */
+int or_model_forward(or_model* m, const int32_t* tokens, int seq, float* logits_out, char* err, size_t errlen) {
+  const int d = m->hidden, kv_dim = m->kv_heads * m->head_dim, ffn = m->inter;
+  if (seq < 1) {
+    if (err) snprintf(err, errlen, "forward: need at least one token");
+    return -1;
+  }
+  for (int t = 0; t < seq; t++) {
+    if (tokens[t] < 0 || tokens[t] >= m->vocab) {
+      if (err) snprintf(err, errlen, "token %d at position %d is outside the vocabulary", tokens[t], t);
+      return -1;
+    }
+  }
+  const int past = or_kvcache_allocate(m->cache, seq, err, errlen);
+  if (past < 0) return -1;
+  const int total = past + seq;
+  float* x = (float*)malloc(sizeof(float) * (size_t)seq * d);
+  float* normed = (float*)malloc(sizeof(float) * (size_t)d);
+  float* qkv = (float*)malloc(sizeof(float) * (size_t)(d + 2 * kv_dim));
+  float* q = (float*)malloc(sizeof(float) * (size_t)seq * d);
+  float* k = (float*)malloc(sizeof(float) * (size_t)seq * kv_dim);
+  float* v = (float*)malloc(sizeof(float) * (size_t)seq * kv_dim);
+  float* att = (float*)malloc(sizeof(float) * (size_t)seq * d);
+  float* scores = (float*)malloc(sizeof(float) * (size_t)total);
+  float* gate = (float*)malloc(sizeof(float) * (size_t)ffn);
+  float* up = (float*)malloc(sizeof(float) * (size_t)ffn);
+  float* projected = (float*)malloc(sizeof(float) * (size_t)d);
+  float* logits = (float*)malloc(sizeof(float) * (size_t)m->vocab);
+
+  /* #embed (model.js:195-210) of the int8 table */
+  for (int t = 0; t < seq; t++) {
+    const double s = (double)m->emb_scales[tokens[t]];
+    const int8_t* row = m->emb + (size_t)tokens[t] * d;
+    for (int i = 0; i < d; i++) x[(size_t)t * d + i] = (float)((double)row[i] * s);
+  }
+  for (int layer = 0; layer < m->layers; layer++) {
+    const or_layer* w = &m->w[layer];
+    for (int t = 0; t < seq; t++) {
+      or_rmsnorm(x + (size_t)t * d, w->in_norm, m->eps, d, normed);
+      matvec_int8(w->qkv, w->qkv_scales, normed, d + 2 * kv_dim, d, w->qkv_bias, qkv, m->threads);
+      for (int i = 0; i < d; i++) q[(size_t)t * d + i] = round_f16(qkv[i]);
+      for (int i = 0; i < kv_dim; i++) {
+        k[(size_t)t * kv_dim + i] = round_f16(qkv[d + i]);
+        v[(size_t)t * kv_dim + i] = round_f16(qkv[d + kv_dim + i]);
+      }
+      const int position = past + t;
+      for (int h = 0; h < m->heads; h++) or_rope_inplace(q, t * d + h * m->head_dim, m->head_dim, position, m->inv_freq);
+      for (int h = 0; h < m->kv_heads; h++) {
+        or_rope_inplace(k, t * kv_dim + h * m->head_dim, m->head_dim, position, m->inv_freq);
+      }
+      for (int i = 0; i < kv_dim; i++) k[(size_t)t * kv_dim + i] = round_f16(k[(size_t)t * kv_dim + i]);
+    }
+    or_kvcache_write_at(m->cache, layer, past, k, v, seq);
+    or_grouped_attention(q, or_kvcache_keys_up_to(m->cache, layer, total),
+                         or_kvcache_values_up_to(m->cache, layer, total), att, scores, seq, past, m->heads,
+                         m->kv_heads, m->head_dim);
+    for (int t = 0; t < seq; t++) {
+      matvec_int8(w->o, w->o_scales, att + (size_t)t * d, d, d, NULL, projected, m->threads);
+      for (int i = 0; i < d; i++) x[(size_t)t * d + i] += projected[i];
+    }
+    for (int t = 0; t < seq; t++) {
+      float* row = x + (size_t)t * d;
+      or_rmsnorm(row, w->post_norm, m->eps, d, normed);
+      matvec_int8(w->gate, w->gate_scales, normed, ffn, d, NULL, gate, m->threads);
+      matvec_int8(w->up, w->up_scales, normed, ffn, d, NULL, up, m->threads);
+      or_swiglu_inplace(gate, up, ffn);
+      matvec_int8(w->down, w->down_scales, gate, d, ffn, NULL, projected, m->threads);
+      for (int i = 0; i < d; i++) row[i] += projected[i];
+    }
+  }
+  or_kvcache_commit(m->cache, seq);
+  or_rmsnorm(x + (size_t)(seq - 1) * d, m->final_norm, m->eps, d, normed);
+  matvec_int8(m->emb, m->emb_scales, normed, m->vocab, d, NULL, logits, m->threads);
+  const int best = or_argmax(logits, m->vocab);
+  if (logits_out) memcpy(logits_out, logits, sizeof(float) * (size_t)m->vocab);
+  free(x);
+  free(normed);
+  free(qkv);
+  free(q);
+  free(k);
+  free(v);
+  free(att);
+  free(scores);
+  free(gate);
+  free(up);
+  free(projected);
+  free(logits);
+  return best;
+}

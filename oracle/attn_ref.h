@@ -141,6 +141,33 @@ void or_dequantize_int8_per_channel(const int8_t* codes, const float* scales, in
 /* ops.js:33-41: out[r] = bias[r] + sum_c W[r][c] x[c], f64 accumulation, f32 store. */
 void or_matvec(const float* w, const float* x, int rows, int cols, const float* bias, float* out);
 
+/* ---- the decoder around attention: src/core/ops.js, src/cpu/model.js ------- */
+void   or_rmsnorm(const float* x, const float* weight, double eps, int n, float* out);  /* ops.js:17-24 */
+double or_silu(double x);                                                             /* ops.js:81-83 */
+void   or_swiglu_inplace(float* gate, const float* up, int n);                        /* ops.js:88-91 */
+int    or_argmax(const float* logits, int n);                                         /* model.js:181-183 */
+/* A Qwen2 decoder over int8 weights (one f32 scale per output row, the codes
+ * widened per element as or_dequantize_int8_per_channel does) and its own f32
+ * KV cache. The weight arrays are borrowed: the caller keeps them alive.
+ * Matrix rows run on `threads` OpenMP threads. */
+typedef struct or_model or_model;
+or_model* or_model_new(int hidden, int inter, int layers, int heads, int kv_heads, int vocab, double theta,
+                       double eps, int capacity, int threads);
+void or_model_free(or_model* m);
+/* qkv [hidden + 2 kv_dim][hidden] with q rows, k rows, v rows; o [hidden][hidden];
+ * gate, up [inter][hidden]; down [hidden][inter]. */
+void or_model_set_layer(or_model* m, int layer, const float* in_norm, const float* post_norm, const int8_t* qkv,
+                        const float* qkv_scales, const float* qkv_bias, const int8_t* o, const float* o_scales,
+                        const int8_t* gate, const float* gate_scales, const int8_t* up, const float* up_scales,
+                        const int8_t* down, const float* down_scales);
+void or_model_set_embedding(or_model* m, const int8_t* codes, const float* scales, const float* final_norm);
+/* model.js:55-161 on the model's cache; returns the greedy pick or -1 (err). */
+int  or_model_forward(or_model* m, const int32_t* tokens, int seq, float* logits_out, char* err, size_t errlen);
+int  or_model_length(const or_model* m);
+void or_model_reset(or_model* m);
+/* cache.js:97-115: [kv_heads][length][head_dim] */
+void or_model_present(const or_model* m, int layer, float* key_out, float* value_out);
+
 #ifdef __cplusplus
 }
 #endif

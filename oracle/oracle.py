@@ -97,6 +97,33 @@ def lib():
         L.or_dequantize_int8_per_channel.argtypes = [_i8p, _f32p, ctypes.c_int, ctypes.c_int, _f32p]
         L.or_matvec.restype = None
         L.or_matvec.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _f32p, _f32p]
+        L.or_rmsnorm.restype = None
+        L.or_rmsnorm.argtypes = [_f32p, _f32p, ctypes.c_double, ctypes.c_int, _f32p]
+        L.or_silu.restype = ctypes.c_double
+        L.or_silu.argtypes = [ctypes.c_double]
+        L.or_swiglu_inplace.restype = None
+        L.or_swiglu_inplace.argtypes = [_f32p, _f32p, ctypes.c_int]
+        L.or_argmax.restype = ctypes.c_int
+        L.or_argmax.argtypes = [_f32p, ctypes.c_int]
+        L.or_model_new.restype = ctypes.c_void_p
+        L.or_model_new.argtypes = [ctypes.c_int] * 6 + [ctypes.c_double, ctypes.c_double, ctypes.c_int,
+                                                        ctypes.c_int]
+        L.or_model_free.restype = None
+        L.or_model_free.argtypes = [ctypes.c_void_p]
+        L.or_model_set_layer.restype = None
+        L.or_model_set_layer.argtypes = [ctypes.c_void_p, ctypes.c_int, _f32p, _f32p, _i8p, _f32p, _f32p, _i8p,
+                                         _f32p, _i8p, _f32p, _i8p, _f32p, _i8p, _f32p]
+        L.or_model_set_embedding.restype = None
+        L.or_model_set_embedding.argtypes = [ctypes.c_void_p, _i8p, _f32p, _f32p]
+        L.or_model_forward.restype = ctypes.c_int
+        L.or_model_forward.argtypes = [ctypes.c_void_p, _i32p, ctypes.c_int, _f32p, ctypes.c_char_p,
+                                       ctypes.c_size_t]
+        L.or_model_length.restype = ctypes.c_int
+        L.or_model_length.argtypes = [ctypes.c_void_p]
+        L.or_model_reset.restype = None
+        L.or_model_reset.argtypes = [ctypes.c_void_p]
+        L.or_model_present.restype = None
+        L.or_model_present.argtypes = [ctypes.c_void_p, ctypes.c_int, _f32p, _f32p]
     return _lib
 
 
@@ -411,3 +438,133 @@ def normal_array(n: int, seed: int) -> np.ndarray:
     out = np.empty(n, np.float32)
     lib().or_normal_array(_p(out, ctypes.c_float), n, seed & 0xFFFFFFFFFFFFFFFF)
     return out
+
+
+# ---- the decoder around attention (src/core/ops.js, src/cpu/model.js) -------------------
+
+def rmsnorm(x, weight, eps: float) -> np.ndarray:
+    """rmsNorm (src/core/ops.js:17-24)."""
+    x = np.ascontiguousarray(f32(x).reshape(-1))
+    w = np.ascontiguousarray(f32(weight).reshape(-1))
+    out = np.empty_like(x)
+    lib().or_rmsnorm(_p(x, ctypes.c_float), _p(w, ctypes.c_float), float(eps), x.size, _p(out, ctypes.c_float))
+    return out
+
+
+def silu(x: float) -> float:
+    """silu (src/core/ops.js:81-83)."""
+    return lib().or_silu(float(x))
+
+
+def swiglu(gate, up) -> np.ndarray:
+    """swigluInPlace (src/core/ops.js:88-91) on a copy of gate."""
+    g = np.ascontiguousarray(f32(gate).reshape(-1)).copy()
+    u = np.ascontiguousarray(f32(up).reshape(-1))
+    lib().or_swiglu_inplace(_p(g, ctypes.c_float), _p(u, ctypes.c_float), g.size)
+    return g
+
+
+def argmax(logits) -> int:
+    """The greedy pick of generate (src/cpu/model.js:181-183): first index of the largest."""
+    x = np.ascontiguousarray(f32(logits).reshape(-1))
+    return lib().or_argmax(_p(x, ctypes.c_float), x.size)
+
+
+def synthetic_weights(hidden: int, inter: int, layers: int, heads: int, kv_heads: int, vocab: int, seed: int,
+                      std: float = 0.02, norm_jitter: float = 0.0, bias_std: float = 0.0) -> dict:
+    """Seeded random-init weights of the Qwen2 architecture, already int8 per output row
+    (quantizeInt8PerChannel's rule, src/core/quantize.js:36-58: scale = max|w|/127, codes =
+    round(w/scale)) with scales rounded to f16: N(0, std) matrices, norm gains 1 (+ N(0, norm_jitter)),
+    q/k/v bias N(0, bias_std). Returns {"layers": [dict], "embedding": (codes, scales16),
+    "final_norm": f32}; every scale array is float16."""
+    rng = np.random.default_rng(seed)
+    kv_dim = kv_heads * (hidden // heads)
+
+    def mat(rows, cols):
+        w = (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(std))
+        peak = np.abs(w).max(axis=1).astype(np.float64)
+        scale = (peak / 127.0).astype(np.float32).astype(np.float16)
+        s32 = scale.astype(np.float64)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            lv = np.where(s32[:, None] > 0, w.astype(np.float64) / s32[:, None], 0.0)
+        codes = np.clip(np.sign(lv) * np.floor(np.abs(lv) + 0.5), -127, 127).astype(np.int8)
+        return codes, scale
+
+    def gain():
+        g = np.ones(hidden, np.float32)
+        if norm_jitter:
+            g += rng.standard_normal(hidden, dtype=np.float32) * np.float32(norm_jitter)
+        return g
+
+    out = {"layers": []}
+    for _ in range(layers):
+        qkv, sqkv = mat(hidden + 2 * kv_dim, hidden)
+        o, so = mat(hidden, hidden)
+        gate, sg = mat(inter, hidden)
+        up, su = mat(inter, hidden)
+        down, sd = mat(hidden, inter)
+        bias = (rng.standard_normal(hidden + 2 * kv_dim, dtype=np.float32) * np.float32(bias_std)
+                if bias_std else np.zeros(hidden + 2 * kv_dim, np.float32))
+        out["layers"].append(dict(input_norm=gain(), post_attn_norm=gain(), qkv=qkv, qkv_scales=sqkv,
+                                  qkv_bias=bias, o=o, o_scales=so, gate=gate, gate_scales=sg, up=up,
+                                  up_scales=su, down=down, down_scales=sd))
+    out["embedding"] = mat(vocab, hidden)
+    out["final_norm"] = gain()
+    return out
+
+
+class OracleModel:
+    """ReferenceModel (src/cpu/model.js:31-231) over int8 weights, in C, with the device
+    path's f16 boundaries (q/k/v after projection, the KV cache)."""
+
+    def __init__(self, weights: dict, hidden, inter, layers, heads, kv_heads, vocab, theta, eps, capacity,
+                 threads: int = 1):
+        self._keep = []
+        self.vocab, self.kv_heads, self.head_dim = vocab, kv_heads, hidden // heads
+        self._m = lib().or_model_new(hidden, inter, layers, heads, kv_heads, vocab, theta, eps, capacity, threads)
+
+        def keep(a, dt):
+            a = np.ascontiguousarray(np.asarray(a).astype(dt))
+            self._keep.append(a)
+            return _p(a, ctypes.c_float if dt == np.float32 else ctypes.c_int8)
+
+        for i, w in enumerate(weights["layers"]):
+            lib().or_model_set_layer(self._m, i, keep(w["input_norm"], np.float32),
+                                     keep(w["post_attn_norm"], np.float32), keep(w["qkv"], np.int8),
+                                     keep(w["qkv_scales"], np.float32), keep(w["qkv_bias"], np.float32),
+                                     keep(w["o"], np.int8), keep(w["o_scales"], np.float32),
+                                     keep(w["gate"], np.int8), keep(w["gate_scales"], np.float32),
+                                     keep(w["up"], np.int8), keep(w["up_scales"], np.float32),
+                                     keep(w["down"], np.int8), keep(w["down_scales"], np.float32))
+        codes, scales = weights["embedding"]
+        lib().or_model_set_embedding(self._m, keep(codes, np.int8), keep(scales, np.float32),
+                                     keep(weights["final_norm"], np.float32))
+
+    def __del__(self):
+        if getattr(self, "_m", None):
+            lib().or_model_free(self._m)
+            self._m = None
+
+    def forward(self, tokens) -> tuple[np.ndarray, int]:
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        logits = np.empty(self.vocab, np.float32)
+        err = ctypes.create_string_buffer(256)
+        best = lib().or_model_forward(self._m, _p(ids, ctypes.c_int32), ids.size, _p(logits, ctypes.c_float),
+                                      err, 256)
+        if best < 0:
+            raise RangeError_(err.value.decode())
+        return logits, best
+
+    @property
+    def length(self) -> int:
+        return lib().or_model_length(self._m)
+
+    def reset(self):
+        lib().or_model_reset(self._m)
+
+    def present(self, layer: int):
+        n = self.length
+        k = np.empty((self.kv_heads, n, self.head_dim), np.float32)
+        v = np.empty_like(k)
+        lib().or_model_present(self._m, layer, _p(k, ctypes.c_float), _p(v, ctypes.c_float))
+        return k, v

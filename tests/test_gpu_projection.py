@@ -87,3 +87,42 @@ def test_linear_rejects_bad_shapes(ctx, oracle):
     with pytest.raises(b2a.B2AError, match="multiple of 16"):
         b2a.linearInt8(ctx, q, np.ones(4, np.float32), None, np.zeros((1, 20), np.float32), np.zeros((1, 4), np.float32),
                        4, 20, 1)
+
+
+def test_attention_block_composes(ctx, oracle):
+    """One decode step of a Qwen2.5 attention block through the library, as
+    src/cpu/model.js:98-128 runs it: fused q/k/v projection (int8, bias) ->
+    RoPE + append + attention over the cache -> o_proj with the residual add.
+    The oracle chains matVec, ropeInPlace, writeAt, groupedAttention and matVec
+    on the same inputs (q/k/v rounded to f16, the dtype handed between kernels)."""
+    from test_gpu_parity import H, KVH, D, THETA, _fill_cache, _oracle_decode, cfg
+    batch, hidden = 3, 896
+    lengths = [37, 200, 513]
+    rope = b2a.RopeTable(ctx, D, THETA, 1024)
+    c = b2a.GpuKVCache(ctx, cfg(1), 600, batch=batch, dtype="f16")
+    hk, hv = _fill_cache(ctx, c, oracle, lengths, 1, "f16", 900)
+    rows = H * D + 2 * KVH * D
+    wq, sq, sq_arg = _weights(oracle, rows, hidden, 5, "f16")
+    wo, so, so_arg = _weights(oracle, hidden, H * D, 6, "f16")
+    rng = np.random.default_rng(13)
+    bias = (rng.standard_normal(rows) * 0.1).astype(np.float32)
+    x = rng.standard_normal((batch, hidden)).astype(np.float32)
+    qo = np.empty((batch, H * D), np.uint16)
+    ko = np.empty((batch, KVH * D), np.uint16)
+    vo = np.empty((batch, KVH * D), np.uint16)
+    b2a.qkvInt8(ctx, wq, sq_arg, bias, x, qo, ko, vo, hidden, H * D, KVH * D, batch, out_dtype="f16", scale_dtype="f16")
+    att = np.empty((batch, 1, H, D), np.float32)
+    b2a.attentionDecode(ctx, c, rope, 0, qo.reshape(batch, 1, H, D), ko.reshape(batch, 1, KVH, D),
+                        vo.reshape(batch, 1, KVH, D), att, H, dtype="f16")
+    xo = np.empty((batch, hidden), np.float32)
+    b2a.linearInt8(ctx, wo, so_arg, None, att.reshape(batch, H * D), xo, hidden, H * D, batch, residual=x,
+                   scale_dtype="f16")
+    Wqkv = oracle.dequantize_int8(wq, sq, rows, hidden)
+    Wo = oracle.dequantize_int8(wo, so, hidden, H * D)
+    for b in range(batch):
+        qkv = oracle.round_to(oracle.matvec(Wqkv, x[b], rows, hidden, bias), "f16")
+        ref_att, _, _ = _oracle_decode(oracle, qkv[:H * D], qkv[H * D:H * D + KVH * D], qkv[H * D + KVH * D:],
+                                       hk[b, 0], hv[b, 0], lengths[b], "f16")
+        ref_x = (oracle.matvec(Wo, ref_att, hidden, H * D).astype(np.float64) + x[b]).astype(np.float32)
+        assert_parity(xo[b], ref_x, "f32", f"attention block seq {b}")
+    rope.close()
