@@ -350,6 +350,13 @@ b2a_status b2a_model_forward(b2a_model* model, const int32_t* tokens, int seq, f
 b2a_status b2a_model_generate(b2a_model* model, const int32_t* prompt, int n_prompt, int max_tokens,
                               const int32_t* stop_tokens, int n_stop, int32_t* tokens_out, float* best_logits,
                               int* n_generated);
+/* How a one-token forward runs: B2A_DECODE_PERSISTENT (the default where the
+ * shape fits: hidden <= 1024, intermediate <= 8192) is one cooperative kernel
+ * per token for every layer, the output projection and the pick;
+ * B2A_DECODE_LAYERED is the per-layer launches a multi-token forward uses. */
+enum { B2A_DECODE_LAYERED = 0, B2A_DECODE_PERSISTENT = 1 };
+b2a_status b2a_model_set_decode_path(b2a_model* model, int path);
+b2a_status b2a_model_decode_path(const b2a_model* model, int* path);
 b2a_status b2a_model_reset(b2a_model* model);
 b2a_status b2a_model_length(const b2a_model* model, int* length);
 /* The model's KV cache (layers x kv heads x capacity, f16), for reading the

@@ -71,6 +71,8 @@ SIGNATURES = {
     "b2a_model_load_final_norm": (_i, [_vp, _vp, _i]),
     "b2a_model_forward": (_i, [_vp, _vp, _i, _vp, _vp, _i]),
     "b2a_model_generate": (_i, [_vp, _vp, _i, _i, _vp, _i, _vp, _vp, _ip]),
+    "b2a_model_set_decode_path": (_i, [_vp, _i]),
+    "b2a_model_decode_path": (_i, [_vp, _ip]),
     "b2a_model_reset": (_i, [_vp]),
     "b2a_model_length": (_i, [_vp, _ip]),
     "b2a_model_cache": (_i, [_vp, _pp]),

@@ -16,8 +16,8 @@ import ctypes
 import numpy as np
 
 from . import _lib
-from ._lib import B2A_DEVICE, B2A_F16, B2A_F32, B2A_HOST, check, load
-from .runtime import CacheConfig, Context
+from ._lib import B2A_DEVICE, B2A_F16, B2A_F32, B2A_HOST, check
+from .runtime import Context
 
 try:
     import torch
@@ -191,6 +191,17 @@ class Model:
 
     def reset(self) -> None:
         check(self.ctx._lib.b2a_model_reset(self.handle))
+
+    @property
+    def decode_path(self) -> str:
+        """"persistent" (one kernel per token) or "layered" (per-layer launches)."""
+        n = ctypes.c_int()
+        check(self.ctx._lib.b2a_model_decode_path(self.handle, ctypes.byref(n)))
+        return "persistent" if n.value == 1 else "layered"
+
+    @decode_path.setter
+    def decode_path(self, path: str) -> None:
+        check(self.ctx._lib.b2a_model_set_decode_path(self.handle, {"layered": 0, "persistent": 1}[path]))
 
     def forward(self, tokenIds, logits: bool = True) -> dict:
         """forward(tokenIds, {cache}) (src/cpu/model.js:55-161) on the model's cache: the

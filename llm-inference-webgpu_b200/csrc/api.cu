@@ -44,7 +44,7 @@ b2a_status cuda_fail(cudaError_t e, const char* what) {
 const char* const kKernelNames[K_NUM_KINDS] = {"attention_simt", "attention_mma", "combine", "rope_append",
                                                "write_at", "grouped_generic", "prefill_tc",
                                                "prefill_pair", "linear_int8", "embed_int8", "rmsnorm",
-                                               "swiglu", "argmax"};
+                                               "swiglu", "argmax", "decode_step"};
 
 namespace {
 cudaEvent_t take_event(b2a_ctx* ctx) {

@@ -46,7 +46,7 @@ struct b2a_ctx {
 namespace b2a {
 // Kernel kinds reported by b2a_timing_read.
 enum KernelKind { K_ATTN_SIMT = 0, K_ATTN_MMA, K_COMBINE, K_ROPE_APPEND, K_WRITE_AT, K_GROUPED, K_PREFILL_TC,
-                  K_PREFILL_PAIR, K_LINEAR, K_EMBED, K_RMSNORM, K_SWIGLU, K_ARGMAX, K_NUM_KINDS };
+                  K_PREFILL_PAIR, K_LINEAR, K_EMBED, K_RMSNORM, K_SWIGLU, K_ARGMAX, K_DECODE_STEP, K_NUM_KINDS };
 extern const char* const kKernelNames[K_NUM_KINDS];
 
 // Brackets one launch with events on the context's stream while timing is on.
@@ -227,14 +227,65 @@ cudaError_t launch_embed_int8(const int32_t* tokens, int count, const int8_t* co
 // out[r][:] = RMSNorm(x[r][:]) * w, rows of `hidden` f32
 cudaError_t launch_rmsnorm(const float* x, const float* w, double eps, int rows, int hidden, float* out,
                            cudaStream_t st);
-// gate[i] = silu(gate[i]) * up[i]
-cudaError_t launch_swiglu(float* gate, const float* up, int64_t n, cudaStream_t st);
+// h[i] = silu(gu[2i]) * gu[2i+1]: gate and up outputs interleaved
+cudaError_t launch_swiglu(const float* gu, float* h, int64_t n, cudaStream_t st);
 // the first index of the largest of logits[0..n) -> *token (and its value ->
 // *value); scratch: kArgmaxScratchBytes, its counter word zeroed once at
 // allocation (the kernel leaves it zeroed)
 constexpr size_t kArgmaxScratchBytes = 8192;
 cudaError_t launch_argmax(const float* logits, int n, int32_t* token, float* value, void* scratch,
                           cudaStream_t st);
+
+// ---- the whole-decoder decode step (k_decode_step.cu) ----------------------
+// One layer's tensors as the step kernel reads them (device pointers).
+struct StepLayer {
+  const int8_t* qkv;      // [hidden + 2 kv_dim][hidden]
+  const int8_t* o;        // [hidden][hidden]
+  const int8_t* gu;       // [2 inter][hidden]: gate row i at 2i, up row i at 2i+1
+  const int8_t* down;     // [hidden][inter]
+  const void* s_qkv;
+  const void* s_o;
+  const void* s_gu;
+  const void* s_down;
+  const float* b_qkv;
+  const float* n_in;
+  const float* n_post;
+};
+struct StepParams {
+  const StepLayer* layers;                 // device array [num_layers]
+  int num_layers, hidden, inter, heads, kv_heads, vocab, scale_dtype;
+  double eps;
+  const int8_t* emb;                       // tied embedding [vocab][hidden] and its scales
+  const void* s_emb;
+  const float* n_final;
+  uint16_t* kc;                            // one sequence's f16 cache: [layer][kv head][pos][64]
+  uint16_t* vc;
+  int64_t s_layer, s_head;
+  int past;                                // keys already cached; the new token goes to `past`
+  const double* rope_cos;                  // [max_positions][32]
+  const double* rope_sin;
+  const int32_t* token_in;
+  int32_t* token_out;
+  float* best_out;                         // the chosen token's logit, or null
+  unsigned long long* key;                 // argmax word of this step, zero on entry
+  float* logits;                           // [vocab]
+  float* x;                                // scratch: [hidden], [hidden + 2 kv_dim], partials, [inter]
+  float* qkv;
+  float* part;
+  float* h;
+  unsigned* bar;                           // grid-barrier arrival counter
+  unsigned bar_base;                       // its value at launch
+  int* abort;                              // set by a CTA whose barrier wait gave up
+  int32_t* err;
+  int32_t* len;                            // device cache length, set to past + 1
+  int attn_chunk, attn_nchunks;            // attention items: heads x chunks of attn_chunk keys (<= 128)
+};
+size_t decode_step_smem_bytes();
+int decode_step_barriers(int num_layers);
+int decode_step_attn_chunk();   // keys per attention item
+bool decode_step_supported(int hidden, int inter, int q_rows, int vocab, int ctas);
+int decode_step_max_ctas();
+cudaError_t launch_decode_step(const StepParams& p, int ctas, cudaStream_t st);
 
 // Device-pointer bodies of b2a_attention_decode (one layer) and
 // b2a_attention_prefill: the caller validated the shapes and holds the context.

@@ -104,15 +104,16 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm(const float* x, const 
   }
 }
 
-// gate[i] = silu(gate[i]) * up[i], silu(g) = g / (1 + exp(-g)) in f64
-// (src/core/ops.js:81-91), stored f32.
-__global__ void __launch_bounds__(256) k_swiglu(float* gate, const float* up, int64_t n) {
+// h[i] = silu(gu[2i]) * gu[2i+1] (gate and up outputs interleaved), silu(g) =
+// g / (1 + exp(-g)) in f64 (src/core/ops.js:81-91), stored f32.
+__global__ void __launch_bounds__(256) k_swiglu(const float* gu, float* h, int64_t n) {
   pdl_enter();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const double g = gate[i];
+    const float2 v = reinterpret_cast<const float2*>(gu)[i];
+    const double g = v.x;
     const double s = __ddiv_rn(g, __dadd_rn(1.0, exp(-g)));
-    gate[i] = __double2float_rn(__dmul_rn(s, static_cast<double>(up[i])));
+    h[i] = __double2float_rn(__dmul_rn(s, static_cast<double>(v.y)));
   }
 }
 
@@ -209,10 +210,10 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, double eps, int rows,
   return launch_pdl(k_rmsnorm, dim3(rows), dim3(kNormThreads), st, x, w, eps, hidden, out);
 }
 
-cudaError_t launch_swiglu(float* gate, const float* up, int64_t n, cudaStream_t st) {
+cudaError_t launch_swiglu(const float* gu, float* h, int64_t n, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
-  return launch_pdl(k_swiglu, dim3(static_cast<unsigned>(blocks)), dim3(256), st, gate, up, n);
+  return launch_pdl(k_swiglu, dim3(static_cast<unsigned>(blocks)), dim3(256), st, gu, h, n);
 }
 
 cudaError_t launch_argmax(const float* logits, int n, int32_t* token, float* value, void* scratch,

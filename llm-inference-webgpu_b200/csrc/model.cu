@@ -6,7 +6,8 @@
 // Device layout: all weights in one allocation, per layer
 //   qkv codes [hidden + 2 kv_dim][hidden] (q rows, k rows, v rows; one
 //   projection with three outputs), o codes [hidden][hidden], gate and up
-//   codes stacked [2 intermediate][hidden] (one projection with two outputs),
+//   codes interleaved by row [2 intermediate][hidden] (gate row i at 2i, up
+//   row i at 2i+1: one projection whose consecutive outputs pair up for SwiGLU),
 //   down codes [hidden][intermediate], then their scales, the qkv bias and the
 //   two norm gains;
 // then the tied embedding [vocab][hidden] with its scales and the final norm.
@@ -53,6 +54,7 @@ struct b2a_model {
   // activations for up to t_cap tokens per forward
   void* d_act = nullptr;
   int t_cap = 0;
+  // gate: the interleaved gate/up outputs [T][2 inter]; up: silu(gate) * up [T][inter]
   float *x = nullptr, *nx = nullptr, *att = nullptr, *gate = nullptr, *up = nullptr;
   uint16_t *q = nullptr, *k = nullptr, *v = nullptr;
   // fixed buffers: logits, prompt tokens, generated tokens and their logits, argmax scratch
@@ -62,6 +64,18 @@ struct b2a_model {
   int32_t* gen = nullptr;                // [capacity]
   float* best = nullptr;                 // [capacity]
   void* arg_scratch = nullptr;
+  // the one-kernel decode step (k_decode_step.cu): its layer table, scratch,
+  // barrier counter and the per-step argmax words
+  int decode_path = 0;                   // B2A_DECODE_LAYERED or B2A_DECODE_PERSISTENT
+  int step_ctas = 0;                     // 0: the step kernel does not fit this shape
+  void* d_step = nullptr;
+  b2a::StepLayer* step_layers = nullptr;
+  float *sx = nullptr, *sqkv = nullptr, *spart = nullptr, *sh = nullptr;
+  unsigned* bar = nullptr;
+  int* abort_flag = nullptr;
+  unsigned long long* keys = nullptr;    // [capacity + 1]
+  unsigned bar_base = 0;
+  int part_chunks = 0;                   // attention chunks per head the partials hold
 };
 
 using namespace b2a;
@@ -92,6 +106,16 @@ b2a_status copy_in(b2a_model* m, void* dst, const void* src, size_t bytes, int f
   return B2A_OK;
 }
 
+// `rows` rows of `width` bytes, packed at the source, to every dst_pitch bytes.
+b2a_status copy_rows(b2a_model* m, void* dst, size_t dst_pitch, const void* src, size_t width, size_t rows, int flags,
+                     const char* what) {
+  if (src == nullptr) return fail(B2A_EINVAL, "null %s", what);
+  const cudaMemcpyKind kind = flags == B2A_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+  const cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, width, width, rows, kind, m->ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return B2A_OK;
+}
+
 b2a_status ensure_activations(b2a_model* m, int tokens) {
   if (tokens <= m->t_cap) return B2A_OK;
   const int t = std::max(tokens, 16);
@@ -100,7 +124,7 @@ b2a_status ensure_activations(b2a_model* m, int tokens) {
   const size_t h2 = align256(static_cast<size_t>(t) * c.hidden_size * 2);
   const size_t kv2 = align256(static_cast<size_t>(t) * m->kv_dim * 2);
   const size_t i4 = align256(static_cast<size_t>(t) * c.intermediate_size * 4);
-  const size_t total = 3 * h4 + h2 + 2 * kv2 + 2 * i4;
+  const size_t total = 3 * h4 + h2 + 2 * kv2 + 3 * i4;
   if (m->d_act) {
     cudaError_t e = cudaFree(m->d_act);   // waits for work still using it
     m->d_act = nullptr;
@@ -117,7 +141,7 @@ b2a_status ensure_activations(b2a_model* m, int tokens) {
   m->k = reinterpret_cast<uint16_t*>(p + 3 * h4 + h2);
   m->v = reinterpret_cast<uint16_t*>(p + 3 * h4 + h2 + kv2);
   m->gate = reinterpret_cast<float*>(p + 3 * h4 + h2 + 2 * kv2);
-  m->up = reinterpret_cast<float*>(p + 3 * h4 + h2 + 2 * kv2 + i4);
+  m->up = reinterpret_cast<float*>(p + 3 * h4 + h2 + 2 * kv2 + 2 * i4);
   m->t_cap = t;
   return B2A_OK;
 }
@@ -153,17 +177,93 @@ LinearParams linear(const int8_t* w, const void* s, int sdt, const float* bias, 
     if (e_ != cudaSuccess) return cuda_fail(e_, what); \
   } while (0)
 
+// Before the first step kernel of a call: the barrier counter, the abort flag
+// and the host's copy of the counter start from zero.
+b2a_status step_reset(b2a_model* m) {
+  if (m->bar == nullptr) return B2A_OK;
+  const cudaError_t e = cudaMemsetAsync(m->bar, 0, 256, m->ctx->stream);   // counter and abort flag
+  if (e != cudaSuccess) return cuda_fail(e, "resetting the step barrier");
+  m->bar_base = 0;
+  return B2A_OK;
+}
+
+bool step_fits(const b2a_model* m, int past) {
+  const int chunk = decode_step_attn_chunk();
+  return m->step_ctas > 0 && (past + chunk) / chunk <= m->part_chunks;
+}
+
+// One decode step of every layer in one cooperative launch: token *d_tok at
+// the cache's length; the pick goes to *d_next (its logit to *d_best), the
+// logits to m->logits; key_slot: a zeroed argmax word.
+b2a_status run_step(b2a_model* m, const int32_t* d_tok, int32_t* d_next, float* d_best,
+                    unsigned long long* key_slot) {
+  b2a_ctx* ctx = m->ctx;
+  const b2a_model_config& c = m->cfg;
+  const int past = m->cache->len[0];
+  StepParams p{};
+  p.layers = m->step_layers;
+  p.num_layers = c.num_layers;
+  p.hidden = c.hidden_size;
+  p.inter = c.intermediate_size;
+  p.heads = c.num_heads;
+  p.kv_heads = c.num_kv_heads;
+  p.vocab = c.vocab_size;
+  p.scale_dtype = c.scale_dtype == B2A_F32 ? DT_F32 : DT_F16;
+  p.eps = c.rms_norm_eps;
+  p.emb = m->emb;
+  p.s_emb = m->s_emb;
+  p.n_final = m->n_final;
+  p.kc = static_cast<uint16_t*>(m->cache->d_k);
+  p.vc = static_cast<uint16_t*>(m->cache->d_v);
+  p.s_layer = m->cache->s_layer;
+  p.s_head = m->cache->s_head;
+  p.past = past;
+  p.rope_cos = m->rope->d_cos;
+  p.rope_sin = m->rope->d_sin;
+  p.token_in = d_tok;
+  p.token_out = d_next;
+  p.best_out = d_best;
+  p.key = key_slot;
+  p.logits = m->logits;
+  p.x = m->sx;
+  p.qkv = m->sqkv;
+  p.part = m->spart;
+  p.h = m->sh;
+  p.bar = m->bar;
+  p.bar_base = m->bar_base;
+  p.abort = m->abort_flag;
+  p.err = ctx->d_err;
+  p.len = m->cache->d_len;
+  // attention items: every head x every chunk of decode_step_attn_chunk() keys
+  p.attn_chunk = decode_step_attn_chunk();
+  p.attn_nchunks = (past + p.attn_chunk) / p.attn_chunk;
+  cudaError_t e;
+  {
+    KernelTimer kt(ctx, K_DECODE_STEP);
+    e = launch_decode_step(p, m->step_ctas, ctx->stream);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "launching the decode step");
+  m->bar_base += static_cast<unsigned>((decode_step_barriers(c.num_layers) + 1) * m->step_ctas);
+  m->cache->len[0] += 1;   // the kernel set the device copy
+  return B2A_OK;
+}
+
 // One forward over `count` tokens already on the device (d_tok), at the
 // cache's length; leaves the last position's logits in m->logits and the
 // argmax in *d_next (and its logit in *d_best when non-null). The caller has
 // validated the shapes and holds the context.
-b2a_status run_forward(b2a_model* m, const int32_t* d_tok, int count, int32_t* d_next, float* d_best) {
+b2a_status run_forward(b2a_model* m, const int32_t* d_tok, int count, int32_t* d_next, float* d_best,
+                       unsigned long long* key_slot) {
   b2a_ctx* ctx = m->ctx;
   cudaStream_t st = ctx->stream;
   const b2a_model_config& c = m->cfg;
   const int H = c.hidden_size, I = c.intermediate_size, KV = m->kv_dim;
   const int sdt = c.scale_dtype == B2A_F32 ? DT_F32 : DT_F16;
   b2a_status s;
+  if (count == 1 && key_slot != nullptr && m->decode_path == B2A_DECODE_PERSISTENT &&
+      step_fits(m, m->cache->len[0])) {
+    return run_step(m, d_tok, d_next, d_best, key_slot);
+  }
   if ((s = ensure_activations(m, count)) != B2A_OK) return s;
 
   MODEL_LAUNCH(K_EMBED, launch_embed_int8(d_tok, count, m->emb, m->s_emb, sdt, H, c.vocab_size, m->x, ctx->d_err, st),
@@ -193,13 +293,9 @@ b2a_status run_forward(b2a_model* m, const int32_t* d_tok, int count, int32_t* d
     MODEL_LAUNCH(K_RMSNORM, launch_rmsnorm(m->x, w.n_post, c.rms_norm_eps, count, H, m->nx, st),
                  "launching rmsnorm");
     p = linear(w.gu, w.s_gu, sdt, nullptr, m->nx, 2 * I, H, count, m->gate, DT_F32, nullptr);
-    p.out[1] = m->up;
-    p.seg_end[0] = I;
-    p.seg_end[1] = 2 * I;
-    p.nseg = 2;
     MODEL_LAUNCH(K_LINEAR, launch_linear_int8(p, st), "launching the gate/up projection");
     MODEL_LAUNCH(K_SWIGLU, launch_swiglu(m->gate, m->up, static_cast<int64_t>(count) * I, st), "launching swiglu");
-    p = linear(w.down, w.s_down, sdt, nullptr, m->gate, H, I, count, m->x, DT_F32, m->x);
+    p = linear(w.down, w.s_down, sdt, nullptr, m->up, H, I, count, m->x, DT_F32, m->x);
     MODEL_LAUNCH(K_LINEAR, launch_linear_int8(p, st), "launching the down projection");
   }
   // only now are the new positions visible (src/cpu/model.js:145-146)
@@ -256,6 +352,7 @@ void free_model(b2a_model* m) {
   if (m->d_weights) cudaFree(m->d_weights);
   if (m->d_act) cudaFree(m->d_act);
   if (m->d_fixed) cudaFree(m->d_fixed);
+  if (m->d_step) cudaFree(m->d_step);
   if (m->cache) b2a_kvcache_destroy(m->cache);
   if (m->rope) b2a_rope_destroy(m->rope);
   delete m;
@@ -370,6 +467,48 @@ b2a_status b2a_model_create(b2a_ctx* ctx, const b2a_model_config* cfg, int capac
   m->best = reinterpret_cast<float*>(f);
   f += align256(static_cast<size_t>(capacity) * 4);
   m->arg_scratch = f;
+
+  // the one-kernel decode step, when this shape fits it
+  const int ctas = decode_step_max_ctas();
+  if (decode_step_supported(c.hidden_size, c.intermediate_size, m->qkv_rows, c.vocab_size, ctas)) {
+    const int part_chunks = (capacity + decode_step_attn_chunk() - 1) / decode_step_attn_chunk();
+    const size_t bytes = align256(sizeof(StepLayer) * c.num_layers) + align256(H * 4) + align256(Q * 4) +
+                         align256(static_cast<size_t>(c.num_heads) * part_chunks * 68 * 4) + align256(I * 4) + 256 +
+                         align256(sizeof(unsigned long long) * (static_cast<size_t>(capacity) + 1));
+    e = cudaMalloc(&m->d_step, bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->d_step, 0, bytes, ctx->stream);
+    std::vector<StepLayer> table(c.num_layers);
+    for (int l = 0; l < c.num_layers; l++) {
+      const b2a_model::Layer& L = m->layers[l];
+      table[l] = StepLayer{L.qkv, L.o, L.gu, L.down, L.s_qkv, L.s_o, L.s_gu, L.s_down, L.b_qkv, L.n_in, L.n_post};
+    }
+    auto* q = static_cast<unsigned char*>(m->d_step);
+    if (e == cudaSuccess) {
+      e = cudaMemcpyAsync(q, table.data(), sizeof(StepLayer) * c.num_layers, cudaMemcpyHostToDevice, ctx->stream);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+      free_model(m);
+      return cuda_fail(e, "allocating the decode-step state");
+    }
+    m->step_layers = reinterpret_cast<StepLayer*>(q);
+    q += align256(sizeof(StepLayer) * c.num_layers);
+    m->sx = reinterpret_cast<float*>(q);
+    q += align256(H * 4);
+    m->sqkv = reinterpret_cast<float*>(q);
+    q += align256(Q * 4);
+    m->spart = reinterpret_cast<float*>(q);
+    q += align256(static_cast<size_t>(c.num_heads) * part_chunks * 68 * 4);
+    m->sh = reinterpret_cast<float*>(q);
+    q += align256(I * 4);
+    m->bar = reinterpret_cast<unsigned*>(q);
+    m->abort_flag = reinterpret_cast<int*>(q + 128);
+    q += 256;
+    m->keys = reinterpret_cast<unsigned long long*>(q);
+    m->step_ctas = ctas;
+    m->part_chunks = part_chunks;
+    m->decode_path = B2A_DECODE_PERSISTENT;
+  }
   *out = m;
   return B2A_OK;
 }
@@ -396,11 +535,12 @@ b2a_status b2a_model_load_layer(b2a_model* m, int layer, const b2a_layer_weights
   if ((s = copy_in(m, L.b_qkv, w->qkv_bias, Q * 4, flags, "qkv bias")) != B2A_OK) return s;
   if ((s = copy_in(m, L.o, w->o, H * H, flags, "o codes")) != B2A_OK) return s;
   if ((s = copy_in(m, L.s_o, w->o_scales, H * ss, flags, "o scales")) != B2A_OK) return s;
-  if ((s = copy_in(m, L.gu, w->gate, I * H, flags, "gate codes")) != B2A_OK) return s;
-  if ((s = copy_in(m, L.gu + I * H, w->up, I * H, flags, "up codes")) != B2A_OK) return s;
-  if ((s = copy_in(m, L.s_gu, w->gate_scales, I * ss, flags, "gate scales")) != B2A_OK) return s;
-  if ((s = copy_in(m, static_cast<unsigned char*>(L.s_gu) + I * ss, w->up_scales, I * ss, flags, "up scales")) !=
-      B2A_OK) {
+  // gate row i -> row 2i, up row i -> row 2i + 1 (and the same for the scales)
+  if ((s = copy_rows(m, L.gu, 2 * H, w->gate, H, I, flags, "gate codes")) != B2A_OK) return s;
+  if ((s = copy_rows(m, L.gu + H, 2 * H, w->up, H, I, flags, "up codes")) != B2A_OK) return s;
+  if ((s = copy_rows(m, L.s_gu, 2 * ss, w->gate_scales, ss, I, flags, "gate scales")) != B2A_OK) return s;
+  if ((s = copy_rows(m, static_cast<unsigned char*>(L.s_gu) + ss, 2 * ss, w->up_scales, ss, I, flags,
+                     "up scales")) != B2A_OK) {
     return s;
   }
   if ((s = copy_in(m, L.down, w->down, H * I, flags, "down codes")) != B2A_OK) return s;
@@ -455,7 +595,12 @@ b2a_status b2a_model_forward(b2a_model* m, const int32_t* tokens, int seq, float
   } else if (d_next == nullptr) {
     d_next = m->gen;
   }
-  if ((s = run_forward(m, d_tok, seq, d_next, nullptr)) != B2A_OK) return s;
+  if ((s = step_reset(m)) != B2A_OK) return s;
+  if (m->keys) {
+    cudaError_t e = cudaMemsetAsync(m->keys, 0, sizeof(unsigned long long), st);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the argmax word");
+  }
+  if ((s = run_forward(m, d_tok, seq, d_next, nullptr, m->keys)) != B2A_OK) return s;
   const size_t lbytes = static_cast<size_t>(m->cfg.vocab_size) * 4;
   if (flags == B2A_HOST) {
     cudaError_t e = cudaSuccess;
@@ -499,11 +644,18 @@ b2a_status b2a_model_generate(b2a_model* m, const int32_t* prompt, int n_prompt,
   m->cache->len[0] = 0;
   cudaError_t e = launch_lengths_update(m->cache->d_len, 0, 1, 0, 1, st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->tokens, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess && m->keys) {
+    e = cudaMemsetAsync(m->keys, 0, sizeof(unsigned long long) * (m->capacity + 1), st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "starting the generation");
+  if ((s = step_reset(m)) != B2A_OK) return s;
   int done = 0;
   for (int step = 0; step < max_tokens; step++) {
     const int32_t* in = step == 0 ? m->tokens : m->gen + step - 1;
-    if ((s = run_forward(m, in, step == 0 ? n_prompt : 1, m->gen + step, m->best + step)) != B2A_OK) return s;
+    if ((s = run_forward(m, in, step == 0 ? n_prompt : 1, m->gen + step, m->best + step,
+                         m->keys ? m->keys + step : nullptr)) != B2A_OK) {
+      return s;
+    }
     done = step + 1;
     if (n_stop > 0) {   // the host sees each token before deciding to go on
       int32_t tok = 0;
@@ -520,6 +672,22 @@ b2a_status b2a_model_generate(b2a_model* m, const int32_t* prompt, int n_prompt,
   if (e != cudaSuccess) return cuda_fail(e, "copying the generated tokens");
   if ((s = stream_sync_check(m->ctx)) != B2A_OK) return s;
   *n_generated = done;
+  return B2A_OK;
+}
+
+b2a_status b2a_model_set_decode_path(b2a_model* m, int path) {
+  if (m == nullptr) return fail(B2A_EINVAL, "null model");
+  if (path != B2A_DECODE_LAYERED && path != B2A_DECODE_PERSISTENT) return fail(B2A_EINVAL, "unknown decode path %d", path);
+  if (path == B2A_DECODE_PERSISTENT && m->step_ctas <= 0) {
+    return fail(B2A_EINVAL, "this model's shape does not fit the one-kernel decode step");
+  }
+  m->decode_path = path;
+  return B2A_OK;
+}
+
+b2a_status b2a_model_decode_path(const b2a_model* m, int* path) {
+  if (m == nullptr || path == nullptr) return fail(B2A_EINVAL, "null argument");
+  *path = m->decode_path;
   return B2A_OK;
 }
 

@@ -72,11 +72,13 @@ def check_pick(gpu_token, ref_logits, err_abs):
         assert gpu_token == o.argmax(ref_logits)
 
 
+@pytest.mark.parametrize("path", ["persistent", "layered"])
 @pytest.mark.parametrize("shape", ["qwen2", "small"])
-def test_prefill_then_decode_matches_oracle(ctx, shape):
+def test_prefill_then_decode_matches_oracle(ctx, shape, path):
     c = QWEN2 if shape == "qwen2" else SMALL
     w = _weights(c, 11)
     gm, om = _gpu_model(ctx, c, w), _oracle_model(c, w)
+    gm.decode_path = path
     rng = np.random.default_rng(5)
     tokens = rng.integers(0, c["vocab"], 37).tolist()
     out = gm.forward(tokens)
@@ -218,3 +220,29 @@ def test_config4_full_size_prefill_and_decode(ctx):
         assert rel <= LOGIT_REL
         check_pick(out["token"], ref, err)
     gm.close()
+
+
+def test_decode_paths_agree_over_a_long_context(ctx):
+    """The one-kernel step and the per-layer launches walk the same 300-token
+    sequence (the step kernel's attention splits into several chunks there)."""
+    c = QWEN2
+    w = _weights(c, 17)
+    a, b = _gpu_model(ctx, c, w, capacity=512), _gpu_model(ctx, c, w, capacity=512)
+    assert a.decode_path == "persistent"
+    b.decode_path = "layered"
+    prompt = np.random.default_rng(9).integers(0, c["vocab"], 290).tolist()
+    ra, rb = a.forward(prompt), b.forward(prompt)
+    assert np.array_equal(ra["logits"], rb["logits"])        # the same prefill path
+    nxt = ra["token"]
+    for _ in range(12):
+        ra, rb = a.forward([nxt]), b.forward([nxt])
+        rel, err = worst_relative(ra["logits"], rb["logits"])
+        assert rel <= LOGIT_REL
+        check_pick(ra["token"], rb["logits"], err)
+        nxt = rb["token"]
+    for layer in range(c["layers"]):
+        ka = o.from_bits(a.present(layer)["key"], "f16")
+        kb = o.from_bits(b.present(layer)["key"], "f16")
+        assert np.abs(ka - kb).max() <= 2e-3
+    a.close()
+    b.close()
