@@ -340,6 +340,8 @@ def run_ours(args) -> None:
         line["prefill"] = bench_prefill(torch, b2a, ctx, stream, dev, pk, args)
     if world == 1 and not args.no_layer:
         line["layer"] = bench_layer(torch, b2a, ctx, stream, dev, args)
+    if world == 1 and not args.no_generation:
+        line["generation"] = bench_generation(torch, b2a, ctx, stream, dev, pk["hbm_gbs"], args)
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, used, sample = cpu_decode_sample(lengths, target_s=args.cpu_seconds)
         # the reference itself is single-threaded JavaScript: the same restatement on one thread beside it
@@ -554,6 +556,136 @@ def bench_layer(torch, b2a, ctx, stream, dev, args) -> dict:
     return res
 
 
+def bench_generation(torch, b2a, ctx, stream, dev, peak_gbs, args) -> dict:
+    """Qwen2.5-0.5B-architecture greedy generation with random-init
+    N(0, 0.02) weights quantized to int8 per output row (f16 scales; norm gains 1, biases 0),
+    a 64-token seeded prompt, then 128 greedy tokens, through the public generate call (host
+    prompt in, host tokens out). The prompt runs the per-layer kernels (tensor-core attention);
+    every decode token is one cooperative kernel over all 24 layers, the output projection and
+    the pick. Roofline: the bytes a decode token must read (every weight byte once, plus the
+    cached keys/values) over its device time, against the measured HBM copy bandwidth."""
+    cfg = b2a.ModelConfig.qwen25_05b()
+    Hd, I, V, L = cfg.hiddenSize, cfg.intermediateSize, cfg.vocabSize, cfg.numLayers
+    Q = Hd + 2 * cfg.kvDim
+    n_prompt, n_new = 64, 128
+    g = torch.Generator(device=dev)
+    g.manual_seed(44)
+
+    def quant(rows, cols):
+        # quantizeInt8PerChannel's rule (src/core/quantize.js:36-58) on the device
+        w = torch.randn(rows, cols, generator=g, device=dev) * 0.02
+        scale = (w.abs().amax(dim=1) / 127.0).half()
+        s32 = scale.float().clamp_min(1e-30)[:, None]
+        lv = w / s32
+        codes = (lv.sign() * (lv.abs() + 0.5).floor()).clamp(-127, 127).to(torch.int8)
+        return codes.contiguous(), scale.contiguous()
+
+    model = b2a.Model(ctx, cfg, n_prompt + n_new, scale_dtype="f16")
+    with torch.cuda.stream(stream):
+        ones = torch.ones(Hd, device=dev)
+        host = {"layers": []}
+        for layer in range(L):
+            qkv, sqkv = quant(Q, Hd)
+            o, so = quant(Hd, Hd)
+            gate, sg = quant(I, Hd)
+            up, su = quant(I, Hd)
+            down, sd = quant(Hd, I)
+            w = dict(input_norm=ones, post_attn_norm=ones, qkv=qkv, qkv_scales=sqkv,
+                     qkv_bias=torch.zeros(Q, device=dev), o=o, o_scales=so, gate=gate, gate_scales=sg,
+                     up=up, up_scales=su, down=down, down_scales=sd)
+            torch.cuda.synchronize(dev)
+            model.load_layer(layer, w)
+            if not args.no_cpu:
+                host["layers"].append({k: (v.float().cpu().numpy() if k.endswith("scales") else v.cpu().numpy())
+                                       for k, v in w.items()})
+        emb, semb = quant(V, Hd)
+        torch.cuda.synchronize(dev)
+        model.load_embedding(emb, semb)
+        model.load_final_norm(ones)
+        if not args.no_cpu:
+            host["embedding"] = (emb.cpu().numpy(), semb.float().cpu().numpy())
+            host["final_norm"] = ones.cpu().numpy()
+        del emb
+    prompt = np.random.default_rng(4).integers(0, V, n_prompt).astype(np.int32).tolist()
+    for _ in range(2):
+        model.generate_all(prompt, n_new)
+    reps = 5
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    walls = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        if _ == reps - 1:
+            e0.record(stream)
+        toks, best = model.generate_all(prompt, n_new)
+        if _ == reps - 1:
+            e1.record(stream)
+        walls.append(time.perf_counter() - t0)
+    torch.cuda.synchronize(dev)
+    dev_ms = e0.elapsed_time(e1)
+    wall = float(np.median(walls))
+    # per-kernel device time of one more run
+    ctx.enable_timing(True)
+    model.generate_all(prompt, n_new)
+    kt = ctx.read_timing()
+    ctx.enable_timing(False)
+    step = kt.get("decode_step", (0, 0.0))
+    step_us = step[1] / max(1, step[0]) * 1e3
+    prefill_ms = sum(v[1] for k, v in kt.items() if k != "decode_step")
+    weight_bytes = L * (Q * Hd + Hd * Hd + 2 * I * Hd + Hd * I) + V * Hd
+    scale_bytes = 2 * (L * (Q + Hd + 2 * I + Hd) + V)
+    mean_ctx = n_prompt + (n_new - 1) / 2.0
+    kv_bytes = L * 2 * cfg.numKVHeads * mean_ctx * D * 2
+    token_bytes = weight_bytes + scale_bytes + kv_bytes
+    achieved = token_bytes / (step_us * 1e-6) / 1e9 if step_us > 0 else None
+    res = {
+        "metric": "config 4 greedy generation", "unit": "tokens/s",
+        "value": round(n_new / wall, 1),
+        "device_tokens_per_s": round(n_new / (dev_ms / 1e3), 1),
+        "config": {"model": "Qwen2.5-0.5B architecture, random-init N(0,0.02)", "layers": L, "hidden": Hd,
+                   "intermediate": I, "vocab": V, "weights": "int8 per output row, f16 scales",
+                   "prompt": n_prompt, "new_tokens": n_new, "batch": 1, "data": "synthetic"},
+        "e2e": {"value": round(n_new / wall, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * n_prompt,
+                "d2h_bytes_per_step": 8 * n_new},
+        "prefill_ms": round(prefill_ms, 3),
+        "decode_us_per_token": round(step_us, 2),
+        "decode_path": model.decode_path,
+        "roofline": {"bound": "hbm", "kernel": "decode_step", "achieved": round(achieved, 1) if achieved else None,
+                     "peak": peak_gbs, "unit": "GB/s", "frac": round(achieved / peak_gbs, 3) if achieved else None,
+                     "traffic": None, "bytes_per_token": int(token_bytes)},
+        "kernels_ms": {k: round(v[1], 3) for k, v in kt.items()},
+        "gpu_launches_per_generation": int(sum(v[0] for v in kt.values())),
+        "tokens_head": [int(t) for t in toks[:8]],
+    }
+    model.decode_path = "layered"
+    t0 = time.perf_counter()
+    model.generate_all(prompt, n_new)
+    res["layered_tokens_per_s"] = round(n_new / (time.perf_counter() - t0), 1)
+    model.close()
+    if not args.no_cpu:
+        res["cpu_baseline"] = cpu_generation_sample(host, cfg, prompt, min(args.cpu_seconds, 20.0))
+    return res
+
+
+def cpu_generation_sample(host: dict, cfg, prompt, target_s: float) -> dict:
+    """The oracle's ReferenceModel restatement (C, f64 reductions, int8 weights widened per
+    element) on the host cores: a short prompt, then decode tokens until target_s passes;
+    tokens/s of the decode tokens."""
+    import os as _os
+    from oracle import oracle as o
+    threads = _os.cpu_count() or 1
+    om = o.OracleModel(host, cfg.hiddenSize, cfg.intermediateSize, cfg.numLayers, cfg.numHeads, cfg.numKVHeads,
+                       cfg.vocabSize, cfg.ropeTheta, cfg.rmsNormEps, 256, threads)
+    _, nxt = om.forward(prompt[:4])
+    n, t0 = 0, time.perf_counter()
+    while n < 64 and (n < 2 or time.perf_counter() - t0 < target_s):
+        _, nxt = om.forward([nxt])
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"4-token prompt, then {n} greedy decode tokens of the full config-4 model"}
+
+
 def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
     """causal prefill, bf16 Q/K/V, RoPE at 0..S-1, fused append, bf16 out."""
     res = {"metric": "prefill-attn TFLOPS", "unit": "TFLOPS", "dtype": "bf16", "sweep": {}}
@@ -678,6 +810,7 @@ def main() -> None:
     ap.add_argument("--no-splitkv", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-layer", action="store_true", help="skip the attention-block (projections) measurement")
+    ap.add_argument("--no-generation", action="store_true", help="skip the config-4 generation measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192, 16384])
     ap.add_argument("--prefill-cache", choices=["f16", "bf16"], default="f16",
