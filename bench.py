@@ -227,6 +227,11 @@ def run_ours(args) -> None:
     stream = torch.cuda.Stream(device=dev)
     ctx = b2a.Context(local)
     ctx.set_stream(stream)
+    if args.generation_only:   # config 4 alone (a short run to profile its launches)
+        res = bench_generation(torch, b2a, ctx, stream, dev, peaks()["hbm_gbs"], args)
+        if rank == 0:
+            print(json.dumps(res))
+        return
     lengths = config3_lengths(rank)
     nb = config3_bytes(lengths)
     with torch.cuda.stream(stream):
@@ -567,7 +572,7 @@ def bench_generation(torch, b2a, ctx, stream, dev, peak_gbs, args) -> dict:
     cfg = b2a.ModelConfig.qwen25_05b()
     Hd, I, V, L = cfg.hiddenSize, cfg.intermediateSize, cfg.vocabSize, cfg.numLayers
     Q = Hd + 2 * cfg.kvDim
-    n_prompt, n_new = 64, 128
+    n_prompt, n_new = 64, args.gen_new_tokens
     g = torch.Generator(device=dev)
     g.manual_seed(44)
 
@@ -609,7 +614,7 @@ def bench_generation(torch, b2a, ctx, stream, dev, peak_gbs, args) -> dict:
     prompt = np.random.default_rng(4).integers(0, V, n_prompt).astype(np.int32).tolist()
     for _ in range(2):
         model.generate_all(prompt, n_new)
-    reps = 5
+    reps = args.gen_reps
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     walls = []
@@ -811,6 +816,9 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-layer", action="store_true", help="skip the attention-block (projections) measurement")
     ap.add_argument("--no-generation", action="store_true", help="skip the config-4 generation measurement")
+    ap.add_argument("--generation-only", action="store_true", help="only the config-4 generation measurement")
+    ap.add_argument("--gen-new-tokens", type=int, default=128, help="greedy tokens per generation (config 4: 128)")
+    ap.add_argument("--gen-reps", type=int, default=5, help="timed generations")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--prefill-seqs", type=int, nargs="+", default=[8, 64, 512, 2048, 8192, 16384])
     ap.add_argument("--prefill-cache", choices=["f16", "bf16"], default="f16",

@@ -749,14 +749,16 @@ __device__ void consumer(const StepParams& p, StepSmem& sm, const unsigned char*
       if (xthread) xv = __ldcg(reinterpret_cast<const float4*>(p.x) + tid);
       const float sx = norm_digits(sm, H, xv, p.eps, rd);
       walk_rows(p, sm, ring, sg, rd, w, 2, [&](int r, int first, int stride, int cnt, const float (&y)[4]) {
-        // rows come as (gate, up) pairs: lanes 0 and 1 finish pairs 0 and 1
+        // rows come as (gate, up) pairs: lanes 0 and 1 finish pairs 0 and 1;
         if (2 * lane < cnt) {
           const float yg = lane == 0 ? y[0] : y[2];
           const float yu = lane == 0 ? y[1] : y[3];
           const int row = r + first + lane * stride - sg.r0;   // even: the gate row
-          const double gv = yg * sx * sm.rowscale[row];
-          const double uv = yu * sx * sm.rowscale[row + 1];
-          p.h[(sg.r0 + row) >> 1] = __double2float_rn(__dmul_rn(__ddiv_rn(gv, __dadd_rn(1.0, exp(-gv))), uv));
+          // silu in f32 here (the per-layer kernel keeps the reference's f64):
+          // one division and one expf on the chunk's critical path
+          const float gv = yg * sx * sm.rowscale[row];
+          const float uv = yu * sx * sm.rowscale[row + 1];
+          p.h[(sg.r0 + row) >> 1] = __fdiv_rn(gv, 1.f + expf(-gv)) * uv;
         }
       });
     }
