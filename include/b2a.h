@@ -358,6 +358,44 @@ enum { B2A_DECODE_LAYERED = 0, B2A_DECODE_PERSISTENT = 1 };
 b2a_status b2a_model_set_decode_path(b2a_model* model, int path);
 b2a_status b2a_model_decode_path(const b2a_model* model, int* path);
 b2a_status b2a_model_reset(b2a_model* model);
+
+/* ---- weights: safetensors files (Safetensors, src/core/safetensors.js:36-199) -------
+ * Opening reads and validates the header against the file's size with the
+ * reference's checks and messages (B2A_EINVAL): "not a safetensors file",
+ * "header length L does not fit in a N-byte file", "header is not valid UTF-8
+ * JSON: ...", "NAME: unknown dtype ...", "NAME: shape must be an array of
+ * non-negative integers", "NAME: data_offsets must be a pair", "NAME: bad
+ * data_offsets [b, e]", "NAME: ends at E but the data section is only D bytes",
+ * "NAME: shape [..] of DT needs X bytes but the header reserves Y", "B overlaps
+ * A". Tensor bytes are read on demand (a file is pread, a memory image is
+ * copied at open). Names come in the header's order. */
+typedef struct b2a_safetensors b2a_safetensors;
+b2a_status b2a_safetensors_open(const char* path, b2a_safetensors** out);
+b2a_status b2a_safetensors_open_memory(const void* bytes, size_t size, b2a_safetensors** out);
+b2a_status b2a_safetensors_close(b2a_safetensors* st);
+int b2a_safetensors_count(const b2a_safetensors* st);
+/* The index-th name (header order); NULL when out of range. Valid until close. */
+const char* b2a_safetensors_name(const b2a_safetensors* st, int index);
+/* The __metadata__ object as JSON text, or NULL when the header has none. */
+const char* b2a_safetensors_metadata(const b2a_safetensors* st);
+/* info(name): dtype ("F32", "BF16", ...; at least 16 chars of room), up to
+ * max_dims dimensions, their count and the tensor's byte length. B2A_EINVAL
+ * 'no tensor named "NAME"' for an unknown name. */
+b2a_status b2a_safetensors_info(const b2a_safetensors* st, const char* name, char* dtype, int64_t* shape,
+                                int max_dims, int* ndim, int64_t* byte_length);
+/* readRaw: the tensor's bytes as stored (capacity >= byte_length). */
+b2a_status b2a_safetensors_read_raw(const b2a_safetensors* st, const char* name, void* dst, size_t capacity);
+/* readF32: widened to f32 (F32, BF16, F16, F64 rounded to nearest even);
+ * "NAME: cannot widen DT to f32" otherwise. count >= the element count. */
+b2a_status b2a_safetensors_read_f32(const b2a_safetensors* st, const char* name, float* dst, size_t count);
+/* The model's weights from a Qwen2 checkpoint (GpuModel.load, src/gpu/model.js:147-207;
+ * config.checkAgainst, src/core/config.js:125-150): the file must hold exactly
+ * the tensors the model's config implies (tied embeddings: no lm_head.weight),
+ * each with its shape, else B2A_EINVAL "weights do not match config (N
+ * problems): ...". Every matrix is widened to f32, quantized to int8 per output
+ * row (b2a_quantize_int8_per_channel; the scale then stored in the model's
+ * scale dtype) and uploaded with the norms and q/k/v biases. */
+b2a_status b2a_model_load_safetensors(b2a_model* model, const b2a_safetensors* st);
 b2a_status b2a_model_length(const b2a_model* model, int* length);
 /* The model's KV cache (layers x kv heads x capacity, f16), for reading the
  * present keys and values with b2a_kvcache_read. Owned by the model. */

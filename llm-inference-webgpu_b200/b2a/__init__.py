@@ -11,4 +11,5 @@ from .attention import (appendRope, attentionDecode, attentionPrefill, decodePar
                         default_context, groupedAttention, kvHeadFor, linearInt8, lseCombine, qkvInt8,
                         quantizeInt8PerChannel, ropeFrequencies, ropeTables)
 from .model import Model, ModelConfig  # noqa: F401
+from .weights import Safetensors, TensorInfo, write_safetensors  # noqa: F401
 from .runtime import CacheConfig, Context, Exchange, GpuKVCache, RopeTable  # noqa: F401

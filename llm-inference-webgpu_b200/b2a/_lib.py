@@ -74,6 +74,16 @@ SIGNATURES = {
     "b2a_model_set_decode_path": (_i, [_vp, _i]),
     "b2a_model_decode_path": (_i, [_vp, _ip]),
     "b2a_model_reset": (_i, [_vp]),
+    "b2a_safetensors_open": (_i, [ctypes.c_char_p, _pp]),
+    "b2a_safetensors_open_memory": (_i, [_vp, ctypes.c_size_t, _pp]),
+    "b2a_safetensors_close": (_i, [_vp]),
+    "b2a_safetensors_count": (_i, [_vp]),
+    "b2a_safetensors_name": (ctypes.c_char_p, [_vp, _i]),
+    "b2a_safetensors_metadata": (ctypes.c_char_p, [_vp]),
+    "b2a_safetensors_info": (_i, [_vp, ctypes.c_char_p, ctypes.c_char_p, _i64p, _i, _ip, _i64p]),
+    "b2a_safetensors_read_raw": (_i, [_vp, ctypes.c_char_p, _vp, ctypes.c_size_t]),
+    "b2a_safetensors_read_f32": (_i, [_vp, ctypes.c_char_p, _vp, ctypes.c_size_t]),
+    "b2a_model_load_safetensors": (_i, [_vp, _vp]),
     "b2a_model_length": (_i, [_vp, _ip]),
     "b2a_model_cache": (_i, [_vp, _pp]),
 }

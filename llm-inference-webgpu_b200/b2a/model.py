@@ -81,6 +81,39 @@ class ModelConfig:
         self.kvGroupSize = self.numHeads // self.numKVHeads
         self.kvDim = self.numKVHeads * self.headDim
 
+    def expectedTensors(self) -> dict:
+        """config.expectedTensors (src/core/config.js:88-121): every tensor the
+        architecture requires, name -> shape."""
+        d, kv = self.hiddenSize, self.kvDim
+        shapes = {"model.embed_tokens.weight": (self.vocabSize, d), "model.norm.weight": (d,)}
+        for i in range(self.numLayers):
+            p = f"model.layers.{i}."
+            shapes[p + "input_layernorm.weight"] = (d,)
+            shapes[p + "post_attention_layernorm.weight"] = (d,)
+            shapes[p + "self_attn.q_proj.weight"] = (d, d)
+            shapes[p + "self_attn.q_proj.bias"] = (d,)
+            shapes[p + "self_attn.k_proj.weight"] = (kv, d)
+            shapes[p + "self_attn.k_proj.bias"] = (kv,)
+            shapes[p + "self_attn.v_proj.weight"] = (kv, d)
+            shapes[p + "self_attn.v_proj.bias"] = (kv,)
+            shapes[p + "self_attn.o_proj.weight"] = (d, d)
+            shapes[p + "mlp.gate_proj.weight"] = (self.intermediateSize, d)
+            shapes[p + "mlp.up_proj.weight"] = (self.intermediateSize, d)
+            shapes[p + "mlp.down_proj.weight"] = (d, self.intermediateSize)
+        if not self.tieWordEmbeddings:
+            shapes["lm_head.weight"] = (self.vocabSize, d)
+        return shapes
+
+    def parameterCount(self) -> int:
+        """config.parameterCount (src/core/config.js:153-159)."""
+        total = 0
+        for shape in self.expectedTensors().values():
+            n = 1
+            for v in shape:
+                n *= v
+            total += n
+        return total
+
     @staticmethod
     def qwen25_05b(**over) -> "ModelConfig":
         """Qwen2.5-0.5B's architecture."""
@@ -175,6 +208,12 @@ class Model:
         if wc != ws:
             raise ValueError("mix of host and device arrays in one call")
         check(self.ctx._lib.b2a_model_load_embedding(self.handle, ctypes.c_void_p(pc), ctypes.c_void_p(ps), wc))
+
+    def load_safetensors(self, st) -> None:
+        """The weights of a Qwen2 checkpoint (b2a.weights.Safetensors): checked against the
+        config (config.checkAgainst, src/core/config.js:125-150), quantized to int8 per output
+        row and uploaded."""
+        check(self.ctx._lib.b2a_model_load_safetensors(self.handle, st.handle))
 
     def load_final_norm(self, weight) -> None:
         if not (torch is not None and isinstance(weight, torch.Tensor)):

@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <string>
 #include <vector>
 
 #include "b2a.h"
@@ -295,6 +296,11 @@ b2a_status attn_decode_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope
 b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx,
                                int num_heads, const void* q, const void* k, const void* v, b2a_dtype in_dtype,
                                int count, void* out, b2a_dtype out_dtype);
+// safetensors helpers (weights.cu): a byte range of one tensor, and the
+// widening of n stored elements of dtype dt to f32 (false: not widenable)
+b2a_status st_read_range(const b2a_safetensors* st, const char* name, uint64_t offset, uint64_t length, void* dst);
+bool st_widen(const std::string& dt, const void* src, size_t n, float* dst);
+
 // the context's busy flag (one call at a time, src/gpu/model.js:231)
 bool ctx_acquire(b2a_ctx* ctx);
 void ctx_release(b2a_ctx* ctx);

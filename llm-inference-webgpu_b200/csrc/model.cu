@@ -23,8 +23,10 @@
 //   -> commit -> final rmsnorm of the last row -> tied output projection ->
 //   argmax.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <new>
+#include <string>
 #include <vector>
 
 #include "b2a_internal.cuh"
@@ -709,3 +711,163 @@ b2a_status b2a_model_cache(b2a_model* m, b2a_kvcache** cache) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------- weights from a file --
+
+namespace {
+
+// f32 -> f16 bits, round to nearest even (what a Float16 store does)
+uint16_t host_f32_to_f16(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u, ax = x & 0x7fffffffu;
+  if (ax >= 0x7f800000u) return static_cast<uint16_t>(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u | ((ax >> 13) & 0x3ffu) : 0u));
+  if (ax >= 0x477ff000u) return static_cast<uint16_t>(sign | 0x7c00u);   // rounds to infinity
+  if (ax < 0x38800000u) {                                               // f16 subnormal or zero
+    float a;
+    std::memcpy(&a, &ax, 4);
+    return static_cast<uint16_t>(sign | static_cast<uint32_t>(std::nearbyint(a * 16777216.0f)));
+  }
+  uint32_t h = (((ax >> 23) - 112u) << 10) | ((ax & 0x7fffffu) >> 13);
+  const uint32_t rem = ax & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+  return static_cast<uint16_t>(sign | h);
+}
+
+std::string shape_text(const std::vector<int64_t>& s) {
+  std::string t;
+  for (size_t k = 0; k < s.size(); k++) t += (k ? "," : "") + std::to_string(s[k]);
+  return t;
+}
+
+// rows x cols of tensor `name` from row r0: widened to f32, quantized per row
+// (quantize.js:36-58), codes to `codes`, scales (in the model's dtype) to `scales`.
+b2a_status quantize_rows(const b2a_model* m, const b2a_safetensors* st, const char* name, int64_t r0, int rows,
+                         int cols, int8_t* codes, unsigned char* scales, std::vector<float>& f,
+                         std::vector<float>& s32) {
+  char dt[16];
+  b2a_status s = b2a_safetensors_info(st, name, dt, nullptr, 0, nullptr, nullptr);
+  if (s != B2A_OK) return s;
+  int64_t bytes = 0;
+  b2a_safetensors_info(st, name, nullptr, nullptr, 0, nullptr, &bytes);
+  int esz = std::string(dt) == "F64" ? 8 : (std::string(dt) == "F32" ? 4 : 2);
+  const size_t n = static_cast<size_t>(rows) * cols;
+  std::vector<unsigned char> raw(n * esz);
+  f.resize(n);
+  s32.resize(rows);
+  if ((s = st_read_range(st, name, static_cast<uint64_t>(r0) * cols * esz, n * esz, raw.data())) != B2A_OK) return s;
+  if (!st_widen(dt, raw.data(), n, f.data())) return fail(B2A_EINVAL, "%s: cannot widen %s to f32", name, dt);
+  if ((s = b2a_quantize_int8_per_channel(f.data(), rows, cols, codes, s32.data())) != B2A_OK) return s;
+  for (int r = 0; r < rows; r++) {
+    if (m->ssz == 4) {
+      std::memcpy(scales + 4 * r, &s32[r], 4);
+    } else {
+      const uint16_t h = host_f32_to_f16(s32[r]);
+      std::memcpy(scales + 2 * r, &h, 2);
+    }
+  }
+  return B2A_OK;
+}
+
+b2a_status read_vector(const b2a_safetensors* st, const std::string& name, float* dst, size_t n) {
+  return b2a_safetensors_read_f32(st, name.c_str(), dst, n);
+}
+
+}  // namespace
+
+extern "C" b2a_status b2a_model_load_safetensors(b2a_model* m, const b2a_safetensors* st) {
+  if (m == nullptr || st == nullptr) return fail(B2A_EINVAL, "null argument");
+  const b2a_model_config& c = m->cfg;
+  const int64_t H = c.hidden_size, I = c.intermediate_size, KV = m->kv_dim, V = c.vocab_size;
+  // config.expectedTensors / checkAgainst (src/core/config.js:88-150), tied embeddings
+  std::vector<std::pair<std::string, std::vector<int64_t>>> want;
+  want.push_back({"model.embed_tokens.weight", {V, H}});
+  want.push_back({"model.norm.weight", {H}});
+  for (int l = 0; l < c.num_layers; l++) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    want.push_back({p + "input_layernorm.weight", {H}});
+    want.push_back({p + "post_attention_layernorm.weight", {H}});
+    want.push_back({p + "self_attn.q_proj.weight", {H, H}});
+    want.push_back({p + "self_attn.q_proj.bias", {H}});
+    want.push_back({p + "self_attn.k_proj.weight", {KV, H}});
+    want.push_back({p + "self_attn.k_proj.bias", {KV}});
+    want.push_back({p + "self_attn.v_proj.weight", {KV, H}});
+    want.push_back({p + "self_attn.v_proj.bias", {KV}});
+    want.push_back({p + "self_attn.o_proj.weight", {H, H}});
+    want.push_back({p + "mlp.gate_proj.weight", {I, H}});
+    want.push_back({p + "mlp.up_proj.weight", {I, H}});
+    want.push_back({p + "mlp.down_proj.weight", {H, I}});
+  }
+  std::vector<std::string> problems;
+  for (const auto& e : want) {
+    int64_t shape[8];
+    int nd = 0;
+    if (b2a_safetensors_info(st, e.first.c_str(), nullptr, shape, 8, &nd, nullptr) != B2A_OK) {
+      problems.push_back("missing " + e.first);
+      continue;
+    }
+    const std::vector<int64_t> got(shape, shape + std::min(nd, 8));
+    if (got != e.second) {
+      problems.push_back(e.first + ": expected shape [" + shape_text(e.second) + "], file has [" + shape_text(got) +
+                         "]");
+    }
+  }
+  for (int i = 0; i < b2a_safetensors_count(st); i++) {
+    const std::string name = b2a_safetensors_name(st, i);
+    bool known = false;
+    for (const auto& e : want) known |= e.first == name;
+    if (!known) problems.push_back("unexpected tensor " + name);
+  }
+  if (!problems.empty()) {
+    std::string msg = "weights do not match config (" + std::to_string(problems.size()) + " problem" +
+                      (problems.size() == 1 ? "" : "s") + "):";
+    for (size_t k = 0; k < problems.size() && k < 10; k++) msg += "\n  " + problems[k];
+    if (problems.size() > 10) msg += "\n  ... and " + std::to_string(problems.size() - 10) + " more";
+    return fail(B2A_EINVAL, "%s", msg.c_str());
+  }
+
+  const int64_t Q = m->qkv_rows;
+  const size_t ss = m->ssz;
+  std::vector<float> f, s32;
+  b2a_status s;
+  for (int l = 0; l < c.num_layers; l++) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    std::vector<int8_t> qkv(Q * H), o(H * H), gate(I * H), up(I * H), down(H * I);
+    std::vector<unsigned char> sqkv(Q * ss), so(H * ss), sg(I * ss), su(I * ss), sd(H * ss);
+    std::vector<float> bias(Q), nin(H), npost(H);
+    if ((s = quantize_rows(m, st, (p + "self_attn.q_proj.weight").c_str(), 0, H, H, qkv.data(), sqkv.data(), f, s32)) ||
+        (s = quantize_rows(m, st, (p + "self_attn.k_proj.weight").c_str(), 0, KV, H, qkv.data() + H * H,
+                           sqkv.data() + H * ss, f, s32)) ||
+        (s = quantize_rows(m, st, (p + "self_attn.v_proj.weight").c_str(), 0, KV, H, qkv.data() + (H + KV) * H,
+                           sqkv.data() + (H + KV) * ss, f, s32)) ||
+        (s = quantize_rows(m, st, (p + "self_attn.o_proj.weight").c_str(), 0, H, H, o.data(), so.data(), f, s32)) ||
+        (s = quantize_rows(m, st, (p + "mlp.gate_proj.weight").c_str(), 0, I, H, gate.data(), sg.data(), f, s32)) ||
+        (s = quantize_rows(m, st, (p + "mlp.up_proj.weight").c_str(), 0, I, H, up.data(), su.data(), f, s32)) ||
+        (s = quantize_rows(m, st, (p + "mlp.down_proj.weight").c_str(), 0, H, I, down.data(), sd.data(), f, s32)) ||
+        (s = read_vector(st, p + "self_attn.q_proj.bias", bias.data(), H)) ||
+        (s = read_vector(st, p + "self_attn.k_proj.bias", bias.data() + H, KV)) ||
+        (s = read_vector(st, p + "self_attn.v_proj.bias", bias.data() + H + KV, KV)) ||
+        (s = read_vector(st, p + "input_layernorm.weight", nin.data(), H)) ||
+        (s = read_vector(st, p + "post_attention_layernorm.weight", npost.data(), H))) {
+      return s;
+    }
+    b2a_layer_weights w{nin.data(), npost.data(), qkv.data(), sqkv.data(), bias.data(), o.data(), so.data(),
+                        gate.data(), sg.data(), up.data(), su.data(), down.data(), sd.data()};
+    if ((s = b2a_model_load_layer(m, l, &w, B2A_HOST)) != B2A_OK) return s;
+  }
+  // the embedding in blocks of rows (272 MB of bfloat16 for Qwen2.5-0.5B)
+  std::vector<int8_t> ecodes(V * H);
+  std::vector<unsigned char> escales(V * ss);
+  constexpr int64_t kBlock = 8192;
+  for (int64_t r = 0; r < V; r += kBlock) {
+    const int rows = static_cast<int>(std::min(kBlock, V - r));
+    if ((s = quantize_rows(m, st, "model.embed_tokens.weight", r, rows, static_cast<int>(H), ecodes.data() + r * H,
+                           escales.data() + r * ss, f, s32)) != B2A_OK) {
+      return s;
+    }
+  }
+  if ((s = b2a_model_load_embedding(m, ecodes.data(), escales.data(), B2A_HOST)) != B2A_OK) return s;
+  std::vector<float> fin(H);
+  if ((s = read_vector(st, "model.norm.weight", fin.data(), H)) != B2A_OK) return s;
+  return b2a_model_load_final_norm(m, fin.data(), B2A_HOST);
+}
