@@ -738,6 +738,36 @@ def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
                                 "launches_per_step": sum(x[0] for x in kt.values()) / steps}
         cache.close()
         rope.close()
+    # many short prompts at once (b2a_attention_prefill_batch): config 2's S=512 for 32
+    # sequences in one call, the way a server fills the GPU with short prefills
+    nseq, S = 32, 512
+    with torch.cuda.stream(stream):
+        cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(1, KVH, D, H), S, batch=nseq, dtype=args.prefill_cache)
+        rope = b2a.RopeTable(ctx, D, THETA, S)
+        q = torch.randn(nseq, S, H, D, device=dev).bfloat16()
+        k = torch.randn(nseq, S, KVH, D, device=dev).bfloat16()
+        v = torch.randn(nseq, S, KVH, D, device=dev).bfloat16()
+        o = torch.empty(nseq, S, H, D, device=dev, dtype=torch.bfloat16)
+    flops = nseq * 4 * D * H * S * (S + 1) / 2
+    for _ in range(3):
+        b2a.attentionPrefillBatch(ctx, cache, rope, 0, q, k, v, o, S, H, 0, nseq)
+    evs = []
+    for _ in range(20):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        b2a.attentionPrefillBatch(ctx, cache, rope, 0, q, k, v, o, S, H, 0, nseq)
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    res["batched"] = {"sequences": nseq, "seq": S, "ms": round(ms, 4),
+                      "tflops": round(flops / (ms / 1e3) / 1e12, 3),
+                      "frac": round(flops / (ms / 1e3) / 1e12 / pk["bf16_tflops"], 4),
+                      "call": "b2a_attention_prefill_batch (one append launch, one attention launch)"}
+    cache.close()
+    rope.close()
     main = res["sweep"].get("512") or next(iter(res["sweep"].values()))
     res["value"] = main["tflops"]
     res["config"] = {"workload": "config2-causal-prefill", "seq": 512, "heads": "14q/2kv", "head_dim": D,

@@ -195,6 +195,19 @@ b2a_status b2a_attention_prefill(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rop
                                  const void* q, const void* k, const void* v, b2a_dtype in_dtype,
                                  int count, void* out, b2a_dtype out_dtype, int flags);
 
+/* The prefill of `nseq` sequences (seq_begin, seq_begin+1, ...) in one call,
+ * `count` new tokens each at that sequence's own cache length: q
+ * [nseq][count][num_heads][head_dim], k and v [nseq][count][num_kv_heads][head_dim],
+ * out [nseq][count][num_heads][head_dim]; the same arithmetic as nseq calls of
+ * b2a_attention_prefill, in one append launch and one attention launch (many
+ * short prompts fill the GPU together; no reference counterpart, the reference
+ * runs one sequence at a time). Every sequence is checked as
+ * b2a_attention_prefill checks it. */
+b2a_status b2a_attention_prefill_batch(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope, int layer,
+                                       int seq_begin, int nseq, int num_heads, const void* q, const void* k,
+                                       const void* v, b2a_dtype in_dtype, int count, void* out, b2a_dtype out_dtype,
+                                       int flags);
+
 /* ---- the literal drop-in for groupedAttention (src/core/attention.js:32) ---
  * Same arguments and layouts as the JS: q [seq][num_heads*head_dim], keys and
  * values [past+seq][num_kv_heads*head_dim], out [seq][num_heads*head_dim], all

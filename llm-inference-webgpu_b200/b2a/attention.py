@@ -101,6 +101,20 @@ def attentionPrefill(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: in
                                        va.ptr, DTYPES[in_dt], count, oa.ptr, DTYPES[oa.dtype], _where(qa, ka, va, oa)))
 
 
+def attentionPrefillBatch(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k, v, out, count: int,
+                          numHeads: int, seqBegin: int, numSeqs: int, dtype: str | None = None,
+                          out_dtype: str | None = None) -> None:
+    """attentionPrefill for numSeqs sequences in one call (b2a_attention_prefill_batch): q/out
+    [numSeqs, count, numHeads, headDim], k/v [numSeqs, count, numKVHeads, headDim], each sequence
+    at its own cache length."""
+    qa, ka, va = _arg(q, dtype), _arg(k, dtype), _arg(v, dtype)
+    oa = _arg(out, out_dtype or dtype, writable=True)
+    in_dt = _same_dtype(qa, ka, va)
+    check(load().b2a_attention_prefill_batch(ctx.handle, cache.handle, rope.handle, layer, seqBegin, numSeqs,
+                                             numHeads, qa.ptr, ka.ptr, va.ptr, DTYPES[in_dt], count, oa.ptr,
+                                             DTYPES[oa.dtype], _where(qa, ka, va, oa)))
+
+
 def decodePartial(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, q_positions,
                   partial, numHeads: int, dtype: str | None = None) -> None:
     """Split-KV partial over this cache's positions (see b2a_attention_decode_partial).

@@ -1304,12 +1304,13 @@ namespace b2a {
 
 b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx,
                                int num_heads, const void* q, const void* k, const void* v, b2a_dtype in_dtype,
-                               int count, void* dout, b2a_dtype out_dtype) {
+                               int count, void* dout, b2a_dtype out_dtype, int nseq) {
   b2a_status s;
-  const int past = c->len[seq_idx];
+  int past = 0;   // the longest past among the call's sequences
+  for (int b = 0; b < nseq; b++) past = std::max(past, c->len[seq_idx + b]);
   AttnParams p = base_params(ctx, c, rope);
   p.seq_begin = seq_idx;
-  p.batch = 1;
+  p.batch = nseq;
   p.num_layers = 1;
   p.layer_begin = layer;
   p.tokens = count;
@@ -1325,7 +1326,7 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
   cudaError_t e;
   {
     KernelTimer kt(ctx, K_ROPE_APPEND);
-    e = launch_rope_append(p, seq_idx, count, ctx->stream);
+    e = launch_rope_append(p, seq_idx, count, ctx->stream, nseq);
   }
   if (e != cudaSuccess) return cuda_fail(e, "launching the rope append");
   p.k_new = nullptr;
@@ -1334,7 +1335,7 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
     p.tmap_k = &c->tmap_k;
     p.tmap_v = &c->tmap_v;
   }
-  if (prefill_pair_supported(p) && prefill_tiles_per_cta(ctx, count, num_heads) == 2) {
+  if (prefill_pair_supported(p) && prefill_tiles_per_cta(ctx, count, num_heads * nseq) == 2) {
     // tensor-core causal attention, two heads' 128-query tiles per CTA (f16 cache)
     {
       KernelTimer kt(ctx, K_PREFILL_PAIR);
@@ -1357,6 +1358,55 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
 }  // namespace b2a
 
 extern "C" {
+
+b2a_status b2a_attention_prefill_batch(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_begin,
+                                       int nseq, int num_heads, const void* q, const void* k, const void* v,
+                                       b2a_dtype in_dtype, int count, void* out, b2a_dtype out_dtype, int flags) {
+  b2a_status s = check_cache_shape(c, rope, num_heads);
+  if (s != B2A_OK) return s;
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  if (nseq < 1 || seq_begin < 0 || seq_begin + nseq > c->batch) {
+    return fail(B2A_EINVAL, "sequences [%d, %d) out of range [0, %d)", seq_begin, seq_begin + nseq, c->batch);
+  }
+  if (count < 1) return fail(B2A_EINVAL, "forward: need at least one token");
+  for (int b = seq_begin; b < seq_begin + nseq; b++) {
+    const int past = c->len[b];
+    // src/gpu/model.js:249-254, per sequence
+    if (static_cast<int64_t>(past) + count > c->capacity) {
+      return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", past, c->capacity, count);
+    }
+    if (static_cast<int64_t>(past) + count > rope->max_positions) {
+      return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", past + count, rope->max_positions);
+    }
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  const size_t ies = dtype_size(in_dtype);
+  const size_t q_bytes = static_cast<size_t>(nseq) * count * num_heads * c->head_dim * ies;
+  const size_t kv_bytes = static_cast<size_t>(nseq) * count * c->kv_heads * c->head_dim * ies;
+  const size_t out_bytes = static_cast<size_t>(nseq) * count * num_heads * c->head_dim * dtype_size(out_dtype);
+  void* dout = out;
+  if (flags == B2A_HOST) {
+    Stage st;
+    int iq = st.add(q_bytes), ik = st.add(kv_bytes), iv = st.add(kv_bytes), io = st.add(out_bytes);
+    if ((s = ensure_buffer(&ctx->d_stage, &ctx->d_stage_bytes, st.total, "allocating staging")) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iq), q, q_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, ik), k, kv_bytes)) != B2A_OK) return s;
+    if ((s = h2d(ctx, st.ptr(ctx, iv), v, kv_bytes)) != B2A_OK) return s;
+    q = st.ptr(ctx, iq);
+    k = st.ptr(ctx, ik);
+    v = st.ptr(ctx, iv);
+    dout = st.ptr(ctx, io);
+  }
+  if ((s = attn_prefill_device(ctx, c, rope, layer, seq_begin, num_heads, q, k, v, in_dtype, count, dout, out_dtype,
+                               nseq)) != B2A_OK) {
+    return s;
+  }
+  if (flags == B2A_HOST) return d2h_sync(ctx, out, dout, out_bytes);
+  return B2A_OK;
+}
 
 // ----------------------------------------------------- groupedAttention drop-in --
 

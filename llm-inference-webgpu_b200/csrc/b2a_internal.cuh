@@ -200,7 +200,9 @@ __host__ __device__ inline int len_of(const AttnParams& p, int b) {
   return b < p.n_len_inline ? p.len_inline[b] : p.len[p.seq_begin + b];
 }
 
-cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st);
+// RoPE(k) + append of `count` new keys/values for each of nseq sequences from seq_idx
+// (k_new/v_new [nseq][count][kv_heads][D]) at each sequence's length
+cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st, int nseq = 1);
 cudaError_t launch_write_at(const b2a_kvcache* c, int layer, int seq_idx, int at, const void* k,
                             const void* v, int src_dtype, int count, cudaStream_t st);
 cudaError_t launch_read(const b2a_kvcache* c, int layer, int seq_idx, int n, void* k_out, void* v_out,
@@ -295,7 +297,7 @@ b2a_status attn_decode_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope
                               b2a_dtype out_dtype);
 b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int seq_idx,
                                int num_heads, const void* q, const void* k, const void* v, b2a_dtype in_dtype,
-                               int count, void* out, b2a_dtype out_dtype);
+                               int count, void* out, b2a_dtype out_dtype, int nseq = 1);
 // safetensors helpers (weights.cu): a byte range of one tensor, and the
 // widening of n stored elements of dtype dt to f32 (false: not widenable)
 b2a_status st_read_range(const b2a_safetensors* st, const char* name, uint64_t offset, uint64_t length, void* dst);

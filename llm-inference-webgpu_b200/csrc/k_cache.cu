@@ -8,20 +8,23 @@ namespace b2a {
 // src/cpu/model.js:103-116 (rope-k at absolute position past+t, then
 // kv.writeAt), src/gpu/model.js:327-338 (ROPE on k, two copies). One thread
 // per rotation pair (t, kv head, j); the same thread stores both halves of V.
-__global__ void k_rope_append(AttnParams p, int seq_idx, int count) {
+__global__ void k_rope_append(AttnParams p, int seq_first, int count, int nseq) {
   // a kernel launched after this one as a programmatic dependent may start its
   // prologue now; it waits for this grid before reading the cache
   asm volatile("griddepcontrol.launch_dependents;");
   const int half = p.head_dim >> 1;
-  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * half;
-  const int past = p.len[seq_idx];
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * half;   // per sequence
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n * nseq;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int j = static_cast<int>(i % half);
-    const int g = static_cast<int>((i / half) % p.kv_heads);
-    const int t = static_cast<int>(i / (static_cast<int64_t>(half) * p.kv_heads));
+    const int b = static_cast<int>(i / n);
+    const int64_t ib = i - b * n;
+    const int seq_idx = seq_first + b;
+    const int past = p.len[seq_idx];
+    const int j = static_cast<int>(ib % half);
+    const int g = static_cast<int>((ib / half) % p.kv_heads);
+    const int t = static_cast<int>(ib / (static_cast<int64_t>(half) * p.kv_heads));
     const int pos = past + t;
-    const int64_t src = (static_cast<int64_t>(t) * p.kv_heads + g) * p.head_dim;
+    const int64_t src = ((static_cast<int64_t>(b) * count + t) * p.kv_heads + g) * p.head_dim;
     const int64_t dst = seq_idx * p.s_seq + static_cast<int64_t>(p.layer_begin) * p.s_layer +
                         g * p.s_head + static_cast<int64_t>(pos) * p.head_dim;
     const double c = p.rope_cos[static_cast<int64_t>(pos) * half + j];
@@ -36,12 +39,12 @@ __global__ void k_rope_append(AttnParams p, int seq_idx, int count) {
   }
 }
 
-cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st) {
-  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * (p.head_dim / 2);
+cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st, int nseq) {
+  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * (p.head_dim / 2) * nseq;
   if (n == 0) return cudaSuccess;
   const int threads = 256;
   const int blocks = static_cast<int>((n + threads - 1) / threads < 4096 ? (n + threads - 1) / threads : 4096);
-  k_rope_append<<<blocks, threads, 0, st>>>(p, seq_idx, count);
+  k_rope_append<<<blocks, threads, 0, st>>>(p, seq_idx, count, nseq);
   return cudaGetLastError();
 }
 

@@ -96,7 +96,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int first = 2 * (blockIdx.y % pairs);                    // first head of the pair within its group
   const int h0 = g * p.group + first;
   const int ntile = first + 1 < p.group ? 2 : 1;
-  const int bc = p.seq_begin;
+  const int sb = blockIdx.z;                                    // sequence of a batched call
+  const int bc = p.seq_begin + sb;
   const int past = p.len[bc];
   const int q0 = qt * kBM;
   const int q_last = min(q0 + kBM, p.tokens) - 1;               // last valid query of this tile
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       float x[kD], cs[kD / 2], sn[kD / 2];
       if (t < p.tokens) {
-        const int64_t qrow = (static_cast<int64_t>(t) * p.heads + h) * kD;
+        const int64_t qrow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;
         const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos32 + static_cast<int64_t>(a) * (kD / 2));
         const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin32 + static_cast<int64_t>(a) * (kD / 2));
         if (p.in_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0) {
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_wait_ld();
     if (t < p.tokens) {
       const float inv = 1.f / l;
-      const int64_t orow = (static_cast<int64_t>(t) * p.heads + h) * kD;
+      const int64_t orow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;
       void* out = p.partial;       // the output pointer travels in the partial slot for this kernel
       const int odt = p.nchunks;   // and its dtype in nchunks
       if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) {
@@ -446,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 bool prefill_pair_supported(const AttnParams& p) {
-  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch == 1 && p.num_layers == 1 && p.head_dim == kD &&
+  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch >= 1 && p.num_layers == 1 && p.head_dim == kD &&
          p.k_new == nullptr && p.cache_dtype == DT_F16 && p.group >= 1;
 }
 
@@ -457,7 +458,7 @@ cudaError_t launch_prefill_pair(const AttnParams& p, void* out, int out_dtype, c
   q.partial = static_cast<float*>(out);
   q.nchunks = out_dtype;
   const int pairs = (p.group + 1) / 2;
-  const dim3 grid((p.tokens + kBM - 1) / kBM, p.kv_heads * pairs);
+  const dim3 grid((p.tokens + kBM - 1) / kBM, p.kv_heads * pairs, p.batch);
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr[64] = {};

@@ -114,7 +114,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int qt = n_qtiles - 1 - static_cast<int>(blockIdx.x);   // heaviest (latest) tiles first
   const int h = blockIdx.y;
   const int g = h / p.group;
-  const int bc = p.seq_begin;
+  const int sb = blockIdx.z;                                    // sequence of a batched call
+  const int bc = p.seq_begin + sb;
   const int past = p.len[bc];
   const int q0 = qt * kBM;
   const int q_last = min(q0 + kBM, p.tokens) - 1;               // last valid query of this tile
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       float x[kD], cs[kD / 2], sn[kD / 2];
       if (t < p.tokens) {
-        const int64_t qrow = (static_cast<int64_t>(t) * p.heads + h) * kD;
+        const int64_t qrow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;
         const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos32 + static_cast<int64_t>(a) * (kD / 2));
         const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin32 + static_cast<int64_t>(a) * (kD / 2));
         if (p.in_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0) {
@@ -420,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_wait_ld();
     if (t < p.tokens) {
       const float inv = 1.f / l;
-      const int64_t orow = (static_cast<int64_t>(t) * p.heads + h) * kD;
+      const int64_t orow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;
       void* out = p.partial;   // the output pointer travels in the partial slot for this kernel
       const int odt = p.nchunks;   // and its dtype in nchunks
       if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) {
@@ -465,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 bool prefill_tc_supported(const AttnParams& p) {
-  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch == 1 && p.num_layers == 1 && p.head_dim == kD &&
+  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch >= 1 && p.num_layers == 1 && p.head_dim == kD &&
          p.k_new == nullptr && (p.cache_dtype == DT_F16 || p.cache_dtype == DT_BF16);
 }
 
@@ -475,7 +476,7 @@ cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cud
   AttnParams q = p;
   q.partial = static_cast<float*>(out);
   q.nchunks = out_dtype;
-  const dim3 grid((p.tokens + kBM - 1) / kBM, p.heads);
+  const dim3 grid((p.tokens + kBM - 1) / kBM, p.heads, p.batch);
   const CUtensorMap* mk = static_cast<const CUtensorMap*>(p.tmap_k);
   const CUtensorMap* mv = static_cast<const CUtensorMap*>(p.tmap_v);
   int dev = 0;

@@ -1,0 +1,98 @@
+"""Batched prefill (b2a_attention_prefill_batch): several sequences, each at its
+own cache length, in one append launch and one attention launch.
+
+It must give what one b2a_attention_prefill call per sequence gives: the same
+bits on the tensor-core paths (the same kernels, a sequence index more), the
+same cache contents, and the oracle's causal attention (src/cpu/model.js:103-123)
+within the attention tolerance.
+"""
+import numpy as np
+import pytest
+
+import b2a
+from helpers import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+H, KVH, D, THETA = 14, 2, 64, 1e6
+PASTS = [0, 37, 130]
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = b2a.Context(0)
+    yield c
+    c.close()
+
+
+@pytest.fixture(scope="module")
+def rope(ctx):
+    return b2a.RopeTable(ctx, D, THETA, 4096)
+
+
+def _cache(ctx, oracle, dtype, count):
+    """4 sequences; sequences 1..3 hold PASTS[b] cached positions."""
+    c = b2a.GpuKVCache(ctx, b2a.CacheConfig(numLayers=2, numKVHeads=KVH, headDim=D, numHeads=H),
+                       max(PASTS) + count, batch=4, dtype=dtype)
+    lens = [0] + PASTS
+    hk, hv = {}, {}
+    for b, L in enumerate(lens):
+        if L == 0:
+            continue
+        kk = oracle.normal_array(L * KVH * D, 500 + b)
+        vv = oracle.normal_array(L * KVH * D, 600 + b)
+        c.writeAt(1, 0, kk, vv, L, seq=b)
+        hk[b], hv[b] = oracle.round_to(kk, dtype), oracle.round_to(vv, dtype)
+    c.setLengths(lens)
+    return c, hk, hv
+
+
+@pytest.mark.parametrize("cache_dtype,tiles", [("f16", "2"), ("f16", "1"), ("bf16", "1"), ("f32", "1")])
+def test_batched_prefill_equals_one_call_per_sequence(ctx, rope, oracle, monkeypatch, cache_dtype, tiles):
+    monkeypatch.setenv("B2A_PREFILL_TILES", tiles)
+    count, nseq = 70, len(PASTS)
+    q = oracle.round_to(oracle.normal_array(nseq * count * H * D, 71), "f16").reshape(nseq, count, H * D)
+    k = oracle.round_to(oracle.normal_array(nseq * count * KVH * D, 72), "f16").reshape(nseq, count, KVH * D)
+    v = oracle.round_to(oracle.normal_array(nseq * count * KVH * D, 73), "f16").reshape(nseq, count, KVH * D)
+    bits = lambda x: oracle.to_bits(x, "f16")  # noqa: E731
+    cb, hk, hv = _cache(ctx, oracle, cache_dtype, count)
+    cs, _, _ = _cache(ctx, oracle, cache_dtype, count)
+    ob = np.empty((nseq, count, H * D), np.float32)
+    b2a.attentionPrefillBatch(ctx, cb, rope, 1, bits(q), bits(k), bits(v), ob, count, H, 1, nseq, dtype="f16",
+                              out_dtype="f32")
+    os_ = np.empty_like(ob)
+    for i in range(nseq):
+        b2a.attentionPrefill(ctx, cs, rope, 1, bits(q[i]), bits(k[i]), bits(v[i]), os_[i], count, H, seq=1 + i,
+                             dtype="f16", out_dtype="f32")
+    if cache_dtype != "f32":
+        assert np.array_equal(ob, os_)
+    else:   # the CUDA-core path may chunk the keys differently for one sequence and for three
+        assert_parity(ob.reshape(-1), os_.reshape(-1), "f32", "batched vs single (f32 cache)")
+    for i, past in enumerate(PASTS):
+        kb, vb = cb.read(1, past + count, seq=1 + i)
+        ks, vs = cs.read(1, past + count, seq=1 + i)
+        assert np.array_equal(kb, ks) and np.array_equal(vb, vs)
+        # the oracle: RoPE at past..past+count-1, causal over the cached and new keys
+        qr = oracle.rope_rows(q[i], range(past, past + count), D, THETA).reshape(-1)
+        kr = oracle.round_to(oracle.rope_rows(k[i], range(past, past + count), D, THETA), cache_dtype)
+        keys = np.concatenate([hk[1 + i].reshape(past, KVH * D), kr]) if past else kr
+        vals = np.concatenate([hv[1 + i].reshape(past, KVH * D), oracle.round_to(v[i], cache_dtype)]) if past else \
+            oracle.round_to(v[i], cache_dtype)
+        ref = oracle.grouped_attention(qr, keys.reshape(-1), vals.reshape(-1), count, past, H, KVH, D)
+        assert_parity(ob[i].reshape(-1), ref, "f32", f"{cache_dtype} batched prefill, sequence {i}")
+    # the untouched sequence 0 and layer 0 stay as they were
+    assert cb.lengthOf(0) == 0
+    cb.close()
+    cs.close()
+
+
+def test_batched_prefill_checks_every_sequence(ctx, rope, oracle):
+    c, _, _ = _cache(ctx, oracle, "f16", 8)
+    q = np.zeros((3, 20, H * D), np.uint16)
+    k = np.zeros((3, 20, KVH * D), np.uint16)
+    o = np.zeros((3, 20, H * D), np.float32)
+    with pytest.raises(b2a.RangeError, match="cannot add 20 more"):
+        b2a.attentionPrefillBatch(ctx, c, rope, 1, q, k, k, o, 20, H, 1, 3, dtype="f16", out_dtype="f32")
+    with pytest.raises(b2a.B2AError, match="out of range"):
+        b2a.attentionPrefillBatch(ctx, c, rope, 1, q, k, k, o, 8, H, 2, 3, dtype="f16", out_dtype="f32")
+    c.close()
