@@ -657,7 +657,8 @@ def bench_generation(torch, b2a, ctx, stream, dev, peak_gbs, args) -> dict:
         "decode_path": model.decode_path,
         "roofline": {"bound": "hbm", "kernel": "decode_step", "achieved": round(achieved, 1) if achieved else None,
                      "peak": peak_gbs, "unit": "GB/s", "frac": round(achieved / peak_gbs, 3) if achieved else None,
-                     "traffic": None, "bytes_per_token": int(token_bytes)},
+                     "traffic": ncu_traffic("decode_step", "config4-generation-ctx64"),
+                     "traffic_note": "one launch at context 64 (ncu)", "bytes_per_token": int(token_bytes)},
         "kernels_ms": {k: round(v[1], 3) for k, v in kt.items()},
         "gpu_launches_per_generation": int(sum(v[0] for v in kt.values())),
         "tokens_head": [int(t) for t in toks[:8]],
