@@ -339,6 +339,9 @@ def run_ours(args) -> None:
     if clocks:
         line["clocks"] = clocks.summary(t_wall0, t_wall1)
 
+    if world == 1 and not args.no_paged:
+        line["paged"] = bench_paged(torch, b2a, ctx, stream, dev, rope, lengths, nb, q, kn, vn, out, ms_max / args.steps,
+                                    args)
     if not args.no_splitkv:
         line["split_kv"] = bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args)
     if world == 1 and not args.no_prefill:
@@ -363,6 +366,62 @@ def run_ours(args) -> None:
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def bench_paged(torch, b2a, ctx, stream, dev, rope, lengths, nb, q, kn, vn, out, contiguous_ms, args,
+                page_size: int = 256) -> dict:
+    """The config-3 decode step over a paged cache (b2a_kvcache_create_paged): the same 64
+    sequences, lengths and inputs, the pool sized for the positions they hold. Pages are
+    mapped in rounds of one page per sequence, so each sequence's pages are spread over
+    the pool as they would be after interleaved growth."""
+    pages = int(sum(-(-(int(L) + 1) // page_size) for L in lengths))
+    with torch.cuda.stream(stream):
+        pc = b2a.GpuKVCache(ctx, b2a.CacheConfig(LAYERS, KVH, D, H), CAP, batch=SEQS, dtype="f16",
+                            pageSize=page_size, numPages=pages)
+        kp, vp, _ = pc.pools()
+        shape = ((pages + 1) * LAYERS * KVH * page_size, D)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(99)
+        torch.as_tensor(_CAI(kp, shape, "<f2"), device=dev).normal_(generator=gen)
+        torch.as_tensor(_CAI(vp, shape, "<f2"), device=dev).normal_(generator=gen)
+    torch.cuda.synchronize(dev)
+    target = np.asarray(lengths, np.int64) + 1   # the new token's slot too
+    r = 1
+    while True:
+        pc.setLengths(np.minimum(target, r * page_size).astype(np.int32))
+        if r * page_size >= target.max():
+            break
+        r += 1
+    pc.setLengths(np.asarray(lengths, np.int32))
+    assert pc.freePages == 0
+
+    def step():
+        b2a.attentionDecode(ctx, pc, rope, 0, q, kn, vn, out, H, numLayers=LAYERS)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(3, min(args.steps, 500))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    ctx.enable_timing(True)
+    for _ in range(10):
+        step()
+    kt = ctx.read_timing()
+    ctx.enable_timing(False)
+    pool_bytes = pc.byteLength
+    contiguous_bytes = 2 * SEQS * LAYERS * KVH * CAP * D * 2
+    res = {"page_size": page_size, "pages": pages, "value": round(nb["step"] / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+           "ms_per_step": round(ms, 4), "contiguous_ms_per_step": round(contiguous_ms, 4),
+           "pool_bytes": pool_bytes, "contiguous_cache_bytes": contiguous_bytes,
+           "kernels": {k: {"launches": v[0], "avg_ms": round(v[1] / v[0], 4)} for k, v in kt.items()}}
+    pc.close()
+    return res
 
 
 def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict:
@@ -844,6 +903,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-splitkv", action="store_true")
+    ap.add_argument("--no-paged", action="store_true", help="skip the config-3 decode over a paged cache")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-layer", action="store_true", help="skip the attention-block (projections) measurement")
     ap.add_argument("--no-generation", action="store_true", help="skip the config-4 generation measurement")

@@ -139,6 +139,48 @@ b2a_status b2a_kvcache_write_at(b2a_ctx* ctx, b2a_kvcache* cache, int layer, int
 b2a_status b2a_kvcache_read(b2a_ctx* ctx, const b2a_kvcache* cache, int layer, int seq_idx, int n,
                             void* keys_out, void* values_out, int flags);
 
+/* ---- paged KV cache --------------------------------------------------------
+ * The same cache object and operations, the storage split into pages: the pools
+ * hold num_pages pages of page_size positions (plus one scratch page), each page
+ * [num_layers][num_kv_heads][page_size][head_dim], and every sequence has a
+ * page table mapping position p to page table[p / page_size], row p % page_size.
+ * Sequences take pages from the shared pool as they grow (allocate, commit,
+ * set_lengths, write_at, append and the attention calls that append) and give
+ * them back on reset, so a batch of sequences of very different lengths needs
+ * pool memory for the positions it holds, not batch x capacity. capacity stays
+ * the per-sequence bound of the reference's KVCache (cache.js:24-26, 53-58).
+ * page_size: a power of two, at least 128 (a 128-position tile of the attention
+ * kernels never crosses a page). When the pool cannot back a call's new
+ * positions the call fails with B2A_ERANGE "page pool exhausted: U of N pages in
+ * use; sequence S needs K more" and no page of that call is taken. Pages of
+ * positions beyond a sequence's mapped pages read as zeros. */
+b2a_status b2a_kvcache_create_paged(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim,
+                                    int capacity, int batch, b2a_dtype dtype, int page_size,
+                                    int num_pages, b2a_kvcache** out);
+/* The pages of sequence seq_idx in position order (up to max_entries of them)
+ * and how many are mapped. For a paged cache b2a_kvcache_pools' strides[0] is
+ * the page stride: element (layer, h, p) of the sequence is at
+ * pages[p / page_size]*strides[0] + layer*strides[1] + h*strides[2] + (p % page_size)*strides[3].
+ * A contiguous cache reports no pages (*mapped = 0). */
+b2a_status b2a_kvcache_page_table(const b2a_kvcache* cache, int seq_idx, int32_t* pages_out, int max_entries,
+                                  int* mapped);
+/* Pages of the pool not held by any sequence (0 for a contiguous cache). */
+b2a_status b2a_kvcache_free_pages(const b2a_kvcache* cache, int* free_pages);
+
+/* The host page allocator of a paged cache, on its own (no device memory): it
+ * keeps the page tables and the free pages. reserve maps pages until positions
+ * [0, positions) of the sequence are backed (all or nothing); release returns a
+ * sequence's pages (seq_idx -1: every sequence); the next reserve takes the most
+ * recently released page first. */
+typedef struct b2a_pagepool b2a_pagepool;
+b2a_status b2a_pagepool_create(int num_pages, int page_size, int batch, int capacity, b2a_pagepool** out);
+b2a_status b2a_pagepool_destroy(b2a_pagepool* pool);
+b2a_status b2a_pagepool_reserve(b2a_pagepool* pool, int seq_idx, int positions);
+b2a_status b2a_pagepool_release(b2a_pagepool* pool, int seq_idx);
+b2a_status b2a_pagepool_table(const b2a_pagepool* pool, int seq_idx, int32_t* pages_out, int max_entries,
+                              int* mapped);
+b2a_status b2a_pagepool_free_pages(const b2a_pagepool* pool, int* free_pages);
+
 /* ---- fused RoPE(K) + round + append (src/cpu/model.js:103-116; src/gpu/model.js:327-338) */
 /* For sequence seq_idx with length L: rotate each KV head of k[t] at absolute
  * position L+t, round to the cache dtype and store it, and store v[t], at

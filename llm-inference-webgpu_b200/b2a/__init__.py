@@ -12,4 +12,4 @@ from .attention import (appendRope, attentionDecode, attentionPrefill, attention
                         quantizeInt8PerChannel, ropeFrequencies, ropeTables)
 from .model import Model, ModelConfig  # noqa: F401
 from .weights import Safetensors, TensorInfo, write_safetensors  # noqa: F401
-from .runtime import CacheConfig, Context, Exchange, GpuKVCache, RopeTable  # noqa: F401
+from .runtime import CacheConfig, Context, Exchange, GpuKVCache, PagePool, RopeTable  # noqa: F401

@@ -48,6 +48,15 @@ SIGNATURES = {
     "b2a_kvcache_pools": (_i, [_vp, _pp, _pp, _i64p]),
     "b2a_kvcache_write_at": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i]),
     "b2a_kvcache_read": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp, _i]),
+    "b2a_kvcache_create_paged": (_i, [_vp, _i, _i, _i, _i, _i, _i, _i, _i, _pp]),
+    "b2a_kvcache_page_table": (_i, [_vp, _i, _i32p, _i, _ip]),
+    "b2a_kvcache_free_pages": (_i, [_vp, _ip]),
+    "b2a_pagepool_create": (_i, [_i, _i, _i, _i, _pp]),
+    "b2a_pagepool_destroy": (_i, [_vp]),
+    "b2a_pagepool_reserve": (_i, [_vp, _i, _i]),
+    "b2a_pagepool_release": (_i, [_vp, _i]),
+    "b2a_pagepool_table": (_i, [_vp, _i, _i32p, _i, _ip]),
+    "b2a_pagepool_free_pages": (_i, [_vp, _ip]),
     "b2a_append_rope": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _i]),
     "b2a_attention_decode": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i]),
     "b2a_attention_decode_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i]),

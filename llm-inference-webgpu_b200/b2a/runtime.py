@@ -175,9 +175,15 @@ class CacheConfig:
 class GpuKVCache:
     """Device KV cache for `batch` sequences (GpuKVCache src/gpu/model.js:69-84 with the
     KVCache bookkeeping of src/cpu/cache.js:18-119). Storage is head-major per
-    sequence and layer, [kvHead][position][headDim] in `dtype`."""
+    sequence and layer, [kvHead][position][headDim] in `dtype`.
 
-    def __init__(self, ctx: Context, config, capacity, batch: int = 1, dtype: str = "f32"):
+    With pageSize (a power of two >= 128) the cache is paged: the sequences share a
+    pool of numPages pages of pageSize positions, taken as sequences grow and given
+    back on reset (b2a_kvcache_create_paged); capacity stays the per-sequence bound.
+    Every operation works on either layout."""
+
+    def __init__(self, ctx: Context, config, capacity, batch: int = 1, dtype: str = "f32",
+                 pageSize: int = 0, numPages: int = 0):
         if not isinstance(capacity, (int, np.integer)) or isinstance(capacity, bool):
             raise _lib.RangeError(_lib.B2A_ERANGE, f"cache capacity must be a positive integer, got {capacity}")
         self.ctx = ctx
@@ -185,11 +191,34 @@ class GpuKVCache:
         self.capacity = int(capacity)
         self.batch = batch
         self.dtype = dtype
+        self.pageSize = int(pageSize)
+        self.numPages = int(numPages)
         h = ctypes.c_void_p()
-        check(ctx._lib.b2a_kvcache_create(ctx.handle, config.numLayers, config.numKVHeads, config.headDim,
-                                          self.capacity, batch, DTYPES[dtype], ctypes.byref(h)))
+        if self.pageSize:
+            check(ctx._lib.b2a_kvcache_create_paged(ctx.handle, config.numLayers, config.numKVHeads, config.headDim,
+                                                    self.capacity, batch, DTYPES[dtype], self.pageSize,
+                                                    self.numPages, ctypes.byref(h)))
+        else:
+            check(ctx._lib.b2a_kvcache_create(ctx.handle, config.numLayers, config.numKVHeads, config.headDim,
+                                              self.capacity, batch, DTYPES[dtype], ctypes.byref(h)))
         self.handle = h
         ctx._children.add(self)
+
+    # -- pages (paged caches) --
+    def pageTable(self, seq: int = 0) -> np.ndarray:
+        """The pages backing sequence `seq`, in position order (empty when contiguous)."""
+        n = ctypes.c_int()
+        cap = (self.capacity + self.pageSize - 1) // self.pageSize if self.pageSize else 0
+        out = np.zeros(max(cap, 1), np.int32)
+        check(self.ctx._lib.b2a_kvcache_page_table(self.handle, seq, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                                   out.size, ctypes.byref(n)))
+        return out[:n.value].copy()
+
+    @property
+    def freePages(self) -> int:
+        n = ctypes.c_int()
+        check(self.ctx._lib.b2a_kvcache_free_pages(self.handle, ctypes.byref(n)))
+        return n.value
 
     def close(self) -> None:
         if getattr(self, "handle", None):
@@ -312,3 +341,45 @@ class Exchange:
             self.close()
         except Exception:
             pass
+
+
+class PagePool:
+    """The host page allocator of a paged cache on its own (b2a_pagepool_*): page
+    tables and free pages, no device memory."""
+
+    def __init__(self, numPages: int, pageSize: int, batch: int, capacity: int):
+        self._lib = _lib.load()
+        self.pageSize, self.capacity = pageSize, capacity
+        h = ctypes.c_void_p()
+        check(self._lib.b2a_pagepool_create(numPages, pageSize, batch, capacity, ctypes.byref(h)))
+        self.handle = h
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self._lib.b2a_pagepool_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reserve(self, seq: int, positions: int) -> None:
+        check(self._lib.b2a_pagepool_reserve(self.handle, seq, positions))
+
+    def release(self, seq: int | None = None) -> None:
+        check(self._lib.b2a_pagepool_release(self.handle, -1 if seq is None else seq))
+
+    def table(self, seq: int) -> np.ndarray:
+        n = ctypes.c_int()
+        out = np.zeros((self.capacity + self.pageSize - 1) // self.pageSize, np.int32)
+        check(self._lib.b2a_pagepool_table(self.handle, seq, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                           out.size, ctypes.byref(n)))
+        return out[:n.value].copy()
+
+    @property
+    def freePages(self) -> int:
+        n = ctypes.c_int()
+        check(self._lib.b2a_pagepool_free_pages(self.handle, ctypes.byref(n)))
+        return n.value

@@ -242,17 +242,7 @@ constexpr int64_t kMinChunkTiles = 4;
 
 AttnParams base_params(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope) {
   AttnParams p{};
-  p.kc = c->d_k;
-  p.vc = c->d_v;
-  p.kc_w = c->d_k;
-  p.vc_w = c->d_v;
-  p.s_seq = c->s_seq;
-  p.s_layer = c->s_layer;
-  p.s_head = c->s_head;
-  p.cache_dtype = static_cast<int>(c->dtype);
-  p.len = c->d_len;
-  p.kv_heads = c->kv_heads;
-  p.head_dim = c->head_dim;
+  fill_cache_params(p, c);
   p.rope_cos = rope->d_cos;
   p.rope_sin = rope->d_sin;
   p.rope_cos32 = rope->d_cos32;
@@ -497,6 +487,7 @@ b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, 
   }
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
+  if ((s = cache_reserve_all(c, extra)) != B2A_OK) return s;
   AttnParams p = base_params(ctx, c, rope);
   p.seq_begin = 0;
   p.batch = c->batch;
@@ -894,8 +885,16 @@ b2a_status b2a_rope_destroy(b2a_rope* rope) {
 
 // ---------------------------------------------------------------- KV cache --
 
-b2a_status b2a_kvcache_create(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim, int capacity, int batch,
-                              b2a_dtype dtype, b2a_kvcache** out) {
+}  // extern "C"
+
+namespace b2a {
+namespace {
+
+// A contiguous cache (page_size 0: batch blocks of capacity positions) or a
+// paged one (num_pages + 1 pages of page_size positions, the last one the
+// scratch page that unmapped page-table entries name).
+b2a_status create_cache(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim, int capacity, int batch,
+                        b2a_dtype dtype, int page_size, int num_pages, b2a_kvcache** out) {
   if (out == nullptr) return fail(B2A_EINVAL, "null output pointer");
   *out = nullptr;
   // src/cpu/cache.js:24-26
@@ -905,8 +904,23 @@ b2a_status b2a_kvcache_create(b2a_ctx* ctx, int num_layers, int num_kv_heads, in
                 num_kv_heads, head_dim, batch);
   }
   if (!valid_dtype(dtype)) return fail(B2A_EINVAL, "unknown dtype %d", static_cast<int>(dtype));
+  b2a_pagepool* pool = nullptr;
+  if (page_size != 0) {
+    b2a_status s = b2a_pagepool_create(num_pages, page_size, batch, capacity, &pool);
+    if (s != B2A_OK) return s;
+    // every pool row must be addressable by a 32-bit tensor-map coordinate
+    const int64_t rows = (static_cast<int64_t>(num_pages) + 1) * num_layers * num_kv_heads * page_size;
+    if (rows >= (1ll << 31)) {
+      b2a_pagepool_destroy(pool);
+      return fail(B2A_EINVAL, "paged cache of %d pages of %d positions is too large (%lld rows)", num_pages,
+                  page_size, static_cast<long long>(rows));
+    }
+  }
   CallGuard g(ctx);
-  if (!g.ok()) return g.busy_status();
+  if (!g.ok()) {
+    b2a_pagepool_destroy(pool);
+    return g.busy_status();
+  }
   b2a_kvcache* c = new (std::nothrow) b2a_kvcache();
   c->ctx = ctx;
   c->device = ctx->device;
@@ -916,31 +930,67 @@ b2a_status b2a_kvcache_create(b2a_ctx* ctx, int num_layers, int num_kv_heads, in
   c->capacity = capacity;
   c->batch = batch;
   c->dtype = dtype;
-  c->s_head = static_cast<int64_t>(capacity) * head_dim;
+  const int block = page_size != 0 ? page_size : capacity;   // positions per block of the pools
+  const int64_t units = page_size != 0 ? static_cast<int64_t>(num_pages) + 1 : batch;
+  c->s_head = static_cast<int64_t>(block) * head_dim;
   c->s_layer = c->s_head * num_kv_heads;
   c->s_seq = c->s_layer * num_layers;
   c->len.assign(batch, 0);
-  const size_t bytes = static_cast<size_t>(c->s_seq) * batch * dtype_size(dtype);
+  if (page_size != 0) {
+    c->pool = pool;
+    c->page_size = page_size;
+    c->page_shift = 0;
+    while ((1 << c->page_shift) < page_size) c->page_shift++;
+    c->num_pages = num_pages;
+    c->max_pages = (capacity + page_size - 1) / page_size;
+  }
+  const size_t bytes = static_cast<size_t>(c->s_seq) * units * dtype_size(dtype);
   cudaError_t e = cudaMalloc(&c->d_k, bytes);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_v, bytes);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_len, sizeof(int32_t) * batch);
   if (e == cudaSuccess) e = cudaMemsetAsync(c->d_k, 0, bytes, ctx->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(c->d_v, 0, bytes, ctx->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(c->d_len, 0, sizeof(int32_t) * batch, ctx->stream);
+  if (e == cudaSuccess && c->pool != nullptr) {
+    const size_t tbytes = sizeof(int32_t) * static_cast<size_t>(batch) * c->max_pages;
+    e = cudaMalloc(&c->d_pages, tbytes);
+    // every entry starts at the scratch page (the host rows hold the same)
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->d_pages, pool_row(c->pool, 0), tbytes, cudaMemcpyHostToDevice,
+                                              ctx->stream);
+  }
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) {
     if (c->d_k) cudaFree(c->d_k);
     if (c->d_v) cudaFree(c->d_v);
     if (c->d_len) cudaFree(c->d_len);
+    if (c->d_pages) cudaFree(c->d_pages);
+    b2a_pagepool_destroy(c->pool);
     delete c;
     return cuda_fail(e, "allocating the KV cache");
   }
   if (dtype != B2A_F32 && head_dim == 64) {
-    const uint64_t rows = static_cast<uint64_t>(batch) * num_layers * num_kv_heads * capacity;
+    const uint64_t rows = static_cast<uint64_t>(units) * num_layers * num_kv_heads * block;
     c->has_tmaps = encode_pool_map(&c->tmap_k, c->d_k, rows, dtype) && encode_pool_map(&c->tmap_v, c->d_v, rows, dtype);
   }
   *out = c;
   return B2A_OK;
+}
+
+}  // namespace
+}  // namespace b2a
+
+extern "C" {
+
+b2a_status b2a_kvcache_create(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim, int capacity, int batch,
+                              b2a_dtype dtype, b2a_kvcache** out) {
+  return create_cache(ctx, num_layers, num_kv_heads, head_dim, capacity, batch, dtype, 0, 0, out);
+}
+
+b2a_status b2a_kvcache_create_paged(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim, int capacity,
+                                    int batch, b2a_dtype dtype, int page_size, int num_pages, b2a_kvcache** out) {
+  if (out != nullptr) *out = nullptr;
+  if (page_size == 0) return fail(B2A_EINVAL, "page size must be a power of two of at least 128 positions, got 0");
+  return create_cache(ctx, num_layers, num_kv_heads, head_dim, capacity, batch, dtype, page_size, num_pages, out);
 }
 
 b2a_status b2a_kvcache_destroy(b2a_kvcache* c) {
@@ -949,6 +999,8 @@ b2a_status b2a_kvcache_destroy(b2a_kvcache* c) {
   cudaFree(c->d_k);
   cudaFree(c->d_v);
   cudaFree(c->d_len);
+  if (c->d_pages) cudaFree(c->d_pages);
+  b2a_pagepool_destroy(c->pool);
   delete c;
   return B2A_OK;
 }
@@ -961,6 +1013,12 @@ b2a_status b2a_kvcache_allocate(b2a_kvcache* c, int seq_idx, int count, int* at)
   // src/cpu/cache.js:53-58
   if (static_cast<int64_t>(len) + count > c->capacity) {
     return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add %d more", len, c->capacity, count);
+  }
+  if (c->pool != nullptr) {   // a paged cache backs the reserved positions now
+    CallGuard g(c->ctx);
+    if (!g.ok()) return g.busy_status();
+    b2a_status s = cache_reserve1(c, seq_idx, len + count);
+    if (s != B2A_OK) return s;
   }
   *at = len;
   return B2A_OK;
@@ -977,6 +1035,12 @@ b2a_status b2a_kvcache_commit(b2a_kvcache* c, int seq_idx, int count) {
   }
   CallGuard g(c->ctx);
   if (!g.ok()) return g.busy_status();
+  if (c->pool != nullptr) {
+    std::vector<int32_t> want(c->batch);
+    for (int b = 0; b < c->batch; b++) want[b] = (seq_idx >= 0 && b != seq_idx) ? 0 : c->len[b] + count;
+    b2a_status s = cache_reserve(c, 0, c->batch, want.data());
+    if (s != B2A_OK) return s;
+  }
   for (int b = 0; b < c->batch; b++) {
     if (seq_idx >= 0 && b != seq_idx) continue;
     c->len[b] += count;
@@ -1002,6 +1066,8 @@ b2a_status b2a_kvcache_set_lengths(b2a_kvcache* c, const int32_t* lengths) {
   }
   CallGuard g(c->ctx);
   if (!g.ok()) return g.busy_status();
+  b2a_status s = cache_reserve(c, 0, c->batch, lengths);
+  if (s != B2A_OK) return s;
   for (int b = 0; b < c->batch; b++) c->len[b] = lengths[b];
   B2A_CUDA(cudaMemcpyAsync(c->d_len, c->len.data(), sizeof(int32_t) * c->batch, cudaMemcpyHostToDevice,
                            c->ctx->stream),
@@ -1019,6 +1085,8 @@ b2a_status b2a_kvcache_reset(b2a_kvcache* c, int seq_idx) {
     if (seq_idx >= 0 && b != seq_idx) continue;
     c->len[b] = 0;
   }
+  b2a_status s = cache_release(c, seq_idx);   // a paged cache gives the sequence's pages back
+  if (s != B2A_OK) return s;
   cudaError_t e = launch_lengths_update(c->d_len, seq_idx, c->batch, 0, 1, c->ctx->stream);
   if (e != cudaSuccess) return cuda_fail(e, "resetting the device lengths");
   return B2A_OK;
@@ -1026,7 +1094,8 @@ b2a_status b2a_kvcache_reset(b2a_kvcache* c, int seq_idx) {
 
 b2a_status b2a_kvcache_byte_length(const b2a_kvcache* c, size_t* bytes) {
   if (c == nullptr || bytes == nullptr) return fail(B2A_EINVAL, "null argument");
-  *bytes = static_cast<size_t>(c->s_seq) * c->batch * dtype_size(c->dtype) * 2;
+  const size_t units = c->pool != nullptr ? static_cast<size_t>(c->num_pages) + 1 : static_cast<size_t>(c->batch);
+  *bytes = static_cast<size_t>(c->s_seq) * units * dtype_size(c->dtype) * 2;
   return B2A_OK;
 }
 
@@ -1054,6 +1123,10 @@ b2a_status b2a_kvcache_write_at(b2a_ctx* ctx, b2a_kvcache* c, int layer, int seq
   }
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
+  if (count > 0) {
+    b2a_status s = cache_reserve1(c, seq_idx, at + count);
+    if (s != B2A_OK) return s;
+  }
   const size_t bytes = static_cast<size_t>(count) * c->kv_heads * c->head_dim * dtype_size(src_dtype);
   const void* dk = keys;
   const void* dv = values;
@@ -1088,6 +1161,39 @@ b2a_status b2a_kvcache_read(b2a_ctx* ctx, const b2a_kvcache* c, int layer, int s
   const size_t es = dtype_size(c->dtype);
   const size_t head_bytes = static_cast<size_t>(n) * c->head_dim * es;
   const cudaMemcpyKind kind = flags == B2A_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+  if (c->pool != nullptr) {
+    // one copy per (head, page); positions past the mapped pages read as zeros
+    const int P = c->page_size;
+    const int mapped = pool_mapped(c->pool, seq_idx);
+    const int32_t* row = pool_row(c->pool, seq_idx);
+    const size_t pos_bytes = static_cast<size_t>(c->head_dim) * es;
+    const int backed = std::min(n, mapped * P);
+    for (int h = 0; h < c->kv_heads; h++) {
+      char* kd = static_cast<char*>(keys_out) + h * head_bytes;
+      char* vd = static_cast<char*>(values_out) + h * head_bytes;
+      for (int k = 0; k * P < backed; k++) {
+        const int cnt = std::min(P, backed - k * P);
+        const size_t off = (static_cast<size_t>(row[k]) * c->s_seq + static_cast<size_t>(layer) * c->s_layer +
+                            static_cast<size_t>(h) * c->s_head) * es;
+        B2A_CUDA(cudaMemcpyAsync(kd + k * P * pos_bytes, static_cast<const char*>(c->d_k) + off, cnt * pos_bytes, kind,
+                                 ctx->stream), "reading keys");
+        B2A_CUDA(cudaMemcpyAsync(vd + k * P * pos_bytes, static_cast<const char*>(c->d_v) + off, cnt * pos_bytes, kind,
+                                 ctx->stream), "reading values");
+      }
+      if (backed < n) {
+        const size_t zb = static_cast<size_t>(n - backed) * pos_bytes;
+        if (flags == B2A_HOST) {
+          std::memset(kd + backed * pos_bytes, 0, zb);
+          std::memset(vd + backed * pos_bytes, 0, zb);
+        } else {
+          B2A_CUDA(cudaMemsetAsync(kd + backed * pos_bytes, 0, zb, ctx->stream), "reading keys");
+          B2A_CUDA(cudaMemsetAsync(vd + backed * pos_bytes, 0, zb, ctx->stream), "reading values");
+        }
+      }
+    }
+    if (flags == B2A_HOST) B2A_CUDA(cudaStreamSynchronize(ctx->stream), "reading the cache");
+    return B2A_OK;
+  }
   for (int h = 0; h < c->kv_heads; h++) {
     const size_t off = (static_cast<size_t>(seq_idx) * c->s_seq + static_cast<size_t>(layer) * c->s_layer +
                         static_cast<size_t>(h) * c->s_head) * es;
@@ -1119,6 +1225,8 @@ b2a_status b2a_append_rope(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, i
   }
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
+  b2a_status rs = cache_reserve1(c, seq_idx, past + count);
+  if (rs != B2A_OK) return rs;
   const size_t bytes = static_cast<size_t>(count) * c->kv_heads * c->head_dim * dtype_size(src_dtype);
   AttnParams p = base_params(ctx, c, rope);
   p.layer_begin = layer;
@@ -1172,6 +1280,7 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* ro
   }
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
+  if ((s = cache_reserve_all(c, 1)) != B2A_OK) return s;
   AttnParams p = base_params(ctx, c, rope);
   p.seq_begin = 0;
   p.batch = c->batch;
@@ -1218,6 +1327,8 @@ b2a_status attn_decode_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope
                               b2a_dtype out_dtype) {
   int max_keys = 0;
   for (int b = 0; b < c->batch; b++) max_keys = std::max(max_keys, c->len[b] + 1);
+  b2a_status s = cache_reserve_all(c, 1);
+  if (s != B2A_OK) return s;
   AttnParams p = base_params(ctx, c, rope);
   p.seq_begin = 0;
   p.batch = c->batch;
@@ -1308,6 +1419,11 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
   b2a_status s;
   int past = 0;   // the longest past among the call's sequences
   for (int b = 0; b < nseq; b++) past = std::max(past, c->len[seq_idx + b]);
+  if (c->pool != nullptr) {
+    std::vector<int32_t> want(nseq);
+    for (int b = 0; b < nseq; b++) want[b] = c->len[seq_idx + b] + count;
+    if ((s = cache_reserve(c, seq_idx, nseq, want.data())) != B2A_OK) return s;
+  }
   AttnParams p = base_params(ctx, c, rope);
   p.seq_begin = seq_idx;
   p.batch = nseq;

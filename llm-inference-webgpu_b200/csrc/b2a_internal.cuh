@@ -92,6 +92,14 @@ struct b2a_kvcache {
   bool has_tmaps = false;
   CUtensorMap tmap_k;
   CUtensorMap tmap_v;
+  // Paged layout (page_size > 0): the pools hold num_pages + 1 pages of
+  // page_size positions, each [layers][kv_heads][page_size][head_dim]; page
+  // num_pages is a scratch page that every unmapped page-table entry names, so
+  // no table entry ever points outside the pools. The strides above then
+  // describe one page (s_seq = elements per page) and positions are page rows.
+  int page_size = 0, page_shift = 0, num_pages = 0, max_pages = 0;
+  int32_t* d_pages = nullptr;     // [batch][max_pages] device page table
+  b2a_pagepool* pool = nullptr;   // host page tables and free pages
 };
 
 namespace b2a {
@@ -112,6 +120,10 @@ struct AttnParams {
   void* kc_w;                 // same pools, writable (fused append)
   void* vc_w;
   int64_t s_seq, s_layer, s_head;
+  // paged cache: [cache batch][max_pages] page of each 2^page_shift positions
+  // (s_seq is then the page stride); null for a contiguous cache
+  const int32_t* pages;
+  int max_pages, page_shift;
   int cache_dtype;
   const int32_t* len;         // [cache batch] past length per sequence (device)
   int seq_begin;              // first cache sequence of this call
@@ -195,6 +207,22 @@ struct CombineParams {
   int seq_begin, chunk, extra, tokens, heads, num_layers;
 };
 
+// Element offset of (cache sequence bc, layer, kv head g, position pos) in the
+// pools. Contiguous: sequence-major blocks of s_seq elements. Paged: the page
+// that holds pos, then the row pos mod page size within it; a run of positions
+// that starts at a multiple of 128 and stays under the next multiple of 128
+// lies in one page, contiguous, exactly as in the contiguous layout.
+__host__ __device__ inline int64_t kv_elem(const AttnParams& p, int bc, int layer, int g, int pos) {
+  int64_t unit = bc;
+  int off = pos;
+  if (p.pages != nullptr) {
+    unit = p.pages[static_cast<int64_t>(bc) * p.max_pages + (pos >> p.page_shift)];
+    off = pos & ((1 << p.page_shift) - 1);
+  }
+  return unit * p.s_seq + static_cast<int64_t>(layer) * p.s_layer + static_cast<int64_t>(g) * p.s_head +
+         static_cast<int64_t>(off) * p.head_dim;
+}
+
 // Past length of the call's sequence b (by value when the host passed it).
 __host__ __device__ inline int len_of(const AttnParams& p, int b) {
   return b < p.n_len_inline ? p.len_inline[b] : p.len[p.seq_begin + b];
@@ -208,6 +236,34 @@ cudaError_t launch_write_at(const b2a_kvcache* c, int layer, int seq_idx, int at
 cudaError_t launch_read(const b2a_kvcache* c, int layer, int seq_idx, int n, void* k_out, void* v_out,
                         cudaStream_t st);
 cudaError_t launch_lengths_update(int32_t* d_len, int idx, int batch, int count, int mode, cudaStream_t st);
+// the cache's pools, strides and page table in p (the rest of p untouched)
+void fill_cache_params(AttnParams& p, const b2a_kvcache* c);
+
+// ---- paged caches (pages.cu) --------------------------------------------------
+// Entries of the device page table written by one launch, by value.
+constexpr int kPageUpdateMax = 240;
+struct PageUpdate {
+  int n;
+  int32_t idx[kPageUpdateMax];    // entry index seq * max_pages + k
+  int32_t page[kPageUpdateMax];
+};
+cudaError_t launch_page_table_update(int32_t* table, const PageUpdate& u, cudaStream_t st);
+// Backs positions [0, positions[i]) of sequences first..first+n-1 with pages
+// (all or nothing: B2A_ERANGE "page pool exhausted ..." when the free pages do
+// not cover every sequence's new pages) and updates the device table in stream
+// order. A no-op for a contiguous cache. The caller holds the context.
+b2a_status cache_reserve(b2a_kvcache* c, int first, int n, const int32_t* positions);
+inline b2a_status cache_reserve1(b2a_kvcache* c, int seq, int positions) {
+  const int32_t pos = positions;
+  return cache_reserve(c, seq, 1, &pos);
+}
+// cache_reserve for every sequence of the cache, to its length + extra.
+b2a_status cache_reserve_all(b2a_kvcache* c, int extra);
+// Returns the pages of one sequence (seq -1: all) to the pool; no-op when contiguous.
+b2a_status cache_release(b2a_kvcache* c, int seq);
+// host page-pool access for the cache (pages.cu)
+int pool_mapped(const b2a_pagepool* pool, int seq);
+const int32_t* pool_row(const b2a_pagepool* pool, int seq);
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t st);
 bool attn_mma_supported(const AttnParams& p);
 int64_t attn_mma_items(const AttnParams& p, const int32_t* host_len);

@@ -68,7 +68,8 @@ __global__ void __launch_bounds__(kSimtThreads) k_attn_simt(AttnParams p) {
     return;
   }
 
-  const int64_t cache_base = bc * p.s_seq + static_cast<int64_t>(p.layer_begin + l) * p.s_layer + g * p.s_head;
+  const int layer = p.layer_begin + l;
+  const int64_t cache_base = kv_elem(p, bc, layer, g, 0);   // position 0 (contiguous: the row base)
   const double* cosr = p.rope_cos + static_cast<int64_t>(pos_q) * half;
   const double* sinr = p.rope_sin + static_cast<int64_t>(pos_q) * half;
 
@@ -86,7 +87,7 @@ __global__ void __launch_bounds__(kSimtThreads) k_attn_simt(AttnParams p) {
   // one CTA whose chunk holds the new slot.
   if (p.k_new != nullptr && slot >= p0 && slot < p1) {
     const int64_t src = (((static_cast<int64_t>(b) * p.num_layers + l) * p.tokens + t) * p.kv_heads + g) * D;
-    const int64_t dst = cache_base + static_cast<int64_t>(slot) * D;
+    const int64_t dst = kv_elem(p, bc, layer, g, slot);
     for (int j = tid; j < half; j += blockDim.x) {
       float lo, hi;
       rope_pair_f64(ld_as_f32(p.k_new, src + j, p.in_dtype), ld_as_f32(p.k_new, src + j + half, p.in_dtype),
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(kSimtThreads) k_attn_simt(AttnParams p) {
   const int n = p1 - p0;
   // scores: thread i takes positions i and i+128 of the chunk
   for (int i = tid; i < n; i += blockDim.x) {
-    const int64_t krow = cache_base + static_cast<int64_t>(p0 + i) * D;
+    const int64_t krow = p.pages ? kv_elem(p, bc, layer, g, p0 + i) : cache_base + static_cast<int64_t>(p0 + i) * D;
     float acc[kSimtMaxGroup];
 #pragma unroll
     for (int h = 0; h < kSimtMaxGroup; h++) acc[h] = 0.f;
@@ -144,7 +145,8 @@ __global__ void __launch_bounds__(kSimtThreads) k_attn_simt(AttnParams p) {
 #pragma unroll
   for (int h = 0; h < kSimtMaxGroup; h++) acc[h] = 0.f;
   for (int i = hf; i < n; i += nhalves) {
-    const float vv = ld_as_f32(p.vc, cache_base + static_cast<int64_t>(p0 + i) * D + d, p.cache_dtype);
+    const int64_t vrow = p.pages ? kv_elem(p, bc, layer, g, p0 + i) : cache_base + static_cast<int64_t>(p0 + i) * D;
+    const float vv = ld_as_f32(p.vc, vrow + d, p.cache_dtype);
 #pragma unroll
     for (int h = 0; h < kSimtMaxGroup; h++)
       if (h < G) acc[h] = fmaf(sc[h][i], vv, acc[h]);

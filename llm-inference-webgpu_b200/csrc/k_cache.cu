@@ -25,8 +25,7 @@ __global__ void k_rope_append(AttnParams p, int seq_first, int count, int nseq) 
     const int t = static_cast<int>(ib / (static_cast<int64_t>(half) * p.kv_heads));
     const int pos = past + t;
     const int64_t src = ((static_cast<int64_t>(b) * count + t) * p.kv_heads + g) * p.head_dim;
-    const int64_t dst = seq_idx * p.s_seq + static_cast<int64_t>(p.layer_begin) * p.s_layer +
-                        g * p.s_head + static_cast<int64_t>(pos) * p.head_dim;
+    const int64_t dst = kv_elem(p, seq_idx, p.layer_begin, g, pos);
     const double c = p.rope_cos[static_cast<int64_t>(pos) * half + j];
     const double s = p.rope_sin[static_cast<int64_t>(pos) * half + j];
     float lo, hi;
@@ -50,18 +49,35 @@ cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cuda
 
 // src/cpu/cache.js:63-67: rows [count][kv_heads*head_dim] stored as given
 // (rounded to the cache dtype) at positions at..at+count-1, head-major.
-__global__ void k_write_at(void* kc, void* vc, int64_t base, int64_t s_head, const void* k, const void* v,
-                           int src_dt, int cache_dt, int count, int kv_heads, int head_dim, int at) {
-  const int64_t n = static_cast<int64_t>(count) * kv_heads * head_dim;
+__global__ void k_write_at(AttnParams p, int seq_idx, int layer, const void* k, const void* v, int src_dt, int count,
+                           int at) {
+  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * p.head_dim;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int d = static_cast<int>(i % head_dim);
-    const int g = static_cast<int>((i / head_dim) % kv_heads);
-    const int t = static_cast<int>(i / (static_cast<int64_t>(head_dim) * kv_heads));
-    const int64_t dst = base + g * s_head + static_cast<int64_t>(at + t) * head_dim + d;
-    convert_elem(k, i, src_dt, kc, dst, cache_dt);
-    convert_elem(v, i, src_dt, vc, dst, cache_dt);
+    const int d = static_cast<int>(i % p.head_dim);
+    const int g = static_cast<int>((i / p.head_dim) % p.kv_heads);
+    const int t = static_cast<int>(i / (static_cast<int64_t>(p.head_dim) * p.kv_heads));
+    const int64_t dst = kv_elem(p, seq_idx, layer, g, at + t) + d;
+    convert_elem(k, i, src_dt, p.kc_w, dst, p.cache_dtype);
+    convert_elem(v, i, src_dt, p.vc_w, dst, p.cache_dtype);
   }
+}
+
+void fill_cache_params(AttnParams& p, const b2a_kvcache* c) {
+  p.kc = c->d_k;
+  p.vc = c->d_v;
+  p.kc_w = c->d_k;
+  p.vc_w = c->d_v;
+  p.s_seq = c->s_seq;
+  p.s_layer = c->s_layer;
+  p.s_head = c->s_head;
+  p.pages = c->page_size > 0 ? c->d_pages : nullptr;
+  p.max_pages = c->max_pages;
+  p.page_shift = c->page_shift;
+  p.cache_dtype = static_cast<int>(c->dtype);
+  p.len = c->d_len;
+  p.kv_heads = c->kv_heads;
+  p.head_dim = c->head_dim;
 }
 
 cudaError_t launch_write_at(const b2a_kvcache* c, int layer, int seq_idx, int at, const void* k, const void* v,
@@ -70,9 +86,9 @@ cudaError_t launch_write_at(const b2a_kvcache* c, int layer, int seq_idx, int at
   if (n == 0) return cudaSuccess;
   const int threads = 256;
   const int blocks = static_cast<int>((n + threads - 1) / threads < 4096 ? (n + threads - 1) / threads : 4096);
-  const int64_t base = seq_idx * c->s_seq + static_cast<int64_t>(layer) * c->s_layer;
-  k_write_at<<<blocks, threads, 0, st>>>(c->d_k, c->d_v, base, c->s_head, k, v, src_dtype,
-                                         static_cast<int>(c->dtype), count, c->kv_heads, c->head_dim, at);
+  AttnParams p{};
+  fill_cache_params(p, c);
+  k_write_at<<<blocks, threads, 0, st>>>(p, seq_idx, layer, k, v, src_dtype, count, at);
   return cudaGetLastError();
 }
 

@@ -228,7 +228,11 @@ __global__ void __launch_bounds__(kThreads, 3)
   // wait for that kernel to finish. With lengths passed by value the work-item
   // lookup below runs before the wait.
   asm volatile("griddepcontrol.launch_dependents;");
-  if (p.n_len_inline == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (p.n_len_inline == 0) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the earlier kernel's generic-proxy stores are read below by tensor loads (async proxy)
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
 
   // ---- which work item: items are numbered sequence-major, each sequence
   // contributing num_layers * kv_heads * chunks(b) of them.
@@ -273,7 +277,10 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (p.n_len_inline != 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (p.n_len_inline != 0) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
   __syncthreads();
   const int b = ms.item[0];
   if (b < 0) return;   // grid larger than the item count (cannot happen with the host's count)
@@ -291,8 +298,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int n_keys = past + p.horizon_extra;
   const int p0 = c * p.chunk;
   const int p1 = min(p0 + p.chunk, n_keys);
-  const int64_t cache_base = bc * p.s_seq + static_cast<int64_t>(p.layer_begin + l) * p.s_layer + g * p.s_head;
-  const int row_base = static_cast<int>(cache_base / kD);
+  const int layer = p.layer_begin + l;
   const double* cosr = p.rope_cos + static_cast<int64_t>(pos_q) * (kD / 2);
   const double* sinr = p.rope_sin + static_cast<int64_t>(pos_q) * (kD / 2);
 
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     if (tid < kD / 2) {
       const int j = tid;
       const int64_t src = ((static_cast<int64_t>(b) * p.num_layers + l) * p.kv_heads + g) * kD;
-      const int64_t dst = cache_base + static_cast<int64_t>(past) * kD;
+      const int64_t dst = kv_elem(p, bc, layer, g, past);
       float lo, hi;
       rope_pair_f64(ld_as_f32(p.k_new, src + j, p.in_dtype), ld_as_f32(p.k_new, src + j + kD / 2, p.in_dtype),
                     cosr[j], sinr[j], lo, hi);
@@ -325,7 +331,8 @@ __global__ void __launch_bounds__(kThreads, 3)
         if (i >= kStages) mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.err);
         mbar_arrive_expect_tx(&full[s], kStageBytes);
         unsigned char* st = smem + s * kStageBytes;
-        const int y = row_base + p0 + i * kTile;
+        // a 64-position tile starting at a multiple of 64 lies in one page
+        const int y = static_cast<int>(kv_elem(p, bc, layer, g, p0 + i * kTile) / kD);
         tma_load_2d(st, &tmap_k, &full[s], 0, y);
         tma_load_2d(st + kTileBytes, &tmap_v, &full[s], 0, y);
       }

@@ -103,8 +103,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_last = min(q0 + kBM, p.tokens) - 1;               // last valid query of this tile
   const int n_keys = past + q_last + 1;
   const int n_kv = (n_keys + kBN - 1) / kBN;
-  const int64_t cache_base = bc * p.s_seq + static_cast<int64_t>(p.layer_begin) * p.s_layer + g * p.s_head;
-  const int row_base = static_cast<int>(cache_base / kD);
 
   if (tid == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -141,12 +139,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // the cache rows come from the preceding append kernel
       asm volatile("griddepcontrol.wait;" ::: "memory");
+      // the append kernel stored the new rows through the generic proxy; the
+      // tensor loads below read them through the async proxy
+      asm volatile("fence.proxy.async.global;" ::: "memory");
       for (int j = 0; j < n_kv; j++) {
         const int s = j % kStages;
         if (j >= kStages) mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, dead);
         mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
         const uint32_t st = ring + s * kStageBytes;
-        const int y = row_base + j * kBN;
+        // a 128-position tile starting at a multiple of 128 lies in one page
+        const int y = static_cast<int>(kv_elem(p, bc, p.layer_begin, g, j * kBN) / kD);
         tma_load_2d(st, &tmap_k, &kv_full[s], 0, y);
         tma_load_2d(st + kKVBytes / 2, &tmap_k, &kv_full[s], 0, y + 64);
         tma_load_2d(st + kKVBytes, &tmap_v, &kv_full[s], 0, y);
@@ -286,6 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int q4 = 0; q4 < 4; q4++) tmem_ld32(scol + q4 * 32, sr[q4]);
       tmem_wait_ld();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; q4++) tmem_ld_fence(sr[q4]);
       // S_w is in registers: the next S may be written over it
       tc_fence_before();
       mbar_arrive(&s_free[w]);
@@ -323,6 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(ocol, ov[0]);
           tmem_ld32(ocol + 32, ov[1]);
           tmem_wait_ld();
+          tmem_ld_fence(ov[0]);
+          tmem_ld_fence(ov[1]);
 #pragma unroll
           for (int x = 0; x < 2; x++)
 #pragma unroll
@@ -399,6 +405,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_ld32(ocol, ov[0]);
     tmem_ld32(ocol + 32, ov[1]);
     tmem_wait_ld();
+    tmem_ld_fence(ov[0]);
+    tmem_ld_fence(ov[1]);
     if (t < p.tokens) {
       const float inv = 1.f / l;
       const int64_t orow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;

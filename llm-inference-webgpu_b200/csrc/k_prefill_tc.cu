@@ -59,7 +59,7 @@ constexpr int kOffQHi = 0;
 constexpr int kOffQLo = kOffQHi + kQBytes;
 constexpr int kOffRing = kOffQLo + kQBytes;
 constexpr int kOffBars = kOffRing + kStages * kStageBytes;
-constexpr int kNumBars = 2 * kStages + 2 /*s_full*/ + 2 /*p_full*/ + 1 /*o_done*/ + 1 /*q_ready*/;
+constexpr int kNumBars = 2 * kStages + 2 /*s_full*/ + 2 /*p_full*/ + 1 /*o_done*/ + 1 /*q_ready*/ + 1 /*o_final*/;
 constexpr int kSmemTotal = kOffBars + kNumBars * 8 + 16 + 1024;
 
 template <typename T>
@@ -106,7 +106,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_done = p_full + 2;
   uint64_t* q_ready = o_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  // completes once, when the last PV has: the epilogue waits on it, not on
+  // o_done, because a softmax warp can reach the epilogue while o_done is still
+  // two phases short (it never waits for the previous tile's PV), where a
+  // parity wait on o_done cannot tell "two short" from "done"
+  uint64_t* o_final = q_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   bool dead = false;   // set once a bounded wait of this thread gave up
@@ -121,8 +126,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_last = min(q0 + kBM, p.tokens) - 1;               // last valid query of this tile
   const int n_keys = past + q_last + 1;
   const int n_kv = (n_keys + kBN - 1) / kBN;
-  const int64_t cache_base = bc * p.s_seq + static_cast<int64_t>(p.layer_begin) * p.s_layer + g * p.s_head;
-  const int row_base = static_cast<int>(cache_base / kD);
 
   if (tid == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -135,6 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(o_done, 1);
     mbar_init(q_ready, 128);
+    mbar_init(o_final, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -153,12 +157,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // the cache rows come from the preceding append kernel
       asm volatile("griddepcontrol.wait;" ::: "memory");
+      // the append kernel stored the new rows through the generic proxy; the
+      // tensor loads below read them through the async proxy
+      asm volatile("fence.proxy.async.global;" ::: "memory");
       for (int j = 0; j < n_kv; j++) {
         const int s = j % kStages;
         if (j >= kStages) mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, dead);
         mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
         const uint32_t st = smem_u32(smem + kOffRing + s * kStageBytes);
-        const int y = row_base + j * kBN;
+        // a 128-position tile starting at a multiple of 128 lies in one page
+        const int y = static_cast<int>(kv_elem(p, bc, p.layer_begin, g, j * kBN) / kD);
         tma_load_2d(st, &tmap_k, &kv_full[s], 0, y);
         tma_load_2d(st + kKVBytes / 2, &tmap_k, &kv_full[s], 0, y + 64);
         tma_load_2d(st + kKVBytes, &tmap_v, &kv_full[s], 0, y);
@@ -214,6 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&kv_empty[s]);
         mma_commit(o_done);
       }
+      mma_commit(o_final);   // tracks every MMA this thread issued, the last PV included
     }
   } else {
     // ------------------------------------------------------------ softmax
@@ -314,6 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int q4 = 0; q4 < 4; q4++) tmem_ld32(scol + q4 * 32, sr[q4]);
       tmem_wait_ld();
+#pragma unroll
+      for (int q4 = 0; q4 < 4; q4++) tmem_ld_fence(sr[q4]);
       // causal / end-of-sequence mask: key k visible iff k <= a
       const int kbase = j * kBN;
       const bool need_mask = kbase + kBN - 1 > past + q0;
@@ -350,6 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(ocol, ov[0]);
           tmem_ld32(ocol + 32, ov[1]);
           tmem_wait_ld();
+          tmem_ld_fence(ov[0]);
+          tmem_ld_fence(ov[1]);
 #pragma unroll
           for (int x = 0; x < 2; x++)
 #pragma unroll
@@ -412,13 +425,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&p_full[j & 1]);
     }
     // epilogue: O / l -> out rows
-    mbar_wait(o_done, (n_kv - 1) & 1, p.err, dead);
+    mbar_wait(o_final, 0, p.err, dead);
     tc_fence_after();
     uint32_t ov[2][32];
     const uint32_t ocol = tmem + lane_addr + kOCol;
     tmem_ld32(ocol, ov[0]);
     tmem_ld32(ocol + 32, ov[1]);
     tmem_wait_ld();
+    tmem_ld_fence(ov[0]);
+    tmem_ld_fence(ov[1]);
     if (t < p.tokens) {
       const float inv = 1.f / l;
       const int64_t orow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;

@@ -128,6 +128,17 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.ld fills its destination registers asynchronously: they hold the
+// loaded values only once tcgen05.wait::ld has returned. The compiler sees them
+// as produced by the load statement itself and may schedule arithmetic on them
+// above the wait, which then reads whatever the registers held before. Passing
+// the registers through an empty volatile statement placed after the wait
+// (volatile statements keep their order) makes every later use depend on it.
+#define B2A_XREG8(i) "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]), "+r"(r[i + 5]), \
+                     "+r"(r[i + 6]), "+r"(r[i + 7])
+__device__ __forceinline__ void tmem_ld_fence(uint32_t (&r)[32]) {
+  asm volatile("" : B2A_XREG8(0), B2A_XREG8(8), B2A_XREG8(16), B2A_XREG8(24));
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---- named barriers (ids 1..15; __syncthreads uses 0) ---------------------------

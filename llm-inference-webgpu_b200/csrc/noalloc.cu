@@ -97,15 +97,7 @@ extern "C" b2a_status b2a_attention_decode_noalloc(b2a_ctx* ctx, b2a_kvcache* c,
   }
 
   AttnParams p{};
-  p.kc = c->d_k;
-  p.vc = c->d_v;
-  p.kc_w = c->d_k;
-  p.vc_w = c->d_v;
-  p.s_seq = c->s_seq;
-  p.s_layer = c->s_layer;
-  p.s_head = c->s_head;
-  p.cache_dtype = static_cast<int>(c->dtype);
-  p.len = c->d_len;
+  fill_cache_params(p, c);
   p.seq_begin = 0;
   p.batch = c->batch;
   p.num_layers = num_layers;
@@ -188,6 +180,9 @@ extern "C" b2a_status b2a_attention_decode_noalloc(b2a_ctx* ctx, b2a_kvcache* c,
   b2a_status s = scratch_address(ctx->device, &scratch);
   if (s != B2A_OK) return s;
   p.partial = static_cast<float*>(scratch);
+  // a paged cache backs the new slot of every sequence first (host page
+  // tables and a by-value table update: no device allocation)
+  if ((s = cache_reserve_all(c, 1)) != B2A_OK) return s;
 
   e = mma ? launch_attn_mma(p, items, ctx->stream) : launch_attn_simt(p, ctx->stream);
   if (e != cudaSuccess) return cuda_fail(e, "launching the attention kernel");

@@ -64,22 +64,37 @@ def test_batched_prefill_equals_one_call_per_sequence(ctx, rope, oracle, monkeyp
     for i in range(nseq):
         b2a.attentionPrefill(ctx, cs, rope, 1, bits(q[i]), bits(k[i]), bits(v[i]), os_[i], count, H, seq=1 + i,
                              dtype="f16", out_dtype="f32")
-    if cache_dtype != "f32":
-        assert np.array_equal(ob, os_)
-    else:   # the CUDA-core path may chunk the keys differently for one sequence and for three
-        assert_parity(ob.reshape(-1), os_.reshape(-1), "f32", "batched vs single (f32 cache)")
+    refs = []
     for i, past in enumerate(PASTS):
-        kb, vb = cb.read(1, past + count, seq=1 + i)
-        ks, vs = cs.read(1, past + count, seq=1 + i)
-        assert np.array_equal(kb, ks) and np.array_equal(vb, vs)
         # the oracle: RoPE at past..past+count-1, causal over the cached and new keys
         qr = oracle.rope_rows(q[i], range(past, past + count), D, THETA).reshape(-1)
         kr = oracle.round_to(oracle.rope_rows(k[i], range(past, past + count), D, THETA), cache_dtype)
         keys = np.concatenate([hk[1 + i].reshape(past, KVH * D), kr]) if past else kr
         vals = np.concatenate([hv[1 + i].reshape(past, KVH * D), oracle.round_to(v[i], cache_dtype)]) if past else \
             oracle.round_to(v[i], cache_dtype)
-        ref = oracle.grouped_attention(qr, keys.reshape(-1), vals.reshape(-1), count, past, H, KVH, D)
-        assert_parity(ob[i].reshape(-1), ref, "f32", f"{cache_dtype} batched prefill, sequence {i}")
+        refs.append(oracle.grouped_attention(qr, keys.reshape(-1), vals.reshape(-1), count, past, H, KVH, D))
+    if cache_dtype != "f32":
+        if not np.array_equal(ob, os_):
+            # say which call strays from the oracle, and where, before failing
+            where = []
+            for i in range(nseq):
+                for name, o in (("batched", ob[i]), ("single", os_[i])):
+                    err = np.abs(o.reshape(count, H, D) - refs[i].reshape(count, H, D)).max(axis=2)
+                    bad = np.argwhere(err > 1e-2)
+                    where.append(f"seq {i} {name}: max err {err.max():.2e}, {len(bad)} bad (token, head) rows, "
+                                 f"tokens {sorted(set(bad[:, 0].tolist()))[:8]}, heads {sorted(set(bad[:, 1].tolist()))}")
+            for i, past in enumerate(PASTS):
+                kb, vb = cb.read(1, past + count, seq=1 + i)
+                ks, vs = cs.read(1, past + count, seq=1 + i)
+                where.append(f"seq {i} cache: keys equal {np.array_equal(kb, ks)}, values equal {np.array_equal(vb, vs)}")
+            raise AssertionError("batched and per-sequence outputs differ:\n" + "\n".join(where))
+    else:   # the CUDA-core path may chunk the keys differently for one sequence and for three
+        assert_parity(ob.reshape(-1), os_.reshape(-1), "f32", "batched vs single (f32 cache)")
+    for i, past in enumerate(PASTS):
+        kb, vb = cb.read(1, past + count, seq=1 + i)
+        ks, vs = cs.read(1, past + count, seq=1 + i)
+        assert np.array_equal(kb, ks) and np.array_equal(vb, vs)
+        assert_parity(ob[i].reshape(-1), refs[i], "f32", f"{cache_dtype} batched prefill, sequence {i}")
     # the untouched sequence 0 and layer 0 stay as they were
     assert cb.lengthOf(0) == 0
     cb.close()
