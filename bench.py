@@ -312,6 +312,7 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = world * nb["step"] * e2e_steps / (e2e_ms / 1e3) / 1e9
+    link = host_link_gbs(torch, stream, dev, nb["q"] + nb["kv_new"], nb["out"])
 
     pk = peaks()
     achieved = nb["attention_kernel"] / (attn_ms / 1e3) / 1e9
@@ -332,7 +333,8 @@ def run_ours(args) -> None:
                      "launch_ms": round(attn_ms, 4)},
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": nb["q"] + nb["kv_new"],
                 "d2h_bytes_per_step": nb["out"], "ms_per_step": round(e2e_ms / e2e_steps, 4),
-                "path": "b2a_attention_decode with B2A_HOST pointers (pinned)"},
+                "path": "b2a_attention_decode with B2A_HOST pointers (pinned)",
+                "host_link": link},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "kernels": {k: {"launches": v[0], "avg_ms": round(v[1] / v[0], 4)} for k, v in kt.items()},
     }
@@ -366,6 +368,42 @@ def run_ours(args) -> None:
     ctx.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def host_link_gbs(torch, stream, dev, h2d_bytes: int, d2h_bytes: int, reps: int = 20) -> dict:
+    """The host link alone: pinned-host <-> device copies of one step's input and output
+    sizes, each direction by itself and both at once (two streams), CUDA-event timed."""
+    hin = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory()
+    hout = torch.empty(d2h_bytes, dtype=torch.uint8).pin_memory()
+    din = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    dout = torch.empty(d2h_bytes, dtype=torch.uint8, device=dev)
+    other = torch.cuda.Stream(device=dev)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    def both():
+        other.wait_stream(stream)
+        with torch.cuda.stream(other):
+            hout.copy_(dout, non_blocking=True)
+        with torch.cuda.stream(stream):
+            din.copy_(hin, non_blocking=True)
+        stream.wait_stream(other)
+
+    with torch.cuda.stream(stream):
+        t_in = timed(lambda: din.copy_(hin, non_blocking=True))
+        t_out = timed(lambda: hout.copy_(dout, non_blocking=True))
+        t_both = timed(both)
+    return {"h2d_gbs": round(h2d_bytes / (t_in / 1e3) / 1e9, 1), "d2h_gbs": round(d2h_bytes / (t_out / 1e3) / 1e9, 1),
+            "both_ms": round(t_both, 4), "h2d_ms": round(t_in, 4), "d2h_ms": round(t_out, 4)}
 
 
 def bench_paged(torch, b2a, ctx, stream, dev, rope, lengths, nb, q, kn, vn, out, contiguous_ms, args,

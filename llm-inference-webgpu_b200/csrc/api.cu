@@ -385,11 +385,23 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
                                  const void* hk, const void* hv, void* hout, void* dout, int out_dtype, size_t q_seq,
                                  size_t kv_seq, size_t out_seq) {
   const int batch = p.batch;
+  const int layers = p.num_layers;
   const size_t seq_bytes = q_seq + (hk ? 2 * kv_seq : 0) + out_seq;
-  // ~3 MiB of transfers per group and at most 3 groups: more, smaller groups
-  // lose more kernel efficiency (tails, shorter chunks) than they hide copies
-  int groups = static_cast<int>(std::min<size_t>(3, std::max<size_t>(1, batch * seq_bytes / (3u << 20))));
-  if (groups > batch) groups = batch;
+  // Several layers: groups of whole layers for every sequence, so each group's
+  // kernel sees the whole batch (balanced, full-length chunks) and its copies
+  // are strided 2D copies into dense per-group staging; ~1.5 MiB of transfers
+  // per group, at most 8 groups. One layer: groups of sequences, ~3 MiB each
+  // and at most 3 (smaller sequence groups lose more kernel efficiency to
+  // tails and shorter chunks than they hide copies).
+  const bool by_layer = layers >= 2;
+  int groups;
+  if (by_layer) {
+    groups = static_cast<int>(std::min<size_t>(8, std::max<size_t>(1, batch * seq_bytes / (3u << 19))));
+    if (groups > layers) groups = layers;
+  } else {
+    groups = static_cast<int>(std::min<size_t>(3, std::max<size_t>(1, batch * seq_bytes / (3u << 20))));
+    if (groups > batch) groups = batch;
+  }
   if (ctx->copy_in == nullptr) {
     B2A_CUDA(cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking), "creating the upload stream");
   }
@@ -407,6 +419,53 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
   B2A_CUDA(cudaStreamWaitEvent(ctx->copy_in, start, 0), "ordering the upload");
   const char* src_q = static_cast<const char*>(hq);
   char* dst_q = static_cast<char*>(const_cast<void*>(p.q));
+  if (by_layer) {
+    // per layer and sequence: q, new k/v and out bytes
+    const size_t ql = q_seq / layers, kvl = kv_seq / layers, ol = out_seq / layers;
+    char* dst_k = static_cast<char*>(const_cast<void*>(p.k_new));
+    char* dst_v = static_cast<char*>(const_cast<void*>(p.v_new));
+    for (int gi = 0; gi < groups; gi++) {
+      const int l0 = layers * gi / groups, l1 = layers * (gi + 1) / groups, n = l1 - l0;
+      // host [batch][layers][...] rows -> dense staging [batch][n][...] at batch * l0 layer slots
+      B2A_CUDA(cudaMemcpy2DAsync(dst_q + batch * l0 * ql, n * ql, src_q + l0 * ql, q_seq, n * ql, batch,
+                                 cudaMemcpyHostToDevice, ctx->copy_in),
+               "copying q to the device");
+      if (hk) {
+        B2A_CUDA(cudaMemcpy2DAsync(dst_k + batch * l0 * kvl, n * kvl, static_cast<const char*>(hk) + l0 * kvl, kv_seq,
+                                   n * kvl, batch, cudaMemcpyHostToDevice, ctx->copy_in),
+                 "copying new keys to the device");
+        B2A_CUDA(cudaMemcpy2DAsync(dst_v + batch * l0 * kvl, n * kvl, static_cast<const char*>(hv) + l0 * kvl, kv_seq,
+                                   n * kvl, batch, cudaMemcpyHostToDevice, ctx->copy_in),
+                 "copying new values to the device");
+      }
+      B2A_CUDA(cudaEventRecord(ctx->pipe_events[2 * gi], ctx->copy_in), "recording an upload");
+    }
+    int max_keys = 0;
+    for (int b = p.seq_begin; b < p.seq_begin + batch; b++) max_keys = std::max(max_keys, c->len[b] + p.horizon_extra);
+    for (int gi = 0; gi < groups; gi++) {
+      const int l0 = layers * gi / groups, l1 = layers * (gi + 1) / groups, n = l1 - l0;
+      B2A_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->pipe_events[2 * gi], 0), "waiting for an upload");
+      AttnParams pg = p;
+      pg.layer_begin = p.layer_begin + l0;
+      pg.num_layers = n;
+      pg.q = dst_q + batch * l0 * ql;
+      if (hk) {
+        pg.k_new = dst_k + batch * l0 * kvl;
+        pg.v_new = dst_v + batch * l0 * kvl;
+      }
+      char* gout = static_cast<char*>(dout) + batch * l0 * ol;
+      b2a_status s = run_split_kv(ctx, c, pg, max_keys, gout, out_dtype, 0);
+      if (s != B2A_OK) return s;
+      B2A_CUDA(cudaEventRecord(ctx->pipe_events[2 * gi + 1], ctx->stream), "recording a group");
+      B2A_CUDA(cudaStreamWaitEvent(ctx->copy_out, ctx->pipe_events[2 * gi + 1], 0), "ordering a download");
+      B2A_CUDA(cudaMemcpy2DAsync(static_cast<char*>(hout) + l0 * ol, out_seq, gout, n * ol, n * ol, batch,
+                                 cudaMemcpyDeviceToHost, ctx->copy_out),
+               "copying results to the host");
+    }
+    B2A_CUDA(cudaStreamSynchronize(ctx->copy_out), "waiting for the results");
+    B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the kernels");
+    return check_device_error(ctx);
+  }
   for (int gi = 0; gi < groups; gi++) {
     const int b0 = static_cast<int>(static_cast<int64_t>(batch) * gi / groups);
     const int b1 = static_cast<int>(static_cast<int64_t>(batch) * (gi + 1) / groups);
