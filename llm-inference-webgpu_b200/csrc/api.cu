@@ -389,14 +389,16 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
   const size_t seq_bytes = q_seq + (hk ? 2 * kv_seq : 0) + out_seq;
   // Several layers: groups of whole layers for every sequence, so each group's
   // kernel sees the whole batch (balanced, full-length chunks) and its copies
-  // are strided 2D copies into dense per-group staging; ~1.5 MiB of transfers
-  // per group, at most 8 groups. One layer: groups of sequences, ~3 MiB each
-  // and at most 3 (smaller sequence groups lose more kernel efficiency to
-  // tails and shorter chunks than they hide copies).
+  // are strided 2D copies into dense per-group staging. One layer: groups of
+  // sequences. ~3 MiB of transfers per group and at most 3 groups either way:
+  // measured on config 3 (9 MB per call), 1 / 3 / 6 / 8 layer groups took
+  // 0.54 / 0.44 / 0.44 / 0.49 ms per call; more groups add per-group launch
+  // and copy overhead (and, for sequence groups, shorter chunks and tails)
+  // faster than they hide copies.
   const bool by_layer = layers >= 2;
   int groups;
   if (by_layer) {
-    groups = static_cast<int>(std::min<size_t>(8, std::max<size_t>(1, batch * seq_bytes / (3u << 19))));
+    groups = static_cast<int>(std::min<size_t>(3, std::max<size_t>(1, batch * seq_bytes / (3u << 20))));
     if (groups > layers) groups = layers;
   } else {
     groups = static_cast<int>(std::min<size_t>(3, std::max<size_t>(1, batch * seq_bytes / (3u << 20))));
@@ -424,6 +426,10 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
     const size_t ql = q_seq / layers, kvl = kv_seq / layers, ol = out_seq / layers;
     char* dst_k = static_cast<char*>(const_cast<void*>(p.k_new));
     char* dst_v = static_cast<char*>(const_cast<void*>(p.v_new));
+    int max_keys = 0;
+    for (int b = p.seq_begin; b < p.seq_begin + batch; b++) max_keys = std::max(max_keys, c->len[b] + p.horizon_extra);
+    // issued group by group (upload, kernel, download), so the first kernel
+    // is enqueued after one group's copies rather than after all of them
     for (int gi = 0; gi < groups; gi++) {
       const int l0 = layers * gi / groups, l1 = layers * (gi + 1) / groups, n = l1 - l0;
       // host [batch][layers][...] rows -> dense staging [batch][n][...] at batch * l0 layer slots
@@ -439,11 +445,6 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
                  "copying new values to the device");
       }
       B2A_CUDA(cudaEventRecord(ctx->pipe_events[2 * gi], ctx->copy_in), "recording an upload");
-    }
-    int max_keys = 0;
-    for (int b = p.seq_begin; b < p.seq_begin + batch; b++) max_keys = std::max(max_keys, c->len[b] + p.horizon_extra);
-    for (int gi = 0; gi < groups; gi++) {
-      const int l0 = layers * gi / groups, l1 = layers * (gi + 1) / groups, n = l1 - l0;
       B2A_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->pipe_events[2 * gi], 0), "waiting for an upload");
       AttnParams pg = p;
       pg.layer_begin = p.layer_begin + l0;
