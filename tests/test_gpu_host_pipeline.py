@@ -26,9 +26,10 @@ def test_layer_grouped_host_decode_matches_device_decode(oracle):
     dev = torch.device("cuda", 0)
     ctx = b2a.Context(0)
     rope = b2a.RopeTable(ctx, D, THETA, 1024)
-    layers, batch, cap = 24, 32, 700
+    # 64 sequences x 24 layers: ~9 MB of transfers, three layer groups
+    layers, batch, cap = 24, 64, 400
     rng = np.random.default_rng(5)
-    lens = rng.integers(1, 600, size=batch).astype(np.int32)
+    lens = rng.integers(1, 350, size=batch).astype(np.int32)
     cfg = b2a.CacheConfig(numLayers=layers, numKVHeads=KVH, headDim=D, numHeads=H)
     caches = [b2a.GpuKVCache(ctx, cfg, cap, batch=batch, dtype="f16") for _ in range(2)]
     g = torch.Generator(device=dev)
@@ -55,7 +56,7 @@ def test_layer_grouped_host_decode_matches_device_decode(oracle):
     out_dev = out_dev.cpu().numpy()
     assert np.isfinite(out_host).all()
     assert_parity(out_host.reshape(-1), out_dev.reshape(-1), "f32", "host-path vs device-path decode")
-    for b in range(0, batch, 5):
+    for b in range(0, batch, 9):
         for layer in (0, 7, 23):
             kh, vh = caches[0].read(layer, int(lens[b]) + 1, seq=b)
             kd, vd = caches[1].read(layer, int(lens[b]) + 1, seq=b)
