@@ -90,13 +90,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   bool dead = false;   // set once a bounded wait of this thread gave up
   const int n_qtiles = (p.tokens + kBM - 1) / kBM;
-  const int qt = n_qtiles - 1 - static_cast<int>(blockIdx.x);   // heaviest (latest) tiles first
+  // blocks are dispatched in linear order (x fastest): with the query tile in z,
+  // every head pair and sequence of the heaviest (latest) tile starts first
+  const int qt = n_qtiles - 1 - static_cast<int>(blockIdx.z);
   const int pairs = (p.group + 1) >> 1;                          // CTAs per KV group and query tile
-  const int g = blockIdx.y / pairs;
-  const int first = 2 * (blockIdx.y % pairs);                    // first head of the pair within its group
+  const int g = blockIdx.x / pairs;
+  const int first = 2 * (blockIdx.x % pairs);                    // first head of the pair within its group
   const int h0 = g * p.group + first;
   const int ntile = first + 1 < p.group ? 2 : 1;
-  const int sb = blockIdx.z;                                    // sequence of a batched call
+  const int sb = blockIdx.y;                                    // sequence of a batched call
   const int bc = p.seq_begin + sb;
   const int past = p.len[bc];
   const int q0 = qt * kBM;
@@ -455,7 +457,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 bool prefill_pair_supported(const AttnParams& p) {
-  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch >= 1 && p.num_layers == 1 && p.head_dim == kD &&
+  // grid (heads, batch, query tiles): y and z are limited to 65535
+  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch >= 1 && p.batch <= 65535 &&
+         (p.tokens + kBM - 1) / kBM <= 65535 && p.num_layers == 1 && p.head_dim == kD &&
          p.k_new == nullptr && p.cache_dtype == DT_F16 && p.group >= 1;
 }
 
@@ -466,7 +470,7 @@ cudaError_t launch_prefill_pair(const AttnParams& p, void* out, int out_dtype, c
   q.partial = static_cast<float*>(out);
   q.nchunks = out_dtype;
   const int pairs = (p.group + 1) / 2;
-  const dim3 grid((p.tokens + kBM - 1) / kBM, p.kv_heads * pairs, p.batch);
+  const dim3 grid(p.kv_heads * pairs, p.batch, (p.tokens + kBM - 1) / kBM);
   int dev = 0;
   cudaGetDevice(&dev);
   static bool attr[64] = {};

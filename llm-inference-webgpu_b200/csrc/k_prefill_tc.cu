@@ -116,10 +116,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   bool dead = false;   // set once a bounded wait of this thread gave up
   const int n_qtiles = (p.tokens + kBM - 1) / kBM;
-  const int qt = n_qtiles - 1 - static_cast<int>(blockIdx.x);   // heaviest (latest) tiles first
-  const int h = blockIdx.y;
+  // blocks are dispatched in linear order (x fastest): with the query tile in z,
+  // every head and sequence of the heaviest (latest) tile starts before any
+  // lighter tile, so a second wave never holds a heavy tile
+  const int qt = n_qtiles - 1 - static_cast<int>(blockIdx.z);
+  const int h = blockIdx.x;
   const int g = h / p.group;
-  const int sb = blockIdx.z;                                    // sequence of a batched call
+  const int sb = blockIdx.y;                                    // sequence of a batched call
   const int bc = p.seq_begin + sb;
   const int past = p.len[bc];
   const int q0 = qt * kBM;
@@ -481,7 +484,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 bool prefill_tc_supported(const AttnParams& p) {
-  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch >= 1 && p.num_layers == 1 && p.head_dim == kD &&
+  // grid (heads, batch, query tiles): y and z are limited to 65535
+  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch >= 1 && p.batch <= 65535 &&
+         (p.tokens + kBM - 1) / kBM <= 65535 && p.num_layers == 1 && p.head_dim == kD &&
          p.k_new == nullptr && (p.cache_dtype == DT_F16 || p.cache_dtype == DT_BF16);
 }
 
@@ -491,7 +496,7 @@ cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cud
   AttnParams q = p;
   q.partial = static_cast<float*>(out);
   q.nchunks = out_dtype;
-  const dim3 grid((p.tokens + kBM - 1) / kBM, p.heads, p.batch);
+  const dim3 grid(p.heads, p.batch, (p.tokens + kBM - 1) / kBM);
   const CUtensorMap* mk = static_cast<const CUtensorMap*>(p.tmap_k);
   const CUtensorMap* mv = static_cast<const CUtensorMap*>(p.tmap_v);
   int dev = 0;
