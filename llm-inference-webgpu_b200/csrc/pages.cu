@@ -116,6 +116,12 @@ const int32_t* pool_row(const b2a_pagepool* pool, int seq) {
 b2a_status cache_reserve(b2a_kvcache* c, int first, int n, const int32_t* positions) {
   if (c->pool == nullptr || n <= 0) return B2A_OK;
   b2a_pagepool* pool = c->pool;
+  if (first < 0 || first + n > pool->batch) return fail(B2A_EINVAL, "sequences [%d, %d) out of range", first, first + n);
+  for (int i = 0; i < n; i++) {   // callers check capacity first; a table row must never overflow
+    if (positions[i] < 0 || positions[i] > pool->capacity) {
+      return fail(B2A_ERANGE, "cannot back %d positions of a %d-position sequence", positions[i], pool->capacity);
+    }
+  }
   const int64_t need = pages_needed(pool, first, n, positions);
   if (need == 0) return B2A_OK;
   if (need > static_cast<int64_t>(pool->free.size())) {
