@@ -218,6 +218,10 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        # NCCL's banner ("NCCL version ...") goes to stdout, where rank 0's one JSON
+        # line must stand alone: keep NCCL to warnings unless asked for more
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 
     def barrier():
