@@ -1002,7 +1002,7 @@ b2a_status create_cache(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head
     c->page_shift = 0;
     while ((1 << c->page_shift) < page_size) c->page_shift++;
     c->num_pages = num_pages;
-    c->max_pages = (capacity + page_size - 1) / page_size;
+    c->max_pages = static_cast<int>((static_cast<int64_t>(capacity) + page_size - 1) / page_size);
   }
   const size_t bytes = static_cast<size_t>(c->s_seq) * units * dtype_size(dtype);
   cudaError_t e = cudaMalloc(&c->d_k, bytes);

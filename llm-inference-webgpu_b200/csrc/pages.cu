@@ -185,7 +185,7 @@ b2a_status b2a_pagepool_create(int num_pages, int page_size, int batch, int capa
   while ((1 << p->page_shift) < page_size) p->page_shift++;
   p->batch = batch;
   p->capacity = capacity;
-  p->max_pages = (capacity + page_size - 1) / page_size;
+  p->max_pages = static_cast<int>((static_cast<int64_t>(capacity) + page_size - 1) / page_size);
   p->table.assign(static_cast<size_t>(batch) * p->max_pages, num_pages);
   p->mapped.assign(batch, 0);
   p->free.resize(num_pages);
