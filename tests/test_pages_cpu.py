@@ -89,3 +89,35 @@ def test_argument_checks():
         p.reserve(2, 1)
     with pytest.raises(b2a.B2AError, match="out of range"):
         p.release(5)
+
+
+def test_random_reserve_release_keeps_the_pool_consistent():
+    """Random reservations and releases: every page has at most one owner, owners'
+    tables are exactly as long as their reservations need, free + held = pool, and
+    a refused reservation changes nothing."""
+    rng = np.random.default_rng(11)
+    batch, P, pages, cap = 6, 128, 40, 3000
+    p = b2a.PagePool(numPages=pages, pageSize=P, batch=batch, capacity=cap)
+    want = [0] * batch          # pages each sequence must hold
+    for step in range(2000):
+        b = int(rng.integers(batch))
+        if rng.random() < 0.15:
+            p.release(b)
+            want[b] = 0
+        else:
+            pos = int(rng.integers(0, cap + 1))
+            need = -(-pos // P)
+            before = [p.table(i).tolist() for i in range(batch)]
+            extra = max(0, need - want[b])
+            if extra > pages - sum(want):
+                with pytest.raises(b2a.RangeError, match="page pool exhausted"):
+                    p.reserve(b, pos)
+                assert [p.table(i).tolist() for i in range(batch)] == before, step
+            else:
+                p.reserve(b, pos)
+                want[b] = max(want[b], need)
+        tables = [p.table(i).tolist() for i in range(batch)]
+        assert [len(t) for t in tables] == want, step
+        held = [x for t in tables for x in t]
+        assert len(held) == len(set(held)) and all(0 <= x < pages for x in held), step
+        assert p.freePages == pages - len(held), step
