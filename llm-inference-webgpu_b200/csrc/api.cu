@@ -192,30 +192,48 @@ b2a_status h2d(b2a_ctx* ctx, void* dst, const void* src, size_t bytes) {
   return B2A_OK;
 }
 
-// Reads and clears the device error word after the stream is idle: a kernel
-// whose bounded wait gave up reports it there instead of hanging.
-b2a_status check_device_error(b2a_ctx* ctx) {
-  int32_t err = 0;
-  B2A_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(err), cudaMemcpyDeviceToHost), "reading the device error word");
-  if (err != 0) {
-    cudaMemset(ctx->d_err, 0, sizeof(err));
-    // a kernel that gave up may have left merge counters non-zero
-    if (ctx->d_counters) cudaMemset(ctx->d_counters, 0, ctx->d_counters_bytes);
-    if (err == kErrBadToken) {
-      // src/cpu/model.js:203-205
-      return fail(B2A_ERANGE, "a token on the device is outside the vocabulary; results of that call are invalid");
-    }
-    return fail(B2A_ETIMEDOUT, "a device-side wait gave up (error word 0x%x); results of that call are invalid", err);
-  }
+// The device error word: a kernel whose bounded wait gave up reports it there
+// instead of hanging. Host calls read it through pinned host memory with a copy
+// enqueued behind their work, so the one stream synchronisation a call makes
+// covers its results and the word alike.
+b2a_status enqueue_error_read(b2a_ctx* ctx) {
+  B2A_CUDA(cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream),
+           "reading the device error word");
   return B2A_OK;
+}
+
+// Interprets and clears the word read by enqueue_error_read, once the stream is idle.
+b2a_status take_error_word(b2a_ctx* ctx) {
+  const int32_t err = *ctx->h_err;
+  if (err == 0) return B2A_OK;
+  *ctx->h_err = 0;
+  cudaMemsetAsync(ctx->d_err, 0, sizeof(err), ctx->stream);
+  // a kernel that gave up may have left merge counters non-zero
+  if (ctx->d_counters) cudaMemsetAsync(ctx->d_counters, 0, ctx->d_counters_bytes, ctx->stream);
+  cudaStreamSynchronize(ctx->stream);
+  if (err == kErrBadToken) {
+    // src/cpu/model.js:203-205
+    return fail(B2A_ERANGE, "a token on the device is outside the vocabulary; results of that call are invalid");
+  }
+  return fail(B2A_ETIMEDOUT, "a device-side wait gave up (error word 0x%x); results of that call are invalid", err);
+}
+
+// Waits for the context's stream, then reads and clears the device error word.
+b2a_status check_device_error(b2a_ctx* ctx) {
+  b2a_status s = enqueue_error_read(ctx);
+  if (s != B2A_OK) return s;
+  B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the stream");
+  return take_error_word(ctx);
 }
 
 b2a_status d2h_sync(b2a_ctx* ctx, void* dst, const void* src, size_t bytes) {
   if (bytes) {
     B2A_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "copying results to the host");
   }
+  b2a_status s = enqueue_error_read(ctx);
+  if (s != B2A_OK) return s;
   B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the results");
-  return check_device_error(ctx);
+  return take_error_word(ctx);
 }
 
 b2a_status check_cache_shape(const b2a_kvcache* c, const b2a_rope* rope, int num_heads) {
@@ -463,9 +481,11 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
                                  cudaMemcpyDeviceToHost, ctx->copy_out),
                "copying results to the host");
     }
+    b2a_status es = enqueue_error_read(ctx);
+    if (es != B2A_OK) return es;
     B2A_CUDA(cudaStreamSynchronize(ctx->copy_out), "waiting for the results");
     B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the kernels");
-    return check_device_error(ctx);
+    return take_error_word(ctx);
   }
   for (int gi = 0; gi < groups; gi++) {
     const int b0 = static_cast<int>(static_cast<int64_t>(batch) * gi / groups);
@@ -511,9 +531,11 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
                              n * out_seq, cudaMemcpyDeviceToHost, ctx->copy_out),
              "copying results to the host");
   }
+  b2a_status es = enqueue_error_read(ctx);
+  if (es != B2A_OK) return es;
   B2A_CUDA(cudaStreamSynchronize(ctx->copy_out), "waiting for the results");
   B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the kernels");
-  return check_device_error(ctx);
+  return take_error_word(ctx);
 }
 
 
@@ -750,11 +772,14 @@ b2a_status b2a_init(int device, b2a_ctx** out) {
   ctx->stream = ctx->own_stream;
   e = cudaMalloc(&ctx->d_err, 64);
   if (e == cudaSuccess) e = cudaMemset(ctx->d_err, 0, 64);
+  if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&ctx->h_err), 64, cudaHostAllocDefault);
   if (e != cudaSuccess) {
+    if (ctx->d_err) cudaFree(ctx->d_err);
     cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return cuda_fail(e, "allocating the error word");
   }
+  *ctx->h_err = 0;
   *out = ctx;
   return B2A_OK;
 }
@@ -766,6 +791,7 @@ b2a_status b2a_destroy(b2a_ctx* ctx) {
   if (ctx->d_stage) cudaFree(ctx->d_stage);
   if (ctx->d_scratch) cudaFree(ctx->d_scratch);
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->h_err) cudaFreeHost(ctx->h_err);
   if (ctx->d_positions) cudaFree(ctx->d_positions);
   if (ctx->d_counters) cudaFree(ctx->d_counters);
   for (auto& r : ctx->timing_recs) {
@@ -791,7 +817,6 @@ b2a_status b2a_set_stream(b2a_ctx* ctx, void* cuda_stream) {
 b2a_status b2a_synchronize(b2a_ctx* ctx) {
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
-  B2A_CUDA(cudaStreamSynchronize(ctx->stream), "synchronizing the stream");
   return check_device_error(ctx);
 }
 

@@ -26,6 +26,7 @@ struct b2a_ctx {
   void* d_scratch = nullptr;
   size_t d_scratch_bytes = 0;
   int32_t* d_err = nullptr;             // device error word (bounded waits, bounds checks)
+  int32_t* h_err = nullptr;             // pinned host copy of it, read after a call's stream sync
   int32_t* d_counters = nullptr;        // fused split-KV merge counters, kept zeroed
   size_t d_counters_bytes = 0;
   int32_t* d_positions = nullptr;       // staging for host q_positions
