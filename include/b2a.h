@@ -153,7 +153,9 @@ b2a_status b2a_kvcache_read(b2a_ctx* ctx, const b2a_kvcache* cache, int layer, i
  * kernels never crosses a page). When the pool cannot back a call's new
  * positions the call fails with B2A_ERANGE "page pool exhausted: U of N pages in
  * use; sequence S needs K more" and no page of that call is taken. Pages of
- * positions beyond a sequence's mapped pages read as zeros. */
+ * positions beyond a sequence's mapped pages read as zeros. A paged cache's
+ * allocate enqueues its page-table update on the owning context's stream, so,
+ * unlike a contiguous cache's, it returns B2A_EBUSY while a call runs there. */
 b2a_status b2a_kvcache_create_paged(b2a_ctx* ctx, int num_layers, int num_kv_heads, int head_dim,
                                     int capacity, int batch, b2a_dtype dtype, int page_size,
                                     int num_pages, b2a_kvcache** out);
