@@ -14,6 +14,8 @@ import pytest
 from b2a import dist as bd
 
 LOG2E = 1.0 / math.log(2.0)
+RENDEZVOUS_S = 90    # ranks joining (each spawned child imports torch first)
+COLLECTIVE_S = 5     # one collective of the step: a missing rank must fail it quickly
 
 
 def test_position_slices_partition_the_sequence():
@@ -84,8 +86,12 @@ def _worker(rank, world, port, q, kh, vh, total, drop_rank, result_path):
     from oracle import oracle
     from b2a import dist as bdist
 
+    # the rendezvous includes every spawned rank importing torch, which can take
+    # tens of seconds on a loaded machine: give it a generous limit, and bound
+    # the step's collective separately with a group of its own
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=5))
+                            timeout=datetime.timedelta(seconds=RENDEZVOUS_S))
+    step_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=COLLECTIVE_S))
     heads, group, head_dim = q.shape[0], q.shape[0] // kh.shape[0], q.shape[1]
     lo, hi = bdist.position_slice(total, world, rank)
 
@@ -96,7 +102,7 @@ def _worker(rank, world, port, q, kh, vh, total, drop_rank, result_path):
         if rank == drop_rank:
             raise SystemExit(0)   # this rank leaves between steps, before the collective
         flat = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype)
-        dist.all_gather_into_tensor(flat, local)
+        dist.all_gather_into_tensor(flat, local, group=step_group)
         return flat.view((world,) + tuple(local.shape))
 
     def combine_fn(stacked, out):
@@ -151,10 +157,14 @@ def test_split_kv_step_two_ranks_gloo(tmp_path, oracle):
 
 def test_split_kv_step_missing_rank_fails_fast(tmp_path, oracle):
     """A rank that leaves before the gather: the other rank's collective ends
-    with an error within the process group's timeout instead of hanging."""
+    with an error within the step group's timeout instead of hanging."""
+    import time
+    t0 = time.monotonic()
     _, _, _, _, paths = _run(2, 1, tmp_path, oracle)
     assert os.path.exists(paths[0] + ".err"), "rank 0 should have seen the collective fail"
     assert not os.path.exists(paths[0])
+    # spawn + rendezvous + the bounded collective, far below the rendezvous limit
+    assert time.monotonic() - t0 < RENDEZVOUS_S
 
 
 def _handle_worker(rank, world, port, result_path):
@@ -164,7 +174,7 @@ def _handle_worker(rank, world, port, result_path):
     from b2a import dist as bdist
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=5))
+                            timeout=datetime.timedelta(seconds=RENDEZVOUS_S))
     try:
         got = bdist.gather_handles(bytes([rank + 1]) * 64, world)
         with open(result_path, "wb") as f:
