@@ -99,6 +99,16 @@ def config3_bytes(lengths: np.ndarray, cache_es: int = 2, in_es: int = 2, out_es
             "attention_kernel": kv_read + q + kv_new + append, "step": kv_read + q + kv_new + append + out}
 
 
+def config3_block(world: int) -> dict:
+    """The headline workload's `config`, the same on both arms."""
+    nb = config3_bytes(config3_lengths(0))
+    return {"workload": workload_name(), "sequences_per_gpu": SEQS, "layers": LAYERS,
+            "heads": "14q/2kv", "head_dim": D, "kv_len": f"U{{{LMIN}..{LMAX}}} seeded per rank",
+            "cache_dtype": "f16", "q_dtype": "f16", "out_dtype": "f32", "rope_theta": THETA,
+            "bytes_per_step_per_gpu": nb["step"], "parallelism": f"dp{world} (sequences)",
+            "l2": "inputs larger than L2 (KV read per step per GPU %.2f GB)" % (nb["kv_read"] / 1e9)}
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 100 ms while running."""
 
@@ -174,6 +184,74 @@ class _CAI:
     def __init__(self, ptr: int, shape, typestr: str):
         self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
                                          "version": 3, "strides": None}
+
+
+# ------------------------------------------------------- parity samples ---
+# A check of the measured runs' outputs, outside every timed region: sampled
+# rows recomputed in float64 with PyTorch on the same device inputs (the
+# reference's decode, src/cpu/model.js:103-123 over src/core/attention.js:32-66:
+# RoPE of the query at its absolute position, scores scaled by 1/sqrt(64), a
+# max-shifted softmax, the weighted sum of values). The CPU oracle is the
+# tests' checker; this is the benchmark's own sanity check of the same runs.
+
+def _rope_f64(torch, x, positions, dev):
+    """Half-split rotation (src/core/ops.js:147-158) of x [..., rows, 64] at positions [rows], f64."""
+    half = D // 2
+    inv = torch.tensor([THETA ** (-2.0 * j / D) for j in range(half)], dtype=torch.float64, device=dev)
+    ang = torch.as_tensor(np.asarray(positions, np.float64), device=dev)[:, None] * inv[None, :]
+    c, s_ = torch.cos(ang), torch.sin(ang)
+    lo, hi = x[..., :half], x[..., half:]
+    return torch.cat([lo * c - hi * s_, hi * c + lo * s_], dim=-1)
+
+
+def _attend_f64(torch, qr, k, v):
+    """qr [heads, 64]; k, v [kv_heads, n, 64] (f64): softmax(q k^T / 8) v per head, heads grouped."""
+    group = qr.shape[0] // k.shape[0]
+    kk = k.repeat_interleave(group, dim=0)
+    vv = v.repeat_interleave(group, dim=0)
+    sc = torch.einsum("hd,hnd->hn", qr, kk) / math.sqrt(D)
+    return torch.einsum("hn,hnd->hd", torch.softmax(sc, dim=-1), vv)
+
+
+def _summary(errs, scales) -> dict:
+    mx = max(errs) if errs else 0.0
+    rel = max(e / s for e, s in zip(errs, scales) if s > 0) if errs else 0.0
+    return {"max_abs": float(f"{mx:.3g}"), "rel": float(f"{rel:.3g}"), "ok": bool(mx <= 2e-3 and rel <= 1e-2)}
+
+
+def parity_decode(torch, dev, kp, vp, shape, q, out, lengths, picks) -> dict:
+    """Sampled (sequence, layer) rows of a decode whose cache pools are viewed as `shape`
+    [seqs][layers][kv_heads][cap][64] f16; q [seqs][layers][heads][64]; out likewise (f32)."""
+    kv = torch.as_tensor(_CAI(kp, shape, "<f2"), device=dev)
+    vv = torch.as_tensor(_CAI(vp, shape, "<f2"), device=dev)
+    errs, scales = [], []
+    for b, layer in picks:
+        n = int(lengths[b]) + 1
+        qr = _rope_f64(torch, q[b, layer].double(), [n - 1] * q.shape[2], dev)
+        ref = _attend_f64(torch, qr, kv[b, layer, :, :n].double(), vv[b, layer, :, :n].double())
+        errs.append(float((out[b, layer].double() - ref).abs().max()))
+        scales.append(float(ref.abs().max()))
+    res = _summary(errs, scales)
+    res["rows"] = len(picks)
+    return res
+
+
+def parity_prefill(torch, dev, q, k, v, o, rows) -> dict:
+    """Query rows of a causal prefill from position 0: q, o [S][heads][64]; k, v [S][kv][64]
+    (the inputs before RoPE; keys rotated in f64, as exact as an f32 cache allows)."""
+    S = q.shape[0]
+    kr = _rope_f64(torch, k.double().transpose(0, 1), list(range(S)), dev)   # [kv][S][64]
+    vt = v.double().transpose(0, 1)
+    errs, scales = [], []
+    for t in rows:
+        qr = _rope_f64(torch, q[t].double(), [t] * q.shape[1], dev)
+        ref = _attend_f64(torch, qr, kr[:, :t + 1], vt[:, :t + 1])
+        # bf16 output: its own rounding (half an ulp) is not an error of the kernel
+        errs.append(float(((o[t].double() - ref).abs() - ref.abs() * 2.0 ** -8).clamp_min(0).max()))
+        scales.append(float(ref.abs().max()))
+    res = _summary(errs, scales)
+    res["rows"] = len(rows)
+    return res
 
 
 # ---------------------------------------------------------- CPU baselines --
@@ -318,6 +396,16 @@ def run_ours(args) -> None:
     e2e_value = world * nb["step"] * e2e_steps / (e2e_ms / 1e3) / 1e9
     link = host_link_gbs(torch, stream, dev, nb["q"] + nb["kv_new"], nb["out"])
 
+    # parity of the measured step (outside the timed regions): the device call's
+    # output and the host-pointer call's, on 16 sampled rows
+    step()
+    torch.cuda.synchronize(dev)
+    rng = np.random.default_rng(5)
+    picks = [(int(np.argmax(lengths)), 0), (int(np.argmax(lengths)), LAYERS - 1), (int(np.argmin(lengths)), 0)]
+    picks += [(int(rng.integers(SEQS)), int(rng.integers(LAYERS))) for _ in range(13)]
+    parity = {"config3": parity_decode(torch, dev, kp, vp, shape, q, out, lengths, picks),
+              "config3_e2e": parity_decode(torch, dev, kp, vp, shape, q, outh.to(dev), lengths, picks[:4])}
+
     pk = peaks()
     achieved = nb["attention_kernel"] / (attn_ms / 1e3) / 1e9
     traffic = ncu_traffic(attn_name, workload_name())
@@ -325,11 +413,7 @@ def run_ours(args) -> None:
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": workload_name(), "sequences_per_gpu": SEQS, "layers": LAYERS,
-                   "heads": "14q/2kv", "head_dim": D, "kv_len": f"U{{{LMIN}..{LMAX}}} seeded per rank",
-                   "cache_dtype": "f16", "q_dtype": "f16", "out_dtype": "f32", "rope_theta": THETA,
-                   "bytes_per_step_per_gpu": nb["step"], "parallelism": f"dp{world} (sequences)",
-                   "l2": "inputs larger than L2 (KV read per step per GPU %.2f GB)" % (nb["kv_read"] / 1e9)},
+        "config": config3_block(world),
         "roofline": {"bound": "hbm", "kernel": attn_name, "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "peak_source": pk["source"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
@@ -364,6 +448,15 @@ def run_ours(args) -> None:
                                 "sample": sample,
                                 "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
                                                   "sample": sample1}}
+    line["parity"] = parity
+    for key in ("split_kv", "prefill"):   # their own parity samples, gathered in one place
+        if isinstance(line.get(key), dict) and "parity" in line[key]:
+            parity[key] = line[key]["parity"]
+    # the bulky objects first and the compact summaries last, so a reader of the
+    # line's tail sees parity, split-KV and prefill
+    for key in ("kernels", "layer", "generation", "paged", "parity", "split_kv", "prefill"):
+        if key in line:
+            line[key] = line.pop(key)
     barrier()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -573,6 +666,8 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
             kt = ctx.read_timing()
             ctx.enable_timing(False)
             ms = timed(one, steps)
+        extra = {"parity": parity_decode(torch, dev, kp, vp, shape, q.view(nseq, 1, H, D), out.view(nseq, 1, H, D),
+                                         [total] * nseq, [(b, 0) for b in range(nseq)])}
     kv_bytes = nseq * KVH * (total + 1) * D * 2 * 2
     cache.close()
     rope.close()
@@ -589,7 +684,7 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
 
 
 def bench_layer(torch, b2a, ctx, stream, dev, args) -> dict:
-    """SURVEY 8(f)1, the attention block's neighbours: one decode step of one Qwen2.5 layer's
+    """The attention block's neighbours: one decode step of one Qwen2.5 layer's
     attention block through the library - fused int8 q/k/v projection (bias, f16 row scales),
     RoPE + append + attention over the cache, int8 o_proj with the residual add - replayed from a
     CUDA graph. Two shapes: BASELINE config 4 (one sequence, ~128 cached positions, the
@@ -838,6 +933,10 @@ def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
                                 "kernel": attn, "kernel_ms": round(kms, 4) if kms else None,
                                 "kernel_tflops": round(flops / (kms / 1e3) / 1e12, 3) if kms else None,
                                 "launches_per_step": sum(x[0] for x in kt.values()) / steps}
+        if S == 512 or S == max(args.prefill_seqs):
+            # the measured call's output: query rows of the first, middle and last tiles
+            rows = sorted({0, 1, min(S - 1, 127), S // 2, max(0, S - 128), S - 1})
+            res.setdefault("parity", {})[str(S)] = parity_prefill(torch, dev, q, k, v, o, rows)
         cache.close()
         rope.close()
     # many short prompts at once (b2a_attention_prefill_batch): config 2's S=512 for 32
@@ -882,6 +981,20 @@ def bench_prefill(torch, b2a, ctx, stream, dev, pk, args) -> dict:
                            "achieved": bk["kernel_tflops"], "peak": pk["bf16_tflops"], "peak_source": pk["source"],
                            "unit": "TFLOP/s", "frac": round(bk["kernel_tflops"] / pk["bf16_tflops"], 4),
                            "traffic": ncu_traffic(bk["kernel"], f"prefill{best_s}")}
+        # scalar copies of the headline figures (for readers that keep only scalars)
+        res["roofline_seq"] = int(best_s)
+        res["roofline_tflops"] = bk["kernel_tflops"]
+        res["roofline_frac"] = res["roofline"]["frac"]
+    for S_ in ("2048", "16384"):
+        if S_ in res["sweep"] and res["sweep"][S_]["kernel_tflops"]:
+            res[f"s{S_}_kernel_tflops"] = res["sweep"][S_]["kernel_tflops"]
+            res[f"s{S_}_frac"] = round(res["sweep"][S_]["kernel_tflops"] / pk["bf16_tflops"], 4)
+    res["batched_tflops"] = res["batched"]["tflops"]
+    res["batched_frac"] = res["batched"]["frac"]
+    # the bulky sweep before the summaries
+    for key in ("sweep", "batched", "config", "parity", "roofline"):
+        if key in res:
+            res[key] = res.pop(key)
     return res
 
 
@@ -924,9 +1037,7 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": workload_name(), "sequences_per_gpu": SEQS, "layers": LAYERS,
-                   "heads": "14q/2kv", "head_dim": D, "kv_len": f"U{{{LMIN}..{LMAX}}} seeded per rank",
-                   "cache_dtype": "f16"},
+        "config": config3_block(world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": used, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -209,19 +209,21 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope
 
 /* ---- decode that allocates nothing ------------------------------------------
  * No counterpart in the reference: its engine owns its WebGPU buffers itself.
- * Same work, arguments and results as b2a_attention_decode, for callers that
- * cannot allocate device memory: a server that has already handed the GPU's
- * memory to its own pools, or a caller running several streams that must not
- * be stalled by the device-wide synchronization cudaMalloc/cudaFree can cause.
+ * Same work and arguments as b2a_attention_decode, for callers that cannot
+ * allocate device memory: a server that has already handed the GPU's memory
+ * to its own pools, or a caller running several streams that must not be
+ * stalled by the device-wide synchronization cudaMalloc/cudaFree can cause.
+ * Results agree with b2a_attention_decode within the split-KV merge's
+ * rounding, not bit for bit (its chunk sizes may differ).
  * All pointers are device pointers (nothing is staged); the call only enqueues
  * work on the context's stream and never calls cudaMalloc or cudaFree.
  * The split-KV partials go to one fixed device array of
- * B2A_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
- * the process exits. A call whose partials would not fit returns B2A_ERANGE.
- * All calls on a device share that array: calls that overlap on the GPU race
- * and corrupt each other, so order them (e.g. one stream). The first call on
- * each device looks up the array's device address; make it before any stream
- * capture. */
+ * B2A_NOALLOC_SCRATCH_BYTES. b2a_init makes it resident on the context's GPU
+ * (by looking up its address) and loads the kernels this call launches, so
+ * create contexts before filling the GPU's memory; the GPU then holds the
+ * array until the process exits. A call whose partials would not fit returns
+ * B2A_ERANGE. All calls on a device share that array: calls that overlap on
+ * the GPU race and corrupt each other, so order them (e.g. one stream). */
 #define B2A_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
 b2a_status b2a_attention_decode_noalloc(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
                                         int layer_begin, int num_layers, int num_heads,

@@ -12,6 +12,7 @@ from . import build as _build
 B2A_OK, B2A_EINVAL, B2A_ERANGE, B2A_EBUSY, B2A_ECUDA, B2A_ENCCL, B2A_ETIMEDOUT, B2A_ENODEV = range(8)
 B2A_F32, B2A_F16, B2A_BF16 = 0, 1, 2
 B2A_HOST, B2A_DEVICE = 0, 1
+B2A_NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024   # include/b2a.h: the no-alloc decode's fixed array
 
 DTYPES = {"f32": B2A_F32, "f16": B2A_F16, "bf16": B2A_BF16}
 DTYPE_SIZE = {B2A_F32: 4, B2A_F16: 2, B2A_BF16: 2}

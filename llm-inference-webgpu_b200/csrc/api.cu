@@ -780,6 +780,17 @@ b2a_status b2a_init(int device, b2a_ctx** out) {
     return cuda_fail(e, "allocating the error word");
   }
   *ctx->h_err = 0;
+  // the no-alloc decode's scratch array and kernels become resident now, while
+  // the host can still allocate (the runtime would otherwise load them lazily
+  // at that decode's first call)
+  b2a_status s = noalloc_prepare(device);
+  if (s != B2A_OK) {
+    cudaFreeHost(ctx->h_err);
+    cudaFree(ctx->d_err);
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return s;
+  }
   *out = ctx;
   return B2A_OK;
 }

@@ -271,6 +271,14 @@ int64_t attn_mma_items(const AttnParams& p, const int32_t* host_len);
 int attn_mma_max_fused_chunks();
 cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st);
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t st);
+// Load a module's kernels onto the current device ahead of their first launch.
+cudaError_t preload_attn_mma();
+cudaError_t preload_attn_simt();
+cudaError_t preload_pages();
+// Called by b2a_init with `device` current: makes the no-alloc decode's scratch
+// array and every kernel that decode launches resident on the device, so that
+// later no-alloc calls need no device memory at all (noalloc.cu).
+b2a_status noalloc_prepare(int device);
 bool prefill_tc_supported(const AttnParams& p);
 cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cudaStream_t st);
 bool prefill_pair_supported(const AttnParams& p);

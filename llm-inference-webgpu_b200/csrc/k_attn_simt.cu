@@ -354,6 +354,16 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Loads the CUDA-core decode and the combine kernels onto the current device
+// (otherwise loaded lazily at their first launch, which allocates device memory).
+cudaError_t preload_attn_simt() {
+  cudaFuncAttributes a;
+  cudaError_t e = cudaFuncGetAttributes(&a, k_attn_simt<64>);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, k_combine);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, k_combine_wide);
+  return e;
+}
+
 // src/core/attention.js:32-66 over position-major f32 arrays, any head layout,
 // head_dim <= 256. One CTA per (query t, head h); keys are walked in chunks of
 // 1024 with an online (rescaled) softmax so any context length fits.

@@ -772,6 +772,16 @@ int64_t attn_mma_items(const AttnParams& p, const int32_t* host_len) {
   return items;
 }
 
+// Loads both instantiations onto the current device (the runtime otherwise
+// loads a kernel's code lazily, at its first launch, which allocates device
+// memory for it).
+cudaError_t preload_attn_mma() {
+  cudaFuncAttributes a;
+  cudaError_t e = cudaFuncGetAttributes(&a, k_decode_mma<__half>);
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, k_decode_mma<__nv_bfloat16>);
+  return e;
+}
+
 cudaError_t launch_attn_mma(const AttnParams& p, int64_t items, cudaStream_t st) {
   if (!attn_mma_supported(p) || p.chunk % kTile != 0) return cudaErrorInvalidValue;
   if (items == 0) return cudaSuccess;

@@ -13,9 +13,15 @@
 // first time a shape needs more room; this entry point never does.
 //
 // Instead, the split-KV partials live in one file-scope device array of
-// B2A_NOALLOC_SCRATCH_BYTES bytes. The CUDA runtime creates it when it loads
-// this library's device code onto a GPU, and every GPU that loads the library
-// holds it until the process exits. All calls on a device share that one
+// B2A_NOALLOC_SCRATCH_BYTES bytes. The CUDA runtime loads a module's device
+// code and variables lazily, on first use, and loading allocates device
+// memory. So b2a_init, when it creates a context, calls noalloc_prepare below
+// for the context's device: that looks up the array's address (which makes
+// the runtime create the array) and loads every kernel this decode launches.
+// From then on the GPU holds the array until the process exits, and calls of
+// b2a_attention_decode_noalloc on that device allocate nothing. A host that
+// cannot allocate later should therefore create its contexts before it hands
+// the GPU's memory to its own pools. All calls on a device share that one
 // array, and it keeps whatever the previous call left in it: nothing in it has
 // to start at zero, because every partial the merge step reads is written
 // earlier in the same call. Two calls whose work overlaps on the GPU (on
@@ -24,10 +30,11 @@
 // must order such calls, for example by issuing them on one stream.
 //
 // Host code cannot pass the array's name to a kernel: in host code that name
-// is only a host-side stand-in, not a device address. The first call on each
-// device looks up the array's device address with cudaGetSymbolAddress (with
-// that device current) and keeps it; make that first call before any stream
-// capture begins.
+// is only a host-side stand-in, not a device address. The set-up looks up the
+// array's device address with cudaGetSymbolAddress, once per device and with
+// that device current, and keeps it; the decode passes that address to the
+// kernels. Because the set-up runs in b2a_init, stream capture that begins
+// after the context exists never sees it.
 #include <cmath>
 #include <mutex>
 
@@ -66,6 +73,21 @@ b2a_status scratch_address(int device, void** out) {
 bool valid_dtype(int d) { return d == B2A_F32 || d == B2A_F16 || d == B2A_BF16; }
 
 }  // namespace
+
+namespace b2a {
+
+b2a_status noalloc_prepare(int device) {
+  void* ptr = nullptr;
+  b2a_status s = scratch_address(device, &ptr);
+  if (s != B2A_OK) return s;
+  cudaError_t e = preload_attn_mma();
+  if (e == cudaSuccess) e = preload_attn_simt();
+  if (e == cudaSuccess) e = preload_pages();
+  if (e != cudaSuccess) return cuda_fail(e, "loading the decode kernels onto the device");
+  return B2A_OK;
+}
+
+}  // namespace b2a
 
 extern "C" b2a_status b2a_attention_decode_noalloc(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope,
                                                    int layer_begin, int num_layers, int num_heads, const void* q,

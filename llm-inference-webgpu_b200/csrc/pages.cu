@@ -102,6 +102,11 @@ struct UpdateBatch {
 
 }  // namespace
 
+cudaError_t preload_pages() {
+  cudaFuncAttributes a;
+  return cudaFuncGetAttributes(&a, k_page_table_update);
+}
+
 cudaError_t launch_page_table_update(int32_t* table, const PageUpdate& u, cudaStream_t st) {
   if (u.n <= 0) return cudaSuccess;
   k_page_table_update<<<(u.n + 127) / 128, 128, 0, st>>>(table, u);

@@ -49,3 +49,32 @@ def assert_parity(got, ref, out_dtype: str = "f32", what: str = "") -> dict:
     assert c["max_abs_beyond_rounding"] <= ATOL, f"{what}: {c}"
     assert c["rel"] <= RTOL, f"{what}: {c}"
     return c
+
+
+def check_decode_rows(oracle, cache, q, lengths, picks, out, cache_dtype: str, theta: float = 1e6,
+                      kn=None, what: str = "") -> list:
+    """Decode outputs of (sequence, layer) rows against the oracle's decode
+    (src/cpu/model.js:103-123: RoPE(q) at position L, attention over the L
+    cached positions plus the appended one). The cache contents, including the
+    appended row at position L, are read back from the device, so a call may
+    fill its cache on the GPU; when `kn` (the new keys, [batch][layers][kv
+    heads][64], unrotated) is given, the appended key row must also equal the
+    oracle's RoPE(k) rounded to the cache dtype, bit for bit. q and out are
+    float arrays [batch][layers][heads][64]. Returns the comparisons."""
+    heads, hd = q.shape[2], q.shape[3]
+    kvh = cache.config.numKVHeads
+    res = []
+    for b, layer in picks:
+        L = int(lengths[b])
+        kb, vb = cache.read(layer, L + 1, seq=b)
+        kc = oracle.from_bits(kb, cache_dtype)
+        vc = oracle.from_bits(vb, cache_dtype)
+        qr = oracle.rope_rows(np.asarray(q[b, layer], np.float32).reshape(1, heads * hd), [L], hd, theta)
+        ref = oracle.decode_head_major(qr.reshape(-1), np.ascontiguousarray(kc), np.ascontiguousarray(vc), L + 1, L,
+                                       heads, kvh, hd)
+        res.append(assert_parity(np.asarray(out[b, layer]).reshape(-1), ref, "f32", f"{what} seq {b} layer {layer}"))
+        if kn is not None:
+            kr = oracle.rope_rows(np.asarray(kn[b, layer], np.float32).reshape(1, kvh * hd), [L], hd, theta)
+            want = oracle.to_bits(kr.reshape(kvh, hd), cache_dtype)
+            assert np.array_equal(kb[:, L], want), f"{what} seq {b} layer {layer}: appended key bits differ"
+    return res

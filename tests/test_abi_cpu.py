@@ -79,3 +79,14 @@ def test_status_names():
     lib = _lib.load()
     assert lib.b2a_status_name(2) == b"B2A_ERANGE"
     assert lib.b2a_status_name(3) == b"B2A_EBUSY"
+
+
+def test_noalloc_scratch_size_matches_header():
+    import re
+    with open(os.path.join(ROOT, "include", "b2a.h")) as f:
+        m = re.search(r"#define B2A_NOALLOC_SCRATCH_BYTES \(([0-9 *]+)\)", f.read())
+    assert m is not None
+    n = 1
+    for part in m.group(1).split("*"):
+        n *= int(part)
+    assert n == _lib.B2A_NOALLOC_SCRATCH_BYTES
