@@ -434,6 +434,9 @@ def run_ours(args) -> None:
                                     args)
     if not args.no_splitkv:
         line["split_kv"] = bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args)
+        # the same with 24 layers per step (one launch per rank), so that a GPU's
+        # share of the stream outweighs the exchange's fixed latency
+        line["split_kv_24"] = bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args, layers=24)
     if world == 1 and not args.no_prefill:
         line["prefill"] = bench_prefill(torch, b2a, ctx, stream, dev, pk, args)
     if world == 1 and not args.no_layer:
@@ -449,12 +452,12 @@ def run_ours(args) -> None:
                                 "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
                                                   "sample": sample1}}
     line["parity"] = parity
-    for key in ("split_kv", "prefill"):   # their own parity samples, gathered in one place
+    for key in ("split_kv", "split_kv_24", "prefill"):   # their own parity samples, gathered in one place
         if isinstance(line.get(key), dict) and "parity" in line[key]:
             parity[key] = line[key]["parity"]
     # the bulky objects first and the compact summaries last, so a reader of the
     # line's tail sees parity, split-KV and prefill
-    for key in ("kernels", "layer", "generation", "paged", "parity", "split_kv", "prefill"):
+    for key in ("kernels", "layer", "generation", "paged", "parity", "split_kv", "split_kv_24", "prefill"):
         if key in line:
             line[key] = line.pop(key)
     barrier()
@@ -559,33 +562,34 @@ def bench_paged(torch, b2a, ctx, stream, dev, rope, lengths, nb, q, kn, vn, out,
     return res
 
 
-def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict:
+def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args, layers: int = 1) -> dict:
     """8 sequences with a 32768-position f16 cache and one new
-    token each, the KV positions split across the ranks; per step: this rank's
-    partial (o, m, l) kernel, an NCCL all-gather of the partials, the LSE combine."""
+    token each, the KV positions split across the ranks (layers > 1: that many
+    layers per step, all in one launch per rank). One GPU: the plain decode call.
+    Several: the exchange inside the attention kernel (peer stores over NVLink),
+    with the NCCL all-gather path (partials kernel, all-gather, combine) beside it."""
     from b2a import dist as bd
     nseq, total = 8, 32768
     lo, hi = bd.position_slice(total, world, rank)
     n_local = hi - lo
-    last = rank == world - 1
     with torch.cuda.stream(stream):
-        cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(1, KVH, D, H), n_local + 1, batch=nseq, dtype="f16")
+        cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(layers, KVH, D, H), n_local + 1, batch=nseq, dtype="f16")
         rope = b2a.RopeTable(ctx, D, THETA, total + 1)
         kp, vp, _ = cache.pools()
         gen = torch.Generator(device=dev)
         gen.manual_seed(777 + rank)
-        shape = (nseq, 1, KVH, n_local + 1, D)
+        shape = (nseq, layers, KVH, n_local + 1, D)
         torch.as_tensor(_CAI(kp, shape, "<f2"), device=dev).normal_(generator=gen)
         torch.as_tensor(_CAI(vp, shape, "<f2"), device=dev).normal_(generator=gen)
         cache.setLengths([n_local] * nseq)
         g2 = torch.Generator(device=dev)
         g2.manual_seed(4242)   # the same query and new token on every rank
-        q = torch.randn(nseq, H, D, device=dev, generator=g2).half()
-        kn = torch.randn(nseq, KVH, D, device=dev, generator=g2).half()
-        vn = torch.randn(nseq, KVH, D, device=dev, generator=g2).half()
+        q = torch.randn(nseq, layers, H, D, device=dev, generator=g2).half()
+        kn = torch.randn(nseq, layers, KVH, D, device=dev, generator=g2).half()
+        vn = torch.randn(nseq, layers, KVH, D, device=dev, generator=g2).half()
         pos = torch.full((nseq,), total, dtype=torch.int32, device=dev)
-        local = torch.empty(nseq, H, D + 4, device=dev)
-        out = torch.empty(nseq, H, D, device=dev)
+        local = torch.empty(nseq, layers, H, D + 4, device=dev)
+        out = torch.empty(nseq, layers, H, D, device=dev)
     def timed(step_fn, n):
         """Device time of n back-to-back steps (max over ranks)."""
         torch.cuda.synchronize(dev)
@@ -610,7 +614,7 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
     peer, peer_error = None, None
     if world > 1:
         try:
-            peer = bd.PeerSplitKV(ctx, cache, rope, 0, H, rank, world)
+            peer = bd.PeerSplitKV(ctx, cache, rope, 0, H, rank, world, num_layers=layers)
         except RuntimeError as e:   # raised on every rank alike
             peer_error = str(e)[:200]
     if peer is not None:
@@ -630,7 +634,7 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
             peer.step(q, kn, vn, pos, out)
         ms = timed(graph.replay, steps)
         # the NCCL all-gather baseline (partials kernel, all-gather, combine kernel)
-        nccl = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world)
+        nccl = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world, num_layers=layers)
         with torch.cuda.stream(stream):
             for _ in range(max(3, args.warmup)):
                 nccl.step(q, kn, vn, pos, local, out)
@@ -641,7 +645,7 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
         peer.close()
     elif world > 1:
         # no peer mapping: the NCCL path is the measured one
-        nccl = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world)
+        nccl = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world, num_layers=layers)
         with torch.cuda.stream(stream):
             for _ in range(max(3, args.warmup)):
                 nccl.step(q, kn, vn, pos, local, out)
@@ -656,7 +660,7 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
         # one GPU holds the whole context: the plain decode call, whose kernel
         # splits the positions over the CTAs and merges the chunks itself
         def one():
-            b2a.attentionDecode(ctx, cache, rope, 0, q, kn, vn, out, H)
+            b2a.attentionDecode(ctx, cache, rope, 0, q, kn, vn, out, H, numLayers=layers)
         with torch.cuda.stream(stream):
             for _ in range(max(3, args.warmup)):
                 one()
@@ -666,16 +670,19 @@ def bench_splitkv(torch, dist, b2a, ctx, stream, dev, rank, world, args) -> dict
             kt = ctx.read_timing()
             ctx.enable_timing(False)
             ms = timed(one, steps)
-        extra = {"parity": parity_decode(torch, dev, kp, vp, shape, q.view(nseq, 1, H, D), out.view(nseq, 1, H, D),
-                                         [total] * nseq, [(b, 0) for b in range(nseq)])}
-    kv_bytes = nseq * KVH * (total + 1) * D * 2 * 2
+        picks = [(b, (5 * b) % layers) for b in range(nseq)]
+        extra = {"parity": parity_decode(torch, dev, kp, vp, shape, q, out, [total] * nseq, picks)}
+    kv_bytes = nseq * layers * KVH * (total + 1) * D * 2 * 2
     cache.close()
     rope.close()
-    return {"metric": "split-KV decode GB/s", "value": round(kv_bytes * steps / (ms / 1e3) / 1e9, 1),
-            "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps, **extra,
+    gbs = kv_bytes * steps / (ms / 1e3) / 1e9   # the whole context's bytes over the max-over-ranks time
+    return {"metric": "split-KV decode GB/s", "value": round(gbs, 1),
+            "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps,
+            "hbm_frac_per_gpu": round(gbs / world / peaks()["hbm_gbs"], 4), **extra,
             "kernels": {k: {"launches": v[0], "avg_ms": round(v[1] / v[0], 4)} for k, v in kt.items()},
-            "config": {"workload": "config5-split-kv-decode", "sequences": nseq, "kv_len": total,
-                       "cache_dtype": "f16", "layers": 1, "kv_bytes_per_step": kv_bytes,
+            "config": {"workload": "config5-split-kv-decode" + (f"-{layers}-layers" if layers > 1 else ""),
+                       "sequences": nseq, "kv_len": total,
+                       "cache_dtype": "f16", "layers": layers, "kv_bytes_per_step": kv_bytes,
                        "parallelism": f"context-parallel over {world} GPU(s)",
                        "collective": ("in-kernel exchange: peer stores of (o, m, l) partials + flags over NVLink, "
                                       "LSE combine in rank order (CUDA graph replay)" if peer is not None else

@@ -276,6 +276,16 @@ b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* cache, const 
                                         int layer, int num_heads, const void* q,
                                         const void* k_new, const void* v_new, b2a_dtype in_dtype,
                                         const int32_t* q_positions, float* partial, int flags);
+/* The same for layers [layer_begin, layer_begin + num_layers) in one launch
+ * (the per-layer decode dispatch of src/gpu/model.js:323-346, one call per
+ * decode step instead of one per layer): q [batch][num_layers][num_heads][64],
+ * k_new/v_new [batch][num_layers][num_kv_heads][64], partial
+ * [batch][num_layers][num_heads][head_dim + 4] (combine with
+ * b2a_lse_combine as batch * num_layers rows). */
+b2a_status b2a_attention_decode_partial_layers(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
+                                               int layer_begin, int num_layers, int num_heads, const void* q,
+                                               const void* k_new, const void* v_new, b2a_dtype in_dtype,
+                                               const int32_t* q_positions, float* partial, int flags);
 /* Log-sum-exp combine of `num_parts` partials laid out [num_parts][batch][num_heads][head_dim+4]
  * in ascending part order, into out [batch][num_heads][head_dim] (out_dtype). */
 b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch,
@@ -328,6 +338,10 @@ typedef struct b2a_exchange b2a_exchange;
 #define B2A_EXCHANGE_HANDLE_BYTES 64
 b2a_status b2a_exchange_create(b2a_ctx* ctx, int world, int rank, int batch, int num_heads, int num_kv_heads,
                                b2a_exchange** out);
+/* An exchange for calls that cover num_layers layers each
+ * (b2a_attention_decode_split_layers); b2a_exchange_create is num_layers 1. */
+b2a_status b2a_exchange_create_layers(b2a_ctx* ctx, int world, int rank, int batch, int num_layers,
+                                      int num_heads, int num_kv_heads, b2a_exchange** out);
 b2a_status b2a_exchange_handle(const b2a_exchange* ex, void* handle);
 b2a_status b2a_exchange_open(b2a_exchange* ex, const void* handles);
 /* Wires rank `peer` of ex to another exchange object of this process on the same
@@ -343,6 +357,17 @@ b2a_status b2a_attention_decode_split(b2a_ctx* ctx, b2a_kvcache* cache, const b2
                                       int num_heads, const void* q, const void* k_new, const void* v_new,
                                       b2a_dtype in_dtype, const int32_t* q_positions, b2a_exchange* ex,
                                       void* out, b2a_dtype out_dtype, int flags);
+/* One decode step over layers [layer_begin, layer_begin + num_layers) in one
+ * launch (the per-layer dispatch of src/gpu/model.js:323-346 folded into one
+ * call): layouts as b2a_attention_decode_partial_layers, out
+ * [batch][num_layers][num_heads][head_dim]; the exchange must have been made
+ * for num_layers, and its (sequence, layer, KV head) groups must fit on the
+ * GPU at once (three CTAs per SM). */
+b2a_status b2a_attention_decode_split_layers(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
+                                             int layer_begin, int num_layers, int num_heads, const void* q,
+                                             const void* k_new, const void* v_new, b2a_dtype in_dtype,
+                                             const int32_t* q_positions, b2a_exchange* ex, void* out,
+                                             b2a_dtype out_dtype, int flags);
 
 /* ---- the Qwen2 decoder around the attention path ------------------------------
  * ReferenceModel.forward / generate (src/cpu/model.js:55-187) and

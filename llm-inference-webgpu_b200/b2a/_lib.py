@@ -65,16 +65,20 @@ SIGNATURES = {
     "b2a_attention_prefill_batch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _i, _i]),
     "b2a_grouped_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i]),
     "b2a_attention_decode_partial": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i]),
+    "b2a_attention_decode_partial_layers": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i]),
     "b2a_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _i, _i]),
     "b2a_quantize_int8_per_channel": (_i, [_vp, _i, _i, _vp, _vp]),
     "b2a_linear_int8": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp, _i, _i]),
     "b2a_qkv_int8": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i]),
     "b2a_exchange_create": (_i, [_vp, _i, _i, _i, _i, _i, _pp]),
+    "b2a_exchange_create_layers": (_i, [_vp, _i, _i, _i, _i, _i, _i, _pp]),
     "b2a_exchange_handle": (_i, [_vp, _vp]),
     "b2a_exchange_open": (_i, [_vp, _vp]),
     "b2a_exchange_connect_local": (_i, [_vp, _i, _vp]),
     "b2a_exchange_destroy": (_i, [_vp]),
     "b2a_attention_decode_split": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i]),
+    "b2a_attention_decode_split_layers": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i,
+                                                _i]),
     "b2a_model_create": (_i, [_vp, _vp, _i, _pp]),
     "b2a_model_destroy": (_i, [_vp]),
     "b2a_model_load_layer": (_i, [_vp, _i, _vp, _i]),

@@ -115,49 +115,49 @@ def attentionPrefillBatch(ctx: Context, cache: GpuKVCache, rope: RopeTable, laye
                                              DTYPES[oa.dtype], _where(qa, ka, va, oa)))
 
 
+def _positions(ctx: Context, q_positions, where: int):
+    """The per-sequence absolute positions as int32 where the call's data lives."""
+    if where == _lib.B2A_HOST:
+        pos = np.ascontiguousarray(q_positions, dtype=np.int32)
+        return pos.ctypes.data, pos
+    import torch
+    pos = q_positions if isinstance(q_positions, torch.Tensor) else torch.as_tensor(
+        np.asarray(q_positions, np.int32), device=f"cuda:{ctx.device}")
+    pos = pos.to(torch.int32).contiguous()
+    return pos.data_ptr(), pos
+
+
 def decodePartial(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, q_positions,
-                  partial, numHeads: int, dtype: str | None = None) -> None:
-    """Split-KV partial over this cache's positions (see b2a_attention_decode_partial).
-    partial [batch, numHeads, headDim+4] f32."""
+                  partial, numHeads: int, dtype: str | None = None, numLayers: int = 1) -> None:
+    """Split-KV partial over this cache's positions (see b2a_attention_decode_partial;
+    numLayers > 1: b2a_attention_decode_partial_layers over layers [layer, layer+numLayers)).
+    partial [batch, numHeads, headDim+4] f32 ([batch, numLayers, numHeads, headDim+4])."""
     qa, ka, va, pa = _arg(q, dtype), _arg(k_new, dtype), _arg(v_new, dtype), _arg(partial, writable=True)
     in_dt = _same_dtype(qa, ka, va)
     where = _where(qa, ka, va, pa)
-    if where == _lib.B2A_HOST:
-        pos = np.ascontiguousarray(q_positions, dtype=np.int32)
-        pos_ptr, keep = pos.ctypes.data, pos
-    else:
-        import torch
-        pos = q_positions if isinstance(q_positions, torch.Tensor) else torch.as_tensor(
-            np.asarray(q_positions, np.int32), device=f"cuda:{ctx.device}")
-        pos = pos.to(torch.int32).contiguous()
-        pos_ptr, keep = pos.data_ptr(), pos
-    check(load().b2a_attention_decode_partial(ctx.handle, cache.handle, rope.handle, layer, numHeads, qa.ptr,
-                                              ka.ptr if ka else None, va.ptr if va else None, DTYPES[in_dt],
-                                              pos_ptr, pa.ptr, where))
+    pos_ptr, keep = _positions(ctx, q_positions, where)
+    check(load().b2a_attention_decode_partial_layers(ctx.handle, cache.handle, rope.handle, layer, numLayers,
+                                                     numHeads, qa.ptr, ka.ptr if ka else None,
+                                                     va.ptr if va else None, DTYPES[in_dt], pos_ptr, pa.ptr, where))
     del keep
 
 
 def decodeSplit(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, q_positions,
-                exchange, out, numHeads: int, dtype: str | None = None, out_dtype: str | None = None) -> None:
+                exchange, out, numHeads: int, dtype: str | None = None, out_dtype: str | None = None,
+                numLayers: int = 1) -> None:
     """One split-KV decode step with the cross-rank exchange inside the kernel
-    (b2a_attention_decode_split): this rank's positions, then every rank's
-    partials combined in rank order into out [batch, numHeads, headDim]."""
+    (b2a_attention_decode_split_layers over layers [layer, layer+numLayers)): this
+    rank's positions, then every rank's partials combined in rank order into
+    out [batch, numHeads, headDim] ([batch, numLayers, numHeads, headDim])."""
     qa, ka, va = _arg(q, dtype), _arg(k_new, dtype), _arg(v_new, dtype)
     oa = _arg(out, out_dtype, writable=True)
     in_dt = _same_dtype(qa, ka, va)
     where = _where(qa, ka, va, oa)
-    if where == _lib.B2A_HOST:
-        pos = np.ascontiguousarray(q_positions, dtype=np.int32)
-        pos_ptr, keep = pos.ctypes.data, pos
-    else:
-        import torch
-        pos = q_positions if isinstance(q_positions, torch.Tensor) else torch.as_tensor(
-            np.asarray(q_positions, np.int32), device=f"cuda:{ctx.device}")
-        pos = pos.to(torch.int32).contiguous()
-        pos_ptr, keep = pos.data_ptr(), pos
-    check(load().b2a_attention_decode_split(ctx.handle, cache.handle, rope.handle, layer, numHeads, qa.ptr,
-                                            ka.ptr if ka else None, va.ptr if va else None, DTYPES[in_dt], pos_ptr,
-                                            exchange.handle, oa.ptr, DTYPES[oa.dtype], where))
+    pos_ptr, keep = _positions(ctx, q_positions, where)
+    check(load().b2a_attention_decode_split_layers(ctx.handle, cache.handle, rope.handle, layer, numLayers, numHeads,
+                                                   qa.ptr, ka.ptr if ka else None, va.ptr if va else None,
+                                                   DTYPES[in_dt], pos_ptr, exchange.handle, oa.ptr, DTYPES[oa.dtype],
+                                                   where))
     del keep
 
 

@@ -95,17 +95,20 @@ def nccl_gather_fn(group=None):
 
 
 def cuda_split_kv(ctx, cache, rope, layer: int, num_heads: int, rank: int, world: int, group=None,
-                  dtype: str | None = None) -> SplitKVDecode:
-    """SplitKVDecode wired to libb2a's partial and combine kernels and NCCL."""
+                  dtype: str | None = None, num_layers: int = 1) -> SplitKVDecode:
+    """SplitKVDecode wired to libb2a's partial and combine kernels and NCCL, over
+    layers [layer, layer + num_layers) per step (partials [batch, layers, heads, 68])."""
     from . import attention as A
 
     head_dim = cache.config.headDim
 
     def partial_fn(q, k_new, v_new, positions, out_partial):
-        A.decodePartial(ctx, cache, rope, layer, q, k_new, v_new, positions, out_partial, num_heads, dtype=dtype)
+        A.decodePartial(ctx, cache, rope, layer, q, k_new, v_new, positions, out_partial, num_heads, dtype=dtype,
+                        numLayers=num_layers)
 
     def combine_fn(stacked, out):
-        A.lseCombine(ctx, stacked, world, stacked.shape[1], num_heads, head_dim, out)
+        rows = stacked.shape[1] * num_layers   # (sequence, layer) rows
+        A.lseCombine(ctx, stacked, world, rows, num_heads, head_dim, out)
 
     return SplitKVDecode(rank, world, partial_fn, nccl_gather_fn(group), combine_fn)
 
@@ -144,15 +147,16 @@ class PeerSplitKV:
     launch per rank; every rank must call it the same number of times."""
 
     def __init__(self, ctx, cache, rope, layer: int, num_heads: int, rank: int, world: int, group=None,
-                 dtype: str | None = None):
+                 dtype: str | None = None, num_layers: int = 1):
         from .runtime import Exchange
 
         self.ctx, self.cache, self.rope, self.layer = ctx, cache, rope, layer
         self.num_heads, self.rank, self.world, self.dtype = num_heads, rank, world, dtype
+        self.num_layers = num_layers
         self.exchange = None
         err = None
         try:
-            self.exchange = Exchange(ctx, world, rank, cache.batch, num_heads, cache.config.numKVHeads)
+            self.exchange = Exchange(ctx, world, rank, cache.batch, num_heads, cache.config.numKVHeads, num_layers)
             handle = self.exchange.handle_bytes()
         except Exception as e:   # every rank must still reach the collectives below
             err, handle = e, bytes(64)
@@ -175,7 +179,7 @@ class PeerSplitKV:
 
         A.decodeSplit(self.ctx, self.cache, self.rope, self.layer, q, k_new if self.holds_new_token else None,
                       v_new if self.holds_new_token else None, positions, self.exchange, out, self.num_heads,
-                      dtype=self.dtype)
+                      dtype=self.dtype, numLayers=self.num_layers)
         return out
 
     def close(self) -> None:

@@ -307,10 +307,13 @@ class Exchange:
     one, shares handle() with the others, and calls open() with all handles in
     rank order."""
 
-    def __init__(self, ctx: Context, world: int, rank: int, batch: int, numHeads: int, numKVHeads: int):
+    def __init__(self, ctx: Context, world: int, rank: int, batch: int, numHeads: int, numKVHeads: int,
+                 numLayers: int = 1):
         self.ctx = ctx
         h = ctypes.c_void_p()
-        check(ctx._lib.b2a_exchange_create(ctx.handle, world, rank, batch, numHeads, numKVHeads, ctypes.byref(h)))
+        check(ctx._lib.b2a_exchange_create_layers(ctx.handle, world, rank, batch, numLayers, numHeads, numKVHeads,
+                                                  ctypes.byref(h)))
+        self.numLayers = numLayers
         self.handle = h
         self.world, self.rank = world, rank
         ctx._children.add(self)

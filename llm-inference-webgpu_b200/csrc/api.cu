@@ -16,7 +16,7 @@
 // step / done counters; peer[r] is rank r's allocation as mapped here.
 struct b2a_exchange {
   int device = 0;
-  int world = 1, rank = 0, batch = 0, heads = 0, kv_heads = 0, rows = 0, groups = 0;
+  int world = 1, rank = 0, batch = 0, layers = 1, heads = 0, kv_heads = 0, rows = 0, groups = 0;
   void* base = nullptr;
   size_t bytes = 0, c_off = 0;
   void* peer[b2a::kMaxWorld] = {};
@@ -543,15 +543,17 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
 // decode): ex == nullptr writes the partials [batch][heads][D+4] (fuse mode 1);
 // otherwise the kernel exchanges them with the other ranks and writes the
 // combined output in out_dtype (fuse mode 2).
-b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_heads,
-                            const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
+b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer, int num_layers,
+                            int num_heads, const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
                             const int32_t* q_positions, b2a_exchange* ex, void* out, b2a_dtype out_dtype, int flags) {
   b2a_status s = check_cache_shape(c, rope, num_heads);
   if (s != B2A_OK) return s;
   if (q == nullptr || out == nullptr || q_positions == nullptr) return fail(B2A_EINVAL, "null argument");
   if ((k_new == nullptr) != (v_new == nullptr)) return fail(B2A_EINVAL, "give both new keys and values, or neither");
   if (!valid_dtype(in_dtype)) return fail(B2A_EINVAL, "unknown dtype");
-  if (layer < 0 || layer >= c->layers) return fail(B2A_EINVAL, "layer %d out of range [0, %d)", layer, c->layers);
+  if (layer < 0 || num_layers < 1 || layer + num_layers > c->layers) {
+    return fail(B2A_EINVAL, "layers [%d, %d) outside the cache's %d", layer, layer + num_layers, c->layers);
+  }
   const int extra = k_new ? 1 : 0;
   int max_keys = 0;
   for (int b = 0; b < c->batch; b++) {
@@ -573,7 +575,7 @@ b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, 
   AttnParams p = base_params(ctx, c, rope);
   p.seq_begin = 0;
   p.batch = c->batch;
-  p.num_layers = 1;
+  p.num_layers = num_layers;
   p.layer_begin = layer;
   p.tokens = 1;
   p.heads = num_heads;
@@ -598,9 +600,10 @@ b2a_status decode_positions(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, 
     p.x_rows = ex->rows;
   }
   const size_t ies = dtype_size(in_dtype);
-  const size_t q_bytes = static_cast<size_t>(c->batch) * num_heads * c->head_dim * ies;
-  const size_t kv_bytes = static_cast<size_t>(c->batch) * c->kv_heads * c->head_dim * ies;
-  const size_t out_bytes = static_cast<size_t>(c->batch) * num_heads *
+  const size_t rows_bl = static_cast<size_t>(c->batch) * num_layers;   // (sequence, layer) pairs
+  const size_t q_bytes = rows_bl * num_heads * c->head_dim * ies;
+  const size_t kv_bytes = rows_bl * c->kv_heads * c->head_dim * ies;
+  const size_t out_bytes = rows_bl * num_heads *
                            (ex ? c->head_dim * dtype_size(out_dtype) : (c->head_dim + 4) * sizeof(float));
   void* dout = out;
   if (flags == B2A_HOST) {
@@ -1669,8 +1672,17 @@ b2a_status b2a_attention_decode_partial(b2a_ctx* ctx, b2a_kvcache* c, const b2a_
                                         const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
                                         const int32_t* q_positions, float* partial, int flags) {
   if (partial == nullptr) return fail(B2A_EINVAL, "null argument");
-  return decode_positions(ctx, c, rope, layer, num_heads, q, k_new, v_new, in_dtype, q_positions, nullptr, partial,
+  return decode_positions(ctx, c, rope, layer, 1, num_heads, q, k_new, v_new, in_dtype, q_positions, nullptr, partial,
                           B2A_F32, flags);
+}
+
+b2a_status b2a_attention_decode_partial_layers(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer_begin,
+                                               int num_layers, int num_heads, const void* q, const void* k_new,
+                                               const void* v_new, b2a_dtype in_dtype, const int32_t* q_positions,
+                                               float* partial, int flags) {
+  if (partial == nullptr) return fail(B2A_EINVAL, "null argument");
+  return decode_positions(ctx, c, rope, layer_begin, num_layers, num_heads, q, k_new, v_new, in_dtype, q_positions,
+                          nullptr, partial, B2A_F32, flags);
 }
 
 b2a_status b2a_quantize_int8_per_channel(const float* w, int rows, int cols, int8_t* codes, float* scales) {
@@ -1720,13 +1732,19 @@ b2a_status b2a_qkv_int8(b2a_ctx* ctx, const int8_t* codes, const void* scales, b
 
 b2a_status b2a_exchange_create(b2a_ctx* ctx, int world, int rank, int batch, int num_heads, int num_kv_heads,
                                b2a_exchange** out) {
+  return b2a_exchange_create_layers(ctx, world, rank, batch, 1, num_heads, num_kv_heads, out);
+}
+
+b2a_status b2a_exchange_create_layers(b2a_ctx* ctx, int world, int rank, int batch, int num_layers, int num_heads,
+                                      int num_kv_heads, b2a_exchange** out) {
   if (ctx == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
   *out = nullptr;
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world) {
     return fail(B2A_EINVAL, "rank %d of world %d: the exchange takes 1..%d ranks", rank, world, kMaxWorld);
   }
-  if (batch < 1 || num_kv_heads < 1 || num_heads < 1 || num_heads % num_kv_heads != 0) {
-    return fail(B2A_EINVAL, "bad exchange shape: batch %d, heads %d, kv heads %d", batch, num_heads, num_kv_heads);
+  if (batch < 1 || num_layers < 1 || num_kv_heads < 1 || num_heads < 1 || num_heads % num_kv_heads != 0) {
+    return fail(B2A_EINVAL, "bad exchange shape: batch %d, layers %d, heads %d, kv heads %d", batch, num_layers,
+                num_heads, num_kv_heads);
   }
   CallGuard g(ctx);
   if (!g.ok()) return g.busy_status();
@@ -1736,10 +1754,11 @@ b2a_status b2a_exchange_create(b2a_ctx* ctx, int world, int rank, int batch, int
   ex->world = world;
   ex->rank = rank;
   ex->batch = batch;
+  ex->layers = num_layers;
   ex->heads = num_heads;
   ex->kv_heads = num_kv_heads;
-  ex->rows = batch * num_heads;
-  ex->groups = batch * num_kv_heads;
+  ex->rows = batch * num_layers * num_heads;
+  ex->groups = batch * num_layers * num_kv_heads;
   const size_t x_bytes = 2ull * world * ex->rows * (64 + 4) * sizeof(uint64_t);
   ex->c_off = (x_bytes + 255) & ~size_t(255);
   ex->bytes = ex->c_off + 256;
@@ -1807,7 +1826,18 @@ b2a_status b2a_attention_decode_split(b2a_ctx* ctx, b2a_kvcache* c, const b2a_ro
                                       const void* q, const void* k_new, const void* v_new, b2a_dtype in_dtype,
                                       const int32_t* q_positions, b2a_exchange* ex, void* out, b2a_dtype out_dtype,
                                       int flags) {
+  return b2a_attention_decode_split_layers(ctx, c, rope, layer, 1, num_heads, q, k_new, v_new, in_dtype, q_positions,
+                                           ex, out, out_dtype, flags);
+}
+
+b2a_status b2a_attention_decode_split_layers(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer_begin,
+                                             int num_layers, int num_heads, const void* q, const void* k_new,
+                                             const void* v_new, b2a_dtype in_dtype, const int32_t* q_positions,
+                                             b2a_exchange* ex, void* out, b2a_dtype out_dtype, int flags) {
   if (ex == nullptr || out == nullptr) return fail(B2A_EINVAL, "null argument");
+  if (num_layers != ex->layers) {
+    return fail(B2A_EINVAL, "the exchange was made for %d layers per call; the call has %d", ex->layers, num_layers);
+  }
   if (!valid_dtype(out_dtype)) return fail(B2A_EINVAL, "unknown dtype");
   if (c != nullptr && (c->batch != ex->batch || c->kv_heads != ex->kv_heads || num_heads != ex->heads)) {
     return fail(B2A_EINVAL, "the exchange was made for batch %d, %d/%d heads; the call has batch %d, %d/%d", ex->batch,
@@ -1817,8 +1847,8 @@ b2a_status b2a_attention_decode_split(b2a_ctx* ctx, b2a_kvcache* c, const b2a_ro
   for (int r = 0; r < ex->world; r++) {
     if (ex->peer[r] == nullptr) return fail(B2A_EINVAL, "exchange rank %d is not connected; open the handles first", r);
   }
-  return decode_positions(ctx, c, rope, layer, num_heads, q, k_new, v_new, in_dtype, q_positions, ex, out, out_dtype,
-                          flags);
+  return decode_positions(ctx, c, rope, layer_begin, num_layers, num_heads, q, k_new, v_new, in_dtype, q_positions, ex,
+                          out, out_dtype, flags);
 }
 
 b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch, int num_heads, int head_dim,

@@ -22,12 +22,56 @@ class _CAI:
 
 
 def fill(cache, k, v):
-    """k, v [batch, KVH, n, D] f16 into positions 0..n-1 of layer 0."""
+    """k, v [batch, KVH, n, D] (one layer) or [batch, layers, KVH, n, D] f16 into
+    positions 0..n-1."""
+    if k.dim() == 4:
+        k, v = k[:, None], v[:, None]
+    layers = k.shape[1]
     kp, vp, _ = cache.pools()
-    shape = (cache.batch, 1, KVH, cache.capacity, D)
-    torch.as_tensor(_CAI(kp, shape), device=k.device)[:, 0, :, :k.shape[2]].copy_(k)
-    torch.as_tensor(_CAI(vp, shape), device=v.device)[:, 0, :, :v.shape[2]].copy_(v)
-    cache.setLengths([k.shape[2]] * cache.batch)
+    shape = (cache.batch, layers, KVH, cache.capacity, D)
+    torch.as_tensor(_CAI(kp, shape), device=k.device)[:, :, :, :k.shape[3]].copy_(k)
+    torch.as_tensor(_CAI(vp, shape), device=v.device)[:, :, :, :v.shape[3]].copy_(v)
+    cache.setLengths([k.shape[3]] * cache.batch)
+
+
+def multilayer(ctx, dev, rank, world, failures):
+    """Three layers per call through one exchange: the peer path and the NCCL
+    path against one single-GPU decode of all three layers."""
+    batch, layers, total = 3, 3, 2100
+    lo, hi = bd.position_slice(total, world, rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(6)
+    kfull = torch.randn(batch, layers, KVH, total, D, generator=g, device=dev).half()
+    vfull = torch.randn(batch, layers, KVH, total, D, generator=g, device=dev).half()
+    q = torch.randn(batch, layers, H, D, generator=g, device=dev).half()
+    kn = torch.randn(batch, layers, KVH, D, generator=g, device=dev).half()
+    vn = torch.randn(batch, layers, KVH, D, generator=g, device=dev).half()
+    pos = torch.full((batch,), total, dtype=torch.int32, device=dev)
+    rope = b2a.RopeTable(ctx, D, THETA, total + 1)
+    cache = b2a.GpuKVCache(ctx, b2a.CacheConfig(layers, KVH, D, H), hi - lo + 1, batch=batch, dtype="f16")
+    fill(cache, kfull[:, :, :, lo:hi].contiguous(), vfull[:, :, :, lo:hi].contiguous())
+    peer = bd.PeerSplitKV(ctx, cache, rope, 0, H, rank, world, num_layers=layers)
+    out_peer = torch.empty(batch, layers, H, D, device=dev)
+    for _ in range(3):
+        peer.step(q, kn, vn, pos, out_peer)
+    nccl = bd.cuda_split_kv(ctx, cache, rope, 0, H, rank, world, num_layers=layers)
+    local = torch.empty(batch, layers, H, D + 4, device=dev)
+    out_nccl = torch.empty(batch, layers, H, D, device=dev)
+    nccl.step(q, kn, vn, pos, local, out_nccl)
+    full = b2a.GpuKVCache(ctx, b2a.CacheConfig(layers, KVH, D, H), total + 1, batch=batch, dtype="f16")
+    fill(full, kfull, vfull)
+    out_full = torch.empty(batch, layers, H, D, device=dev)
+    b2a.attentionDecode(ctx, full, rope, 0, q, kn, vn, out_full, H, numLayers=layers)
+    ctx.synchronize()
+    torch.cuda.synchronize(dev)
+    d_peer = (out_peer - out_full).abs().max().item()
+    d_nccl = (out_nccl - out_full).abs().max().item()
+    if not d_peer <= 2e-3:
+        failures.append(f"3-layer peer exchange off by {d_peer}")
+    if not d_nccl <= 2e-3:
+        failures.append(f"3-layer nccl path off by {d_nccl}")
+    peer.close()
+    return d_peer, d_nccl
 
 
 def main():
@@ -74,12 +118,14 @@ def main():
         failures.append(f"peer exchange off by {d_peer}")
     if not d_nccl <= 2e-3:
         failures.append(f"nccl path off by {d_nccl}")
+    with torch.cuda.stream(stream):
+        m_peer, m_nccl = multilayer(ctx, dev, rank, world, failures)
     gathered = torch.empty(world, batch, H, D, device=dev)
     dist.all_gather_into_tensor(gathered.view(world * batch, H, D), out_peer)
     if not all(torch.equal(gathered[0], gathered[r]) for r in range(world)):
         failures.append("ranks disagree")
-    print(f"rank {rank}: peer {d_peer:.2e} nccl {d_nccl:.2e} {'FAIL ' + '; '.join(failures) if failures else 'ok'}",
-          flush=True)
+    print(f"rank {rank}: peer {d_peer:.2e} nccl {d_nccl:.2e} 3-layer peer {m_peer:.2e} nccl {m_nccl:.2e} "
+          f"{'FAIL ' + '; '.join(failures) if failures else 'ok'}", flush=True)
     peer.close()
     dist.destroy_process_group()
     sys.exit(1 if failures else 0)

@@ -414,6 +414,39 @@ def test_split_exchange_single_rank_matches_decode(ctx, rope, oracle):
     ex.close()
 
 
+def test_split_exchange_single_rank_several_layers(ctx, rope, oracle):
+    """Several layers per call (b2a_attention_decode_split_layers and
+    b2a_attention_decode_partial_layers): one exchange covers every (sequence,
+    layer, KV head) group of the call; both paths against the oracle."""
+    batch, layers, L, dtype = 3, 3, 1500, "f16"
+    c = b2a.GpuKVCache(ctx, cfg(layers), L + 1, batch=batch, dtype=dtype)
+    hk, hv = _fill_cache(ctx, c, oracle, [L] * batch, layers, dtype, 720)
+    q = oracle.round_to(oracle.normal_array(batch * layers * H * D, 45), dtype).reshape(batch, layers, H, D)
+    kn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 46), dtype).reshape(batch, layers, KVH, D)
+    vn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 47), dtype).reshape(batch, layers, KVH, D)
+    pos = np.full(batch, L, np.int32)
+    ex = b2a.Exchange(ctx, 1, 0, batch, H, KVH, numLayers=layers)
+    out = np.empty((batch, layers, H, D), np.float32)
+    for _ in range(2):
+        b2a.decodeSplit(ctx, c, rope, 0, oracle.to_bits(q, dtype), oracle.to_bits(kn, dtype),
+                        oracle.to_bits(vn, dtype), pos, ex, out, H, dtype=dtype, numLayers=layers)
+    partial = np.empty((batch, layers, H, D + 4), np.float32)
+    b2a.decodePartial(ctx, c, rope, 0, oracle.to_bits(q, dtype), oracle.to_bits(kn, dtype), oracle.to_bits(vn, dtype),
+                      pos, partial, H, dtype=dtype, numLayers=layers)
+    comb = np.empty((batch, layers, H, D), np.float32)
+    b2a.lseCombine(ctx, partial, 1, batch * layers, H, D, comb)
+    for b in range(batch):
+        for layer in range(layers):
+            ref, _, _ = _oracle_decode(oracle, q[b, layer], kn[b, layer], vn[b, layer], hk[b, layer], hv[b, layer],
+                                       L, dtype)
+            assert_parity(out[b, layer].reshape(-1), ref, "f32", f"exchange seq {b} layer {layer}")
+            assert_parity(comb[b, layer].reshape(-1), ref, "f32", f"partials seq {b} layer {layer}")
+    with pytest.raises(b2a.B2AError):   # an exchange made for 3 layers refuses a 1-layer call
+        b2a.decodeSplit(ctx, c, rope, 0, oracle.to_bits(q[:, 0], dtype), None, None, pos, ex,
+                        np.empty((batch, H, D), np.float32), H, dtype=dtype)
+    ex.close()
+
+
 def test_split_exchange_wait_gives_up_with_error(ctx, rope, oracle):
     """A rank whose peer never arrives: rank 0 of a two-rank exchange whose
     rank 1 is a second exchange object that no kernel ever serves. The kernel's
