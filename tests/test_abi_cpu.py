@@ -90,3 +90,22 @@ def test_noalloc_scratch_size_matches_header():
     for part in m.group(1).split("*"):
         n *= int(part)
     assert n == _lib.B2A_NOALLOC_SCRATCH_BYTES
+
+
+def test_napi_addon_compiles_against_the_header(tmp_path):
+    """addon/b2a_napi.c (the Node-API binding; runtime-unverified: no Node here)
+    compiles warning-free against include/b2a.h and exports the module entry."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no gcc")
+    src = os.path.join(ROOT, "addon", "b2a_napi.c")
+    obj = str(tmp_path / "napi.o")
+    subprocess.run([gcc, "-c", "-O2", "-std=c11", "-Wall", "-Wextra", "-Werror", "-fPIC", "-fvisibility=hidden",
+                    "-I", os.path.join(ROOT, "include"), src, "-o", obj], check=True)
+    syms = subprocess.run(["nm", obj], check=True, capture_output=True, text=True).stdout
+    assert " T napi_register_module_v1" in syms
+    # every libb2a entry the addon calls is one include/b2a.h declares
+    called = set(re.findall(r"\b(b2a_[a-z_0-9]+)\s*\(", open(src).read()))
+    assert called and called <= set(declared_symbols()), called - set(declared_symbols())
