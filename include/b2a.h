@@ -207,6 +207,24 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope
                                 const void* q, const void* k_new, const void* v_new,
                                 b2a_dtype in_dtype, void* out, b2a_dtype out_dtype, int flags);
 
+/* ---- host-pointer decode that returns before the results are back ----------
+ * b2a_attention_decode with B2A_HOST pointers and the same layouts and
+ * results, except that the call only enqueues the work: the uploads of q and
+ * the new keys/values, the attention kernels and the download of `out`. The
+ * reference's readback (src/gpu/device.js:253-270) makes every step wait for
+ * its results; a serving loop that keeps its own host buffers can instead let
+ * consecutive steps overlap on the GPU (one step's uploads and downloads run
+ * under its neighbours' kernels; two device staging slots are used in turn).
+ * Until b2a_synchronize(ctx) returns, the caller must not change q, k_new or
+ * v_new nor read `out` of any call made since the last synchronisation (use
+ * separate host buffers for calls in flight). Pinned host memory keeps the
+ * copies asynchronous. A device-side wait that gave up is reported by
+ * b2a_synchronize. */
+b2a_status b2a_attention_decode_host_async(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope,
+                                           int layer_begin, int num_layers, int num_heads,
+                                           const void* q, const void* k_new, const void* v_new,
+                                           b2a_dtype in_dtype, void* out, b2a_dtype out_dtype);
+
 /* ---- decode that allocates nothing ------------------------------------------
  * No counterpart in the reference: its engine owns its WebGPU buffers itself.
  * Same work and arguments as b2a_attention_decode, for callers that cannot

@@ -61,6 +61,7 @@ SIGNATURES = {
     "b2a_append_rope": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _i]),
     "b2a_attention_decode": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i]),
     "b2a_attention_decode_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i]),
+    "b2a_attention_decode_host_async": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i]),
     "b2a_attention_prefill": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _i, _i]),
     "b2a_attention_prefill_batch": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _i, _i]),
     "b2a_grouped_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i]),

@@ -90,6 +90,24 @@ def attentionDecode(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int
                                       DTYPES[oa.dtype], _where(qa, ka, va, oa)))
 
 
+def attentionDecodeAsync(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, out,
+                         numHeads: int, numLayers: int = 1, dtype: str | None = None,
+                         out_dtype: str | None = None) -> None:
+    """attentionDecode on host arrays (pinned torch tensors keep the copies
+    asynchronous) that returns once the work is enqueued
+    (b2a_attention_decode_host_async): consecutive calls overlap on the GPU.
+    The caller must keep q/k_new/v_new unchanged and not read `out` until
+    ctx.synchronize()."""
+    qa, ka, va = _arg(q, dtype), _arg(k_new, dtype), _arg(v_new, dtype)
+    oa = _arg(out, out_dtype or dtype, writable=True)
+    in_dt = _same_dtype(qa, ka, va)
+    if _where(qa, ka, va, oa) != _lib.B2A_HOST:
+        raise ValueError("attentionDecodeAsync takes host arrays")
+    check(load().b2a_attention_decode_host_async(ctx.handle, cache.handle, rope.handle, layer, numLayers, numHeads,
+                                                 qa.ptr, ka.ptr if ka else None, va.ptr if va else None,
+                                                 DTYPES[in_dt], oa.ptr, DTYPES[oa.dtype]))
+
+
 def attentionPrefill(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k, v, out, count: int,
                      numHeads: int, seq: int = 0, dtype: str | None = None, out_dtype: str | None = None) -> None:
     """Causal attention of `count` new tokens of one sequence over past+count positions,

@@ -222,6 +222,9 @@ b2a_status take_error_word(b2a_ctx* ctx) {
 b2a_status check_device_error(b2a_ctx* ctx) {
   b2a_status s = enqueue_error_read(ctx);
   if (s != B2A_OK) return s;
+  // downloads of asynchronous host-pointer calls run on their own stream
+  if (ctx->copy_out) B2A_CUDA(cudaStreamSynchronize(ctx->copy_out), "waiting for the downloads");
+  if (ctx->copy_in) B2A_CUDA(cudaStreamSynchronize(ctx->copy_in), "waiting for the uploads");
   B2A_CUDA(cudaStreamSynchronize(ctx->stream), "waiting for the stream");
   return take_error_word(ctx);
 }
@@ -401,7 +404,7 @@ b2a_status run_split_kv(b2a_ctx* ctx, const b2a_kvcache* c, AttnParams& p, int m
 // whole batch; q_seq / kv_seq / out_seq are the bytes per sequence.
 b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnParams& p, const void* hq,
                                  const void* hk, const void* hv, void* hout, void* dout, int out_dtype, size_t q_seq,
-                                 size_t kv_seq, size_t out_seq) {
+                                 size_t kv_seq, size_t out_seq, int async_slot) {
   const int batch = p.batch;
   const int layers = p.num_layers;
   const size_t seq_bytes = q_seq + (hk ? 2 * kv_seq : 0) + out_seq;
@@ -433,10 +436,17 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
     B2A_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "creating pipeline events");
     ctx->pipe_events.push_back(e);
   }
-  // uploads wait for earlier work on the context's stream (it may still read the staging buffer)
-  cudaEvent_t start = ctx->pipe_events[2 * groups];
-  B2A_CUDA(cudaEventRecord(start, ctx->stream), "ordering the upload");
-  B2A_CUDA(cudaStreamWaitEvent(ctx->copy_in, start, 0), "ordering the upload");
+  if (async_slot < 0) {
+    // uploads wait for earlier work on the context's stream (it may still read the staging buffer)
+    cudaEvent_t start = ctx->pipe_events[2 * groups];
+    B2A_CUDA(cudaEventRecord(start, ctx->stream), "ordering the upload");
+    B2A_CUDA(cudaStreamWaitEvent(ctx->copy_in, start, 0), "ordering the upload");
+  } else if (ctx->async_used[async_slot]) {
+    // this staging slot's previous call has downloaded its last result (and
+    // so run its last kernel): the uploads may overwrite it; the other slot's
+    // call may still be running, which is what lets consecutive calls overlap
+    B2A_CUDA(cudaStreamWaitEvent(ctx->copy_in, ctx->async_free[async_slot], 0), "ordering the upload");
+  }
   const char* src_q = static_cast<const char*>(hq);
   char* dst_q = static_cast<char*>(const_cast<void*>(p.q));
   if (by_layer) {
@@ -480,6 +490,11 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
       B2A_CUDA(cudaMemcpy2DAsync(static_cast<char*>(hout) + l0 * ol, out_seq, gout, n * ol, n * ol, batch,
                                  cudaMemcpyDeviceToHost, ctx->copy_out),
                "copying results to the host");
+    }
+    if (async_slot >= 0) {
+      B2A_CUDA(cudaEventRecord(ctx->async_free[async_slot], ctx->copy_out), "recording the slot's last download");
+      ctx->async_used[async_slot] = true;
+      return B2A_OK;
     }
     b2a_status es = enqueue_error_read(ctx);
     if (es != B2A_OK) return es;
@@ -530,6 +545,11 @@ b2a_status decode_host_pipelined(b2a_ctx* ctx, const b2a_kvcache* c, const AttnP
     B2A_CUDA(cudaMemcpyAsync(static_cast<char*>(hout) + b0 * out_seq, static_cast<char*>(dout) + b0 * out_seq,
                              n * out_seq, cudaMemcpyDeviceToHost, ctx->copy_out),
              "copying results to the host");
+  }
+  if (async_slot >= 0) {
+    B2A_CUDA(cudaEventRecord(ctx->async_free[async_slot], ctx->copy_out), "recording the slot's last download");
+    ctx->async_used[async_slot] = true;
+    return B2A_OK;
   }
   b2a_status es = enqueue_error_read(ctx);
   if (es != B2A_OK) return es;
@@ -803,6 +823,11 @@ b2a_status b2a_destroy(b2a_ctx* ctx) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->d_stage) cudaFree(ctx->d_stage);
+  if (ctx->copy_out) cudaStreamSynchronize(ctx->copy_out);
+  for (int i = 0; i < 2; i++) {
+    if (ctx->d_async[i]) cudaFree(ctx->d_async[i]);
+    if (ctx->async_free[i]) cudaEventDestroy(ctx->async_free[i]);
+  }
   if (ctx->d_scratch) cudaFree(ctx->d_scratch);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
@@ -1412,9 +1437,70 @@ b2a_status b2a_attention_decode(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* ro
     return decode_host_pipelined(ctx, c, p, q, k_new, v_new, out, dout, static_cast<int>(out_dtype),
                                  static_cast<size_t>(num_layers) * num_heads * c->head_dim * ies,
                                  static_cast<size_t>(num_layers) * c->kv_heads * c->head_dim * ies,
-                                 static_cast<size_t>(num_layers) * num_heads * c->head_dim * dtype_size(out_dtype));
+                                 static_cast<size_t>(num_layers) * num_heads * c->head_dim * dtype_size(out_dtype), -1);
   }
   return run_split_kv(ctx, c, p, max_keys, dout, static_cast<int>(out_dtype), 0);
+}
+
+b2a_status b2a_attention_decode_host_async(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rope, int layer_begin,
+                                           int num_layers, int num_heads, const void* q, const void* k_new,
+                                           const void* v_new, b2a_dtype in_dtype, void* out, b2a_dtype out_dtype) {
+  b2a_status s = check_cache_shape(c, rope, num_heads);
+  if (s != B2A_OK) return s;
+  if (q == nullptr || out == nullptr) return fail(B2A_EINVAL, "null q or out");
+  if ((k_new == nullptr) != (v_new == nullptr)) return fail(B2A_EINVAL, "give both new keys and values, or neither");
+  if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype)) return fail(B2A_EINVAL, "unknown dtype");
+  if (layer_begin < 0 || num_layers < 1 || layer_begin + num_layers > c->layers) {
+    return fail(B2A_EINVAL, "layers [%d, %d) outside the cache's %d", layer_begin, layer_begin + num_layers, c->layers);
+  }
+  for (int b = 0; b < c->batch; b++) {
+    const int past = c->len[b];
+    if (past + 1 > c->capacity) {
+      return fail(B2A_ERANGE, "cache holds %d of %d positions; cannot add 1 more", past, c->capacity);
+    }
+    if (past + 1 > rope->max_positions) {
+      return fail(B2A_ERANGE, "position %d exceeds the %d-entry rope table", past + 1, rope->max_positions);
+    }
+  }
+  CallGuard g(ctx);
+  if (!g.ok()) return g.busy_status();
+  if ((s = cache_reserve_all(c, 1)) != B2A_OK) return s;
+  const int slot = ctx->async_next;
+  if (ctx->async_free[slot] == nullptr) {
+    B2A_CUDA(cudaEventCreateWithFlags(&ctx->async_free[slot], cudaEventDisableTiming), "creating a slot event");
+  }
+  const size_t ies = dtype_size(in_dtype);
+  const size_t q_bytes = static_cast<size_t>(c->batch) * num_layers * num_heads * c->head_dim * ies;
+  const size_t kv_bytes = static_cast<size_t>(c->batch) * num_layers * c->kv_heads * c->head_dim * ies;
+  const size_t out_bytes = static_cast<size_t>(c->batch) * num_layers * num_heads * c->head_dim * dtype_size(out_dtype);
+  Stage st;
+  int iq = st.add(q_bytes), ik = st.add(k_new ? kv_bytes : 0), iv = st.add(k_new ? kv_bytes : 0),
+      io = st.add(out_bytes);
+  // growing a slot frees it first, which waits for every call still using it
+  if ((s = ensure_buffer(&ctx->d_async[slot], &ctx->d_async_bytes[slot], st.total, "allocating async staging")) !=
+      B2A_OK) {
+    return s;
+  }
+  char* base = static_cast<char*>(ctx->d_async[slot]);
+  AttnParams p = base_params(ctx, c, rope);
+  p.seq_begin = 0;
+  p.batch = c->batch;
+  p.num_layers = num_layers;
+  p.layer_begin = layer_begin;
+  p.tokens = 1;
+  p.heads = num_heads;
+  p.group = num_heads / c->kv_heads;
+  p.in_dtype = static_cast<int>(in_dtype);
+  p.q = base + st.offsets[iq];
+  p.k_new = k_new ? base + st.offsets[ik] : nullptr;
+  p.v_new = k_new ? base + st.offsets[iv] : nullptr;
+  p.horizon_extra = 1;
+  s = decode_host_pipelined(ctx, c, p, q, k_new, v_new, out, base + st.offsets[io], static_cast<int>(out_dtype),
+                            static_cast<size_t>(num_layers) * num_heads * c->head_dim * ies,
+                            static_cast<size_t>(num_layers) * c->kv_heads * c->head_dim * ies,
+                            static_cast<size_t>(num_layers) * num_heads * c->head_dim * dtype_size(out_dtype), slot);
+  if (s == B2A_OK) ctx->async_next = slot ^ 1;
+  return s;
 }
 
 }  // extern "C"

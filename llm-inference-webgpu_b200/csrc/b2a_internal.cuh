@@ -43,6 +43,14 @@ struct b2a_ctx {
   cudaStream_t copy_in = nullptr;
   cudaStream_t copy_out = nullptr;
   std::vector<cudaEvent_t> pipe_events;
+  // asynchronous host-pointer decode (b2a_attention_decode_host_async): two
+  // staging slots used in turn, each free again once its event (recorded
+  // after the slot's last download) has completed
+  void* d_async[2] = {nullptr, nullptr};
+  size_t d_async_bytes[2] = {0, 0};
+  cudaEvent_t async_free[2] = {nullptr, nullptr};
+  bool async_used[2] = {false, false};
+  int async_next = 0;
 };
 
 namespace b2a {

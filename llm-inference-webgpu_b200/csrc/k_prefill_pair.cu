@@ -12,11 +12,17 @@
 //                 S_w = Q_w . K_j^T    M=128 N=128 K=64  into S_w
 //                 O_w += P_w . V_j     M=128 N=64  K=128 (A = P_w from TMEM)
 //               S_w(j+1) is issued as soon as softmax w has read S_w(j) into
-//               registers, so it runs under that tile's exponentials.
+//               registers, so it runs under that tile's exponentials. The
+//               whole warp runs the loop and waits; one elected lane issues
+//               (a converged warp issues tcgen05.mma markedly faster than a
+//               lone lane: the S/PV issue no longer trails the softmax).
 //   warps 2-3   idle after setup.
 //   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: TMEM lane =
 //               query row, thread r owns row r. Two softmax warps per SM
-//               sub-partition hide each other's MUFU/FMA latency.
+//               sub-partition share its exponential unit; with no hand-over
+//               between them the two tiles settle half a KV step apart, so
+//               one tile's TMEM traffic, row max and P store run under the
+//               other's exponentials.
 // TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
 // P_0 [384,448) P_1 [448,512) (P as packed f16 pairs, separate from S so the
 // next S can be written while P is still being produced or consumed).
@@ -50,8 +56,6 @@ constexpr int kColO = 256;                     // + 64 w
 constexpr int kColP = 384;                     // + 64 w
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
-constexpr int kBarTurn0 = 1;                   // named barriers of the exponential turns
-constexpr int kBarTurn1 = 2;
 
 // smem layout (offsets from a 1024-aligned base)
 constexpr int kOffQ = 0;                       // + w * kQBytes
@@ -159,17 +163,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // Every lane runs the loop and its waits (a lane whose bounded wait gave
+    // up skips its later waits but keeps the same sequence of elect.sync
+    // calls, so the warp stays converged); the elected lane issues and commits.
+    {
       const uint32_t q_base = smem_u32(smem + kOffQ);
       for (int w = 0; w < ntile; w++) mbar_wait(&q_ready[w], 0, p.err, dead);
       auto issue_s = [&](int w, int j) {
         const uint32_t kt = ring + (j % kStages) * kStageBytes;
         const uint32_t qw = q_base + w * kQBytes;
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; kk++) {
-          mma_ss(tmem + kColS + w * kBN, sdesc_sw128(qw + kk * 32), sdesc_sw128(kt + kk * 32), kIdescS, kk > 0);
+          for (int kk = 0; kk < kD / 16; kk++) {
+            mma_ss(tmem + kColS + w * kBN, sdesc_sw128(qw + kk * 32), sdesc_sw128(kt + kk * 32), kIdescS, kk > 0);
+          }
+          mma_commit(&s_full[w]);
         }
-        mma_commit(&s_full[w]);
+        __syncwarp();
       };
       mbar_wait(&kv_full[0], 0, p.err, dead);
       tc_fence_after();
@@ -179,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j + 1 < n_kv) mbar_wait(&kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, p.err, dead);
         const uint32_t vt = ring + s * kStageBytes + kKVBytes;
         // per tile: the next S as soon as softmax w has read this one, then this
-        // tile's PV once its P is in TMEM (tile 1 runs half a turn behind tile 0)
+        // tile's PV once its P is in TMEM (the tiles run about half a step apart)
         for (int w = 0; w < ntile; w++) {
           if (j + 1 < n_kv) {
             mbar_wait(&s_free[w], j & 1, p.err, dead);
@@ -188,14 +198,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mbar_wait(&p_full[w], j & 1, p.err, dead);
           tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; kk++) {
-            mma_ts(tmem + kColO + w * kD, tmem + kColP + w * (kBN / 2) + kk * 8, sdesc_sw128(vt + kk * 2048),
-                   kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kBN / 16; kk++) {
+              mma_ts(tmem + kColO + w * kD, tmem + kColP + w * (kBN / 2) + kk * 8, sdesc_sw128(vt + kk * 2048),
+                     kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit(&pv_done[w]);
           }
-          mma_commit(&pv_done[w]);
+          __syncwarp();
         }
-        mma_commit(&kv_empty[s]);
+        if (elect_one()) mma_commit(&kv_empty[s]);
+        __syncwarp();
       }
     }
   }
@@ -271,12 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&q_ready[w]);
     }
 
-    // The two tiles take turns on the exponentials (the multi-function unit is
-    // the bottleneck): tile 0 may start tile j's exponentials once tile 1 has
-    // finished tile j-1's, tile 1 once tile 0 has finished tile j's. Each
-    // side's max, TMEM traffic and waits overlap the other side's exponentials.
-    const bool pingpong = ntile == 2;
-    if (pingpong && w == 1) named_arrive<kBarTurn0, 256>();
     const uint32_t scol = tmem + lane_addr + kColS + w * kBN;
     const uint32_t ocol = tmem + lane_addr + kColO + w * kD;
     const uint32_t pcol = tmem + lane_addr + kColP + w * (kBN / 2);
@@ -345,15 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = 2^(s*sc - m) as f16 pairs, packed in place: pair c lands in word
       // c of sr[0..1], whose S values were consumed before it is written
       // (the scale-and-shift and the row sums run as packed f32 pairs)
-      float nbt = nb;
-      if (pingpong) {
-        if (w == 0) named_sync<kBarTurn0, 256>();
-        else named_sync<kBarTurn1, 256>();
-        // the exponentials depend on a value produced after the barrier, so
-        // the compiler cannot hoist them above it
-        asm volatile("" : "+f"(nbt));
-      }
-      const uint64_t sc2 = f2_pack(sc, sc), nb2 = f2_pack(nbt, nbt);
+      const uint64_t sc2 = f2_pack(sc, sc), nb2 = f2_pack(nb, nb);
       uint64_t sums[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int q4 = 0; q4 < 4; q4++) {
@@ -367,12 +367,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = q4 * 16 + e / 2;
           sr[col >> 5][col & 31] = pack_f16x2(p0, p1);
         }
-      }
-      if (pingpong) {
-        // every exponential feeds a sum: pin the sums before handing over the turn
-        asm volatile("" : "+l"(sums[0]), "+l"(sums[1]), "+l"(sums[2]), "+l"(sums[3]));
-        if (w == 0) named_arrive<kBarTurn1, 256>();
-        else if (j + 1 < n_kv) named_arrive<kBarTurn0, 256>();
       }
       {
         float a0, a1;

@@ -178,7 +178,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop and its waits; one elected lane issues and
+    // commits (a converged warp issues tcgen05.mma faster than a lone lane).
+    {
       const uint32_t q_hi = smem_u32(smem + kOffQHi), q_lo = smem_u32(smem + kOffQLo);
       mbar_wait(q_ready, 0, p.err, dead);
       tc_fence_after();
@@ -188,17 +190,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t kt = smem_u32(smem + kOffRing + s * kStageBytes);
         const uint32_t d = tmem + (j & 1) * kBN;
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; kk++) {
-          mma_ss(d, sdesc_sw128(q_hi + kk * 32), sdesc_sw128(kt + kk * 32), kIdescS, kk > 0);
-        }
-        if (kSplit) {
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < kD / 16; kk++) {
-            mma_ss(d, sdesc_sw128(q_lo + kk * 32), sdesc_sw128(kt + kk * 32), kIdescS, 1);
+            mma_ss(d, sdesc_sw128(q_hi + kk * 32), sdesc_sw128(kt + kk * 32), kIdescS, kk > 0);
           }
+          if (kSplit) {
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; kk++) {
+              mma_ss(d, sdesc_sw128(q_lo + kk * 32), sdesc_sw128(kt + kk * 32), kIdescS, 1);
+            }
+          }
+          mma_commit(&s_full[j & 1]);
         }
-        mma_commit(&s_full[j & 1]);
+        __syncwarp();
       };
       issue_s(0);
       for (int j = 0; j < n_kv; j++) {
@@ -212,20 +217,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = j % kStages;
         const uint32_t vt = smem_u32(smem + kOffRing + s * kStageBytes + kKVBytes);
         const uint32_t pcol = tmem + (j & 1) * kBN;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; kk++) {
-          mma_ts(tmem + kOCol, pcol + kk * 8, sdesc_sw128(vt + kk * 2048), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (kSplit) {
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; kk++) {
-            mma_ts(tmem + kOCol, pcol + 64 + kk * 8, sdesc_sw128(vt + kk * 2048), kIdescPV, 1u);
+            mma_ts(tmem + kOCol, pcol + kk * 8, sdesc_sw128(vt + kk * 2048), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
           }
+          if (kSplit) {
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; kk++) {
+              mma_ts(tmem + kOCol, pcol + 64 + kk * 8, sdesc_sw128(vt + kk * 2048), kIdescPV, 1u);
+            }
+          }
+          mma_commit(&kv_empty[s]);
+          mma_commit(o_done);
         }
-        mma_commit(&kv_empty[s]);
-        mma_commit(o_done);
+        __syncwarp();
       }
-      mma_commit(o_final);   // tracks every MMA this thread issued, the last PV included
+      // tracks every MMA the elected lane issued, the last PV included
+      if (elect_one()) mma_commit(o_final);
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ softmax

@@ -53,6 +53,15 @@ __device__ __forceinline__ void mbar_wait(uint64_t* bar, uint32_t parity, int32_
   }
 }
 
+// One lane of a converged warp (the lowest active), as tcgen05.mma issue wants:
+// a whole warp that runs the issue loop and lets one elected lane issue keeps
+// the tensor pipe fed markedly better than a loop run by a lone lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}" : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(

@@ -506,3 +506,44 @@ def test_host_pipelined_decode_matches_device_path(ctx, rope, oracle):
         b2a.attentionDecode(ctx, c, rope, 0, qh, knh, vnh, out_host, H, numLayers=layers)
         diff = (out_host - out_dev.cpu()).abs().max().item()
         assert diff < 1e-4, diff
+
+
+@pytest.mark.parametrize("layers", [24, 1])
+def test_host_async_decode_matches_device_path(ctx, rope, oracle, layers):
+    """Host-pointer decode calls that return before their results are back
+    (b2a_attention_decode_host_async): four calls in flight with different
+    inputs and output buffers, one synchronisation, then every output equals
+    the device-pointer call's on the same inputs."""
+    import torch
+    batch, cap = 32, 700
+    c = b2a.GpuKVCache(ctx, cfg(layers), cap, batch=batch, dtype="f16")
+    dev = torch.device("cuda", 0)
+    kp, vp, _ = c.pools()
+    g = torch.Generator(device=dev)
+    g.manual_seed(19)
+
+    class _CAI:
+        def __init__(self, ptr, shape):
+            self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f2", "data": (ptr, False), "version": 3}
+
+    torch.as_tensor(_CAI(kp, (batch, layers, KVH, cap, D)), device=dev).normal_(generator=g)
+    torch.as_tensor(_CAI(vp, (batch, layers, KVH, cap, D)), device=dev).normal_(generator=g)
+    torch.cuda.synchronize(dev)
+    c.setLengths(np.random.default_rng(3).integers(1, cap - 1, size=batch).astype(np.int32))
+    steps = []
+    for i in range(4):
+        q = torch.randn(batch, layers, H, D, device=dev, generator=g).half()
+        kn = torch.randn(batch, layers, KVH, D, device=dev, generator=g).half()
+        vn = torch.randn(batch, layers, KVH, D, device=dev, generator=g).half()
+        ref = torch.empty(batch, layers, H, D, device=dev)
+        b2a.attentionDecode(ctx, c, rope, 0, q, kn, vn, ref, H, numLayers=layers)
+        steps.append((q.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory(),
+                      torch.full((batch, layers, H, D), float("nan")).pin_memory(), ref))
+    ctx.synchronize()
+    for qh, knh, vnh, outh, _ in steps:
+        b2a.attentionDecodeAsync(ctx, c, rope, 0, qh, knh, vnh, outh, H, numLayers=layers)
+    ctx.synchronize()
+    for i, (_, _, _, outh, ref) in enumerate(steps):
+        diff = (outh - ref.cpu()).abs().max().item()
+        assert diff < 1e-4, (i, diff)
+    c.close()
