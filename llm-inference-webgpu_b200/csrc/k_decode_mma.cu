@@ -53,7 +53,7 @@ struct __align__(16) MergeSmem {
   int item[4];
 };
 
-constexpr int kSmemTotal = kSmemRing + static_cast<int>(sizeof(MergeSmem)) + 2 * kStages * 8 + 1024;
+constexpr int kSmemTotal = kSmemRing + static_cast<int>(sizeof(MergeSmem)) + (2 * kStages + 2) * 8 + 1024;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -110,6 +110,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Untiled bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -220,6 +228,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   MergeSmem& ms = *reinterpret_cast<MergeSmem*>(smem + kSmemRing);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmemRing + sizeof(MergeSmem));
   uint64_t* empty = full + kStages;
+  uint64_t* qbar = empty + kStages;   // the query tile and its rotation row landed
+  uint64_t* pbar = qbar + 1;          // the fused merge's partials landed
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Programmatic dependent launch: the next kernel in the stream may begin its
@@ -275,6 +285,8 @@ __global__ void __launch_bounds__(kThreads, 3)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    mbar_init(qbar, 1);
+    mbar_init(pbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (p.n_len_inline != 0) {
@@ -302,30 +314,77 @@ __global__ void __launch_bounds__(kThreads, 3)
   const double* cosr = p.rope_cos + static_cast<int64_t>(pos_q) * (kD / 2);
   const double* sinr = p.rope_sin + static_cast<int64_t>(pos_q) * (kD / 2);
 
-  // ---- fused append of the new token (the CTA whose chunk holds the slot)
-  if (p.k_new != nullptr && past >= p0 && past < p1) {
+  // The group's queries and the position's f32 rotation row reach shared
+  // memory by bulk copies that the producer issues ahead of the ring fills
+  // (plain loads issued beside them wait behind the whole grid's first fills);
+  // so do, in the CTA whose chunk holds the new token's slot, the new key and
+  // value rows and the f64 rotation row of the fused append. That CTA writes
+  // the appended row to the cache and patches it into the shared-memory tile
+  // that holds the slot, so its stream starts with everyone else's instead of
+  // after the append. Blocks that are not 16-byte aligned take per-element
+  // loads, with the append done before the stream starts.
+  const int ntiles = (p1 - p0 + kTile - 1) / kTile;
+  const bool has_append = p.k_new != nullptr && past >= p0 && past < p1;
+  const int in_es = p.in_dtype == DT_F32 ? 4 : 2;
+  const int64_t qbase = ((static_cast<int64_t>(b) * p.num_layers + l) * p.heads + g * G) * kD;
+  const int64_t nsrc = ((static_cast<int64_t>(b) * p.num_layers + l) * p.kv_heads + g) * kD;
+  const unsigned char* qsrc = static_cast<const unsigned char*>(p.q) + qbase * in_es;
+  const uint32_t qbytes = static_cast<uint32_t>(G * kD * in_es);
+  const uint32_t row_bytes = static_cast<uint32_t>(kD * in_es);
+  const float* c32 = p.rope_cos32 + static_cast<int64_t>(pos_q) * (kD / 2);
+  const float* s32 = p.rope_sin32 + static_cast<int64_t>(pos_q) * (kD / 2);
+  const unsigned char* ksrc = has_append ? static_cast<const unsigned char*>(p.k_new) + nsrc * in_es : nullptr;
+  const unsigned char* vsrc = has_append ? static_cast<const unsigned char*>(p.v_new) + nsrc * in_es : nullptr;
+  uintptr_t amask = reinterpret_cast<uintptr_t>(qsrc) | reinterpret_cast<uintptr_t>(c32) |
+                    reinterpret_cast<uintptr_t>(s32);
+  if (has_append) {
+    amask |= reinterpret_cast<uintptr_t>(ksrc) | reinterpret_cast<uintptr_t>(vsrc) |
+             reinterpret_cast<uintptr_t>(cosr) | reinterpret_cast<uintptr_t>(sinr);
+  }
+  const bool staged = (amask & 15) == 0;
+  // staging areas in the merge area (free until the tile loop ends)
+  float* q_raw = &ms.o[2][0][0];                    // raw queries [G][64], <= 2 KiB
+  float* stg = &ms.o[3][0][0];                      // 2 KiB:
+  float* cs_raw = stg;                              //   f32 cos[32], sin[32]      (256 B)
+  unsigned char* k_raw = reinterpret_cast<unsigned char*>(stg + 64);    // new key row  (<= 256 B)
+  unsigned char* v_raw = reinterpret_cast<unsigned char*>(stg + 128);   // new value row (<= 256 B)
+  double* cs64 = reinterpret_cast<double*>(stg + 192);                  // f64 cos[32], sin[32] (512 B)
+  // the tile and the consumer warp whose 16 positions hold the slot
+  const int a_tile = (past - p0) / kTile, a_row = (past - p0) % kTile, a_warp = a_row / 16;
+
+  // ---- fused append, unstaged form: before the stream starts
+  if (has_append && !staged) {
     if (tid < kD / 2) {
       const int j = tid;
-      const int64_t src = ((static_cast<int64_t>(b) * p.num_layers + l) * p.kv_heads + g) * kD;
       const int64_t dst = kv_elem(p, bc, layer, g, past);
       float lo, hi;
-      rope_pair_f64(ld_as_f32(p.k_new, src + j, p.in_dtype), ld_as_f32(p.k_new, src + j + kD / 2, p.in_dtype),
+      rope_pair_f64(ld_as_f32(p.k_new, nsrc + j, p.in_dtype), ld_as_f32(p.k_new, nsrc + j + kD / 2, p.in_dtype),
                     cosr[j], sinr[j], lo, hi);
       st_from_f32(p.kc_w, dst + j, p.cache_dtype, lo);
       st_from_f32(p.kc_w, dst + j + kD / 2, p.cache_dtype, hi);
-      convert_elem(p.v_new, src + j, p.in_dtype, p.vc_w, dst + j, p.cache_dtype);
-      convert_elem(p.v_new, src + j + kD / 2, p.in_dtype, p.vc_w, dst + j + kD / 2, p.cache_dtype);
+      convert_elem(p.v_new, nsrc + j, p.in_dtype, p.vc_w, dst + j, p.cache_dtype);
+      convert_elem(p.v_new, nsrc + j + kD / 2, p.in_dtype, p.vc_w, dst + j + kD / 2, p.cache_dtype);
       // the tensor-memory-access (async proxy) loads below must see these stores
       asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     __syncthreads();
   }
 
-  const int ntiles = (p1 - p0 + kTile - 1) / kTile;
-
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      if (staged) {
+        mbar_arrive_expect_tx(qbar, qbytes + 256 + (has_append ? 2 * row_bytes + 512 : 0));
+        bulk_g2s(q_raw, qsrc, qbytes, qbar);
+        bulk_g2s(cs_raw, c32, 128, qbar);
+        bulk_g2s(cs_raw + 32, s32, 128, qbar);
+        if (has_append) {
+          bulk_g2s(k_raw, ksrc, row_bytes, qbar);
+          bulk_g2s(v_raw, vsrc, row_bytes, qbar);
+          bulk_g2s(cs64, cosr, 256, qbar);
+          bulk_g2s(cs64 + 32, sinr, 256, qbar);
+        }
+      }
       for (int i = 0; i < ntiles; i++) {
         const int s = i % kStages;
         if (i >= kStages) mbar_wait(&empty[s], ((i / kStages) - 1) & 1, p.err);
@@ -348,21 +407,26 @@ __global__ void __launch_bounds__(kThreads, 3)
   // next, or split into two bf16 parts that keep ~16 bits).
   {
     float* qs = &ms.o[0][0][0];   // [G][64] rotated queries
-    const int64_t qbase = ((static_cast<int64_t>(b) * p.num_layers + l) * p.heads + g * G) * kD;
-    const float* c32 = p.rope_cos32 + static_cast<int64_t>(pos_q) * (kD / 2);
-    const float* s32 = p.rope_sin32 + static_cast<int64_t>(pos_q) * (kD / 2);
     constexpr int kPairsPerThread = 2;   // 8 heads x 32 pairs over 128 consumer threads
     float x0[kPairsPerThread], x1[kPairsPerThread], cv[kPairsPerThread], sv[kPairsPerThread];
+    if (staged) mbar_wait(qbar, 0, p.err);
 #pragma unroll
     for (int r = 0; r < kPairsPerThread; r++) {
       const int idx = tid + r * kConsumerWarps * 32;
       const int h = idx >> 5, j = idx & 31;
       x0[r] = x1[r] = cv[r] = sv[r] = 0.f;
       if (h < G) {
-        x0[r] = ld_as_f32(p.q, qbase + h * kD + j, p.in_dtype);
-        x1[r] = ld_as_f32(p.q, qbase + h * kD + j + 32, p.in_dtype);
-        cv[r] = c32[j];
-        sv[r] = s32[j];
+        if (staged) {
+          x0[r] = ld_as_f32(q_raw, h * kD + j, p.in_dtype);
+          x1[r] = ld_as_f32(q_raw, h * kD + j + 32, p.in_dtype);
+          cv[r] = cs_raw[j];
+          sv[r] = cs_raw[32 + j];
+        } else {
+          x0[r] = ld_as_f32(p.q, qbase + h * kD + j, p.in_dtype);
+          x1[r] = ld_as_f32(p.q, qbase + h * kD + j + 32, p.in_dtype);
+          cv[r] = c32[j];
+          sv[r] = s32[j];
+        }
       }
     }
 #pragma unroll
@@ -374,6 +438,37 @@ __global__ void __launch_bounds__(kThreads, 3)
         qs[h * kD + j + 32] = fmaf(x1[r], cv[r], x0[r] * sv[r]);
       }
     }
+  }
+  // ---- fused append, staged form, by the warp that owns the slot's row: the
+  // row to the cache, and kept in registers (lane j: dims j and j + 32 of k
+  // and v) to be patched into the tile; same arithmetic as the unstaged form
+  uint32_t a_k = 0, a_v = 0;   // packed (dim j, dim j + 32) 16-bit codes
+  if (has_append && staged && warp == a_warp) {
+    const int j = lane;
+    const int64_t dst = kv_elem(p, bc, layer, g, past);
+    float lo, hi;
+    rope_pair_f64(ld_as_f32(k_raw, j, p.in_dtype), ld_as_f32(k_raw, j + kD / 2, p.in_dtype), cs64[j], cs64[32 + j],
+                  lo, hi);
+    const bool bf = p.cache_dtype == DT_BF16;
+    const uint32_t k0 = bf ? f32_to_bf16_bits(lo) : f32_to_f16_bits(lo);
+    const uint32_t k1 = bf ? f32_to_bf16_bits(hi) : f32_to_f16_bits(hi);
+    uint32_t v0, v1;
+    if (p.in_dtype == p.cache_dtype) {
+      v0 = reinterpret_cast<const uint16_t*>(v_raw)[j];
+      v1 = reinterpret_cast<const uint16_t*>(v_raw)[j + kD / 2];
+    } else {
+      const float x0v = ld_as_f32(v_raw, j, p.in_dtype), x1v = ld_as_f32(v_raw, j + kD / 2, p.in_dtype);
+      v0 = bf ? f32_to_bf16_bits(x0v) : f32_to_f16_bits(x0v);
+      v1 = bf ? f32_to_bf16_bits(x1v) : f32_to_f16_bits(x1v);
+    }
+    uint16_t* kc = static_cast<uint16_t*>(p.kc_w);
+    uint16_t* vc = static_cast<uint16_t*>(p.vc_w);
+    kc[dst + j] = static_cast<uint16_t>(k0);
+    kc[dst + j + kD / 2] = static_cast<uint16_t>(k1);
+    vc[dst + j] = static_cast<uint16_t>(v0);
+    vc[dst + j + kD / 2] = static_cast<uint16_t>(v1);
+    a_k = k0 | (k1 << 16);
+    a_v = v0 | (v1 << 16);
   }
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
   // Q^T B-fragments for head gq (zero for padding heads): b0 = dims 16ks+2tq..+1,
@@ -414,6 +509,19 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int s = i % kStages;
     mbar_wait(&full[s], (i / kStages) & 1, p.err);
     const int valid = min(kTile, p1 - (p0 + i * kTile)) - 16 * warp;   // positions of my 16 that exist
+    // the appended row, when it lies in my 16 positions of this tile: lane j
+    // writes dims j and j + 32 of k and v over what the tile load brought
+    const bool patch = has_append && staged && i == a_tile && warp == a_warp;
+    if (patch) {
+      unsigned char* kt0 = smem + s * kStageBytes;
+      const int j = lane;
+      const uint32_t o0 = swz(a_row, j >> 3) + 2 * (j & 7), o1 = swz(a_row, (j + kD / 2) >> 3) + 2 * (j & 7);
+      *reinterpret_cast<uint16_t*>(kt0 + o0) = static_cast<uint16_t>(a_k);
+      *reinterpret_cast<uint16_t*>(kt0 + o1) = static_cast<uint16_t>(a_k >> 16);
+      *reinterpret_cast<uint16_t*>(kt0 + kTileBytes + o0) = static_cast<uint16_t>(a_v);
+      *reinterpret_cast<uint16_t*>(kt0 + kTileBytes + o1) = static_cast<uint16_t>(a_v >> 16);
+      __syncwarp();
+    }
     if (valid > 0) {
       const uint32_t kt = ring + s * kStageBytes;
       const uint32_t vt = kt + kTileBytes;
@@ -479,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         mma16816<T>(o[mb], a0, a1, a2, a3, pb0, pb1);
         if (kSplit) mma16816<T>(o[mb], a0, a1, a2, a3, pl0, pl1);
       }
-      if (valid < 16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (valid < 16 || patch) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -590,7 +698,71 @@ __global__ void __launch_bounds__(kThreads, 3)
       o[kD + 3] = 0.f;
     }
   };
-  {
+  // the group's partials, [G][cnt][D+4], into the (drained) ring with one bulk
+  // copy per head when they fit: one round trip to L2 instead of two passes
+  const uint32_t head_bytes = static_cast<uint32_t>(cnt * (kD + 4) * 4);
+  const bool pbulk = G * head_bytes <= static_cast<uint32_t>(kSmemRing);
+  if (pbulk) {
+    if (tid == 0) {
+      // the acquire above made the other CTAs' partial stores visible to this
+      // thread; order them, and the consumers' reads of the ring, before the
+      // async-proxy copies
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(pbar, G * head_bytes);
+      for (int h = 0; h < G; h++) bulk_g2s(smem + h * head_bytes, part_base + h * part_row, head_bytes, pbar);
+    }
+    mbar_wait(pbar, 0, p.err);
+    const float* pv = reinterpret_cast<const float*>(smem);   // [G][cnt][D+4]
+    for (int h = warp; h < G; h += kConsumerWarps) {
+      const float* ph = pv + h * cnt * (kD + 4);
+      float mi[2], li[2];
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int cc = lane + 32 * u;
+        mi[u] = -CUDART_INF_F;
+        li[u] = 0.f;
+        if (cc < cnt) {
+          mi[u] = ph[cc * (kD + 4) + kD];
+          li[u] = ph[cc * (kD + 4) + kD + 1];
+        }
+        if (li[u] > 0.f) mx = fmaxf(mx, mi[u]);
+      }
+      for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+      float L = 0.f;
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const float w = li[u] > 0.f ? exp2f(mi[u] - mx) : 0.f;
+        wts[h * kMaxFusedChunks + lane + 32 * u] = w;
+        L = fmaf(w, li[u], L);
+      }
+      for (int x = 16; x > 0; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+      if (lane == 0) {
+        hinv[h] = p.fuse_mode == 0 ? 1.f / L : L;
+        ms.m[0][h] = mx;
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+    for (int t = tid; t < G * (kD / 4); t += kConsumerWarps * 32) {
+      const int h = t / (kD / 4), d4 = t % (kD / 4);
+      const float4* src = reinterpret_cast<const float4*>(pv + h * cnt * (kD + 4)) + d4;
+      constexpr int kRowVec = (kD + 4) / 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c2 = 0; c2 < cnt; c2++) {
+        const float w = wts[h * kMaxFusedChunks + c2];
+        const float4 v = src[c2 * kRowVec];
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+      put(h, 4 * d4, acc.x);
+      put(h, 4 * d4 + 1, acc.y);
+      put(h, 4 * d4 + 2, acc.z);
+      put(h, 4 * d4 + 3, acc.w);
+    }
+  } else {
     // two passes over the partials (L2): per head (one warp each, a lane per
     // chunk and chunk + 32) the chunk weights 2^(m_c - m*) into shared memory,
     // then the weighted sum with a thread per (head, 4 dims), whose loads are

@@ -234,6 +234,56 @@ def test_uniform_long_decode_equal_chunks(ctx, rope, oracle, batch, length):
         assert_parity(out[b, 0].reshape(-1), ref, "f32", f"seq {b} of {batch} x {length}")
 
 
+@pytest.mark.parametrize("cache_dtype,in_dtype", [("f16", "f16"), ("f16", "f32"), ("bf16", "bf16"), ("bf16", "f32")])
+def test_decode_device_inputs_aligned_and_unaligned(ctx, rope, oracle, cache_dtype, in_dtype):
+    """Device-resident q / k_new / v_new. 16-byte-aligned blocks reach the tensor-core decode
+    kernel's shared memory by bulk copies, and the CTA holding the new token's slot writes the
+    appended row to the cache and patches it into the tile it streams; blocks one element off
+    that alignment take per-element loads with the append done before the stream. Both forms
+    give the same output bits and cache bytes, and both match the oracle (slots at a tile's
+    last row, at a tile's first row, and in the last chunk of a many-chunk group)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[in_dtype]
+    batch, layers = 3, 2
+    lengths = [703, 64, 9000]
+    caches, hist = [], None
+    for _ in range(2):
+        c = b2a.GpuKVCache(ctx, cfg(layers), 9100, batch=batch, dtype=cache_dtype)
+        hist = _fill_cache(ctx, c, oracle, lengths, layers, cache_dtype, 900)
+        caches.append(c)
+    hk, hv = hist
+    q = oracle.round_to(oracle.normal_array(batch * layers * H * D, 11), in_dtype).reshape(batch, layers, H, D)
+    kn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 12), in_dtype).reshape(batch, layers, KVH, D)
+    vn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 13), in_dtype).reshape(batch, layers, KVH, D)
+
+    def dev_tensor(a, offset):
+        flat = torch.zeros(a.size + offset, dtype=tdt, device=dev)
+        flat[offset:] = torch.as_tensor(a.reshape(-1).astype(np.float32)).to(tdt).to(dev)
+        return flat[offset:].view(a.shape)
+
+    outs = []
+    for c, off in zip(caches, (0, 1)):
+        qt, kt, vt = dev_tensor(q, off), dev_tensor(kn, off), dev_tensor(vn, off)
+        assert (qt.data_ptr() % 16 == 0) == (off == 0)
+        out = torch.empty(batch, layers, H, D, device=dev)
+        b2a.attentionDecode(ctx, c, rope, 0, qt, kt, vt, out, H, numLayers=layers)
+        torch.cuda.synchronize(dev)
+        outs.append(out.cpu().numpy())
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    for b in range(batch):
+        for layer in range(layers):
+            ref, kr, vr = _oracle_decode(oracle, q[b, layer], kn[b, layer], vn[b, layer], hk[b, layer],
+                                         hv[b, layer], lengths[b], cache_dtype)
+            assert_parity(outs[0][b, layer].reshape(-1), ref, "f32", f"seq {b} layer {layer}")
+            for c in caches:
+                gk, gv = c.read(layer, lengths[b] + 1, seq=b)
+                assert np.array_equal(gk[:, lengths[b]], oracle.to_bits(kr, cache_dtype))
+                assert np.array_equal(gv[:, lengths[b]], oracle.to_bits(vr, cache_dtype))
+    for c in caches:
+        c.close()
+
+
 # ---------------------------------------------------------- config 2 prefill --
 
 @pytest.mark.parametrize("S", [8, 64, 512])
