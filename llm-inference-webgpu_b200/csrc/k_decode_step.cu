@@ -63,6 +63,7 @@ constexpr int kMaxInter = 8192;
 constexpr int kMaxOutRows = 2048;               // output-projection rows per CTA
 constexpr int kMaxRows = 128;                   // q/k/v rows or gate/up rows per CTA
 constexpr int kMaxOwnRows = 16;                 // hidden rows per CTA
+constexpr int kDownBatch = 8;                   // down-projection rows per pass
 constexpr int kAttnChunk = 128;                 // keys per attention item
 constexpr int kPartPitch = 68;                  // o[64], m, l, pad
 constexpr int kErrBarrier = 32;                 // error word: a grid barrier gave up
@@ -85,7 +86,7 @@ struct StepSmem {
   float rowscale[kMaxOutRows];            // per-row scales of the phase's rows (f32)
   float rowbias[kMaxRows];                // q/k/v bias of the phase's rows
   float xown[kMaxOwnRows];                // this CTA's rows of the residual stream
-  float down_part[kConsumerWarps][4];     // down projection: per-warp row sums
+  float down_part[kConsumerWarps][8];     // down projection: per-warp row sums
   double rope_c[32], rope_s[32];          // cos/sin of this step's position
   float aq[64], ak[64], av[64];           // attention: rotated q, rotated k_new, v_new
   uint16_t k16[64], v16[64];              // the new key/value as stored in the cache
@@ -363,41 +364,46 @@ __device__ __forceinline__ float combine3(int a0, int a1, int a2) {
 
 // Up to four rows (cnt of them valid; the rest repeat row 0) of K <= 1024
 // against the register digits; every lane gets the sums, in digit units.
-__device__ __forceinline__ void dot_rows(const unsigned char* const (&rp)[4], int cnt, int K, const RegDigits& rd,
-                                         float (&y)[4]) {
+template <int R>
+__device__ __forceinline__ void dot_rows(const unsigned char* base, const uint32_t (&ro)[R], int cnt, int K,
+                                         const RegDigits& rd, float (&y)[R]) {
   const int lane = threadIdx.x & 31;
-  int a[4][3];
+  int a[R][3];
 #pragma unroll
-  for (int r = 0; r < 4; r++) a[r][0] = a[r][1] = a[r][2] = 0;
+  for (int r = 0; r < R; r++) a[r][0] = a[r][1] = a[r][2] = 0;
+  // rows in groups of four (four 16-byte weight loads in flight at a time)
 #pragma unroll
-  for (int j = 0; j < 2; j++) {
-    const int u = lane + 32 * j;
-    if (16 * u < K) {
-      int4 w[4];
+  for (int g = 0; g < R; g += 4) {
 #pragma unroll
-      for (int r = 0; r < 4; r++) {
-        if (r < cnt) w[r] = *reinterpret_cast<const int4*>(rp[r] + 16 * u);
-      }
+    for (int j = 0; j < 2; j++) {
+      const int u = lane + 32 * j;
+      if (16 * u < K) {
+        int4 w[4];
 #pragma unroll
-      for (int r = 0; r < 4; r++) {
-        if (r < cnt) {
+        for (int r = 0; r < 4; r++) {
+          if (g + r < cnt) w[r] = *reinterpret_cast<const int4*>(base + ro[g + r] + 16 * u);
+        }
 #pragma unroll
-          for (int k = 0; k < 3; k++) {
-            a[r][k] = __dp4a(w[r].x, rd.d[j][k].x, a[r][k]);
-            a[r][k] = __dp4a(w[r].y, rd.d[j][k].y, a[r][k]);
-            a[r][k] = __dp4a(w[r].z, rd.d[j][k].z, a[r][k]);
-            a[r][k] = __dp4a(w[r].w, rd.d[j][k].w, a[r][k]);
+        for (int r = 0; r < 4; r++) {
+          if (g + r < cnt) {
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+              a[g + r][k] = __dp4a(w[r].x, rd.d[j][k].x, a[g + r][k]);
+              a[g + r][k] = __dp4a(w[r].y, rd.d[j][k].y, a[g + r][k]);
+              a[g + r][k] = __dp4a(w[r].z, rd.d[j][k].z, a[g + r][k]);
+              a[g + r][k] = __dp4a(w[r].w, rd.d[j][k].w, a[g + r][k]);
+            }
           }
         }
       }
     }
   }
 #pragma unroll
-  for (int r = 0; r < 4; r++) y[r] = combine3(a[r][0], a[r][1], a[r][2]);
+  for (int r = 0; r < R; r++) y[r] = combine3(a[r][0], a[r][1], a[r][2]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-    for (int r = 0; r < 4; r++) y[r] += __shfl_xor_sync(0xffffffffu, y[r], o);
+    for (int r = 0; r < R; r++) y[r] += __shfl_xor_sync(0xffffffffu, y[r], o);
   }
 }
 
@@ -461,20 +467,46 @@ __device__ __forceinline__ void walk_rows(const StepParams& p, StepSmem& sm, con
     const unsigned char* st = ring + static_cast<size_t>(s) * kStageBytes;
     const int cnt = first < n ? min(4, pairs * ((n - first + stride - 1) / stride)) : 0;
     if (cnt > 0) {
-      const unsigned char* rp[4];
+      uint32_t ro[4];
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const int row = k < cnt ? first + (k / pairs) * stride + (k % pairs) : first;
-        rp[k] = st + static_cast<size_t>(row) * sg.K;
+        ro[k] = static_cast<uint32_t>(row * sg.K);
       }
       float y[4];
-      dot_rows(rp, cnt, sg.K, rd, y);
+      dot_rows<4>(st, ro, cnt, sg.K, rd, y);
       fn(r, first, stride, cnt, y);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[s]);
     w.iter++;
   }
+}
+
+// Segments whose stages all fit the ring at once (gate/up, down) are taken
+// whole: wait for every stage, spread the rows over the warps, free every
+// stage at the end (a warp's rows then run as one batch of independent dot
+// products instead of one ring stage at a time).
+__device__ __forceinline__ int seg_stages(const Seg& sg) { return (sg.r1 - sg.r0 + sg.rpc - 1) / sg.rpc; }
+__device__ __forceinline__ void seg_wait(const StepParams& p, StepSmem& sm, Walk& w, int nst) {
+  for (int k = 0; k < nst; k++) {
+    const uint32_t it = w.iter + k;
+    mbar_wait(&sm.full[it % kStages], (it / kStages) & 1, p.err, w.dead);
+  }
+}
+// Byte offset in the ring of row i (0-based in the segment) of a segment
+// waited for with seg_wait.
+__device__ __forceinline__ uint32_t seg_off(const Seg& sg, const Walk& w, int i) {
+  const int k = i / sg.rpc;
+  return static_cast<uint32_t>(((w.iter + k) % kStages) * kStageBytes + (i - k * sg.rpc) * sg.K);
+}
+
+__device__ __forceinline__ void seg_free(StepSmem& sm, Walk& w, int nst) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    for (int k = 0; k < nst; k++) mbar_arrive(&sm.empty[(w.iter + k) % kStages]);
+  }
+  w.iter += nst;
 }
 
 __device__ __forceinline__ void pf_scales(StepSmem& sm, const void* scales, int dt, int r0, int r1) {
@@ -748,19 +780,22 @@ __device__ void consumer(const StepParams& p, StepSmem& sm, const unsigned char*
       }
       if (xthread) xv = __ldcg(reinterpret_cast<const float4*>(p.x) + tid);
       const float sx = norm_digits(sm, H, xv, p.eps, rd);
+      // rows come as (gate, up) pairs: lanes 0 and 1 keep pairs 0 and 1 of
+      // the chunk (in shared memory); silu(g) * u of every pair once the
+      // segment is done, off the chunks' path
       walk_rows(p, sm, ring, sg, rd, w, 2, [&](int r, int first, int stride, int cnt, const float (&y)[4]) {
-        // rows come as (gate, up) pairs: lanes 0 and 1 finish pairs 0 and 1;
         if (2 * lane < cnt) {
-          const float yg = lane == 0 ? y[0] : y[2];
-          const float yu = lane == 0 ? y[1] : y[3];
           const int row = r + first + lane * stride - sg.r0;   // even: the gate row
-          // silu in f32 here (the per-layer kernel keeps the reference's f64):
-          // one division and one expf on the chunk's critical path
-          const float gv = yg * sx * sm.rowscale[row];
-          const float uv = yu * sx * sm.rowscale[row + 1];
-          p.h[(sg.r0 + row) >> 1] = __fdiv_rn(gv, 1.f + expf(-gv)) * uv;
+          sm.act[row] = (lane == 0 ? y[0] : y[2]) * sx * sm.rowscale[row];
+          sm.act[row + 1] = (lane == 0 ? y[1] : y[3]) * sx * sm.rowscale[row + 1];
         }
       });
+      consumers_sync();
+      for (int j = tid; 2 * j < sg.r1 - sg.r0; j += kConsumers) {
+        // silu in f32 here (the per-layer kernel keeps the reference's f64)
+        const float gv = sm.act[2 * j], uv = sm.act[2 * j + 1];
+        p.h[(sg.r0 >> 1) + j] = __fdividef(gv, 1.f + __expf(-gv)) * uv;
+      }
     }
     // ---- E: down rows (K = intermediate), residual
     {
@@ -786,57 +821,65 @@ __device__ void consumer(const StepParams& p, StepSmem& sm, const unsigned char*
       }
       consumers_sync();
       const float sx = hmax / 127.f;
-      // each chunk (<= 4 rows) over the whole CTA: thread t takes 16-byte
-      // units t, t+256, ... of the flattened [row][unit] chunk
+      // the whole segment at once, eight rows per pass: thread t takes the
+      // 16-byte units t, t+256, ... of every row of the pass
       const int urow = I / 16;
-      for (int r = sg.r0; r < sg.r1; r += sg.rpc) {
-        const int s = w.iter % kStages;
-        mbar_wait(&sm.full[s], (w.iter / kStages) & 1, p.err, w.dead);
-        const int n = min(sg.rpc, sg.r1 - r);
-        const unsigned char* st = ring + static_cast<size_t>(s) * kStageBytes;
-        int a[4][3] = {};
-        for (int idx = tid; idx < n * urow; idx += kConsumers) {
-          const int row = idx / urow, u = idx - row * urow;
-          const int4 wv = *reinterpret_cast<const int4*>(st + static_cast<size_t>(row) * I + 16 * u);
+      const int nst = seg_stages(sg);
+      const int nrow = sg.r1 - sg.r0;
+      seg_wait(p, sm, w, nst);
+      for (int r0 = 0; r0 < nrow; r0 += kDownBatch) {
+        const int nb = min(kDownBatch, nrow - r0);
+        uint32_t ro[kDownBatch];
+#pragma unroll
+        for (int k = 0; k < kDownBatch; k++) ro[k] = seg_off(sg, w, r0 + (k < nb ? k : 0));
+        int a[kDownBatch][3] = {};
+        for (int u = tid; u < urow; u += kConsumers) {
           const int4 d0 = *reinterpret_cast<const int4*>(&sm.dig[0][4 * u]);
           const int4 d1 = *reinterpret_cast<const int4*>(&sm.dig[1][4 * u]);
           const int4 d2 = *reinterpret_cast<const int4*>(&sm.dig[2][4 * u]);
 #pragma unroll
-          for (int k = 0; k < 4; k++) {
-            if (k == row) {
-              a[k][0] = __dp4a(wv.w, d0.w, __dp4a(wv.z, d0.z, __dp4a(wv.y, d0.y, __dp4a(wv.x, d0.x, a[k][0]))));
-              a[k][1] = __dp4a(wv.w, d1.w, __dp4a(wv.z, d1.z, __dp4a(wv.y, d1.y, __dp4a(wv.x, d1.x, a[k][1]))));
-              a[k][2] = __dp4a(wv.w, d2.w, __dp4a(wv.z, d2.z, __dp4a(wv.y, d2.y, __dp4a(wv.x, d2.x, a[k][2]))));
+          for (int g = 0; g < kDownBatch; g += 4) {   // four weight loads in flight at a time
+            int4 wv[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              if (g + k < nb) wv[k] = *reinterpret_cast<const int4*>(ring + ro[g + k] + 16 * u);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              if (g + k < nb) {
+                int* ak = a[g + k];
+                ak[0] = __dp4a(wv[k].w, d0.w, __dp4a(wv[k].z, d0.z, __dp4a(wv[k].y, d0.y, __dp4a(wv[k].x, d0.x, ak[0]))));
+                ak[1] = __dp4a(wv[k].w, d1.w, __dp4a(wv[k].z, d1.z, __dp4a(wv[k].y, d1.y, __dp4a(wv[k].x, d1.x, ak[1]))));
+                ak[2] = __dp4a(wv[k].w, d2.w, __dp4a(wv[k].z, d2.z, __dp4a(wv[k].y, d2.y, __dp4a(wv[k].x, d2.x, ak[2]))));
+              }
             }
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[s]);
-        w.iter++;
-        float y[4];
+        float y[kDownBatch];
 #pragma unroll
-        for (int k = 0; k < 4; k++) y[k] = combine3(a[k][0], a[k][1], a[k][2]);
+        for (int k = 0; k < kDownBatch; k++) y[k] = combine3(a[k][0], a[k][1], a[k][2]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-          for (int k = 0; k < 4; k++) y[k] += __shfl_xor_sync(0xffffffffu, y[k], o);
+          for (int k = 0; k < kDownBatch; k++) y[k] += __shfl_xor_sync(0xffffffffu, y[k], o);
         }
         if (lane == 0) {
 #pragma unroll
-          for (int k = 0; k < 4; k++) sm.down_part[warp][k] = y[k];
+          for (int k = 0; k < kDownBatch; k++) sm.down_part[warp][k] = y[k];
         }
         consumers_sync();
-        if (tid < n) {
+        if (tid < nb) {
           float t = 0.f;
 #pragma unroll
           for (int k = 0; k < kConsumerWarps; k++) t += sm.down_part[k][tid];
-          const int row = r + tid;
+          const int row = sg.r0 + r0 + tid;
           const float xn = sm.xown[row - own0] + t * sx * sm.rowscale[row - sg.r0];
           sm.xown[row - own0] = xn;
           p.x[row] = xn;
         }
         consumers_sync();
       }
+      seg_free(sm, w, nst);
     }
   }
   // ---- F: final rmsnorm -> output projection rows -> greedy pick
@@ -939,6 +982,13 @@ int decode_step_attn_chunk() { return kAttnChunk; }
 bool decode_step_supported(int hidden, int inter, int q_rows, int vocab, int ctas) {
   if (ctas < 1) return false;
   auto per = [ctas](int rows) { return (rows + ctas - 1) / ctas; };
+  // the gate/up and down segments are taken whole: their stages must fit the ring
+  const int rpc_gu = max(2, min(kStageBytes / max(hidden, 1), 4 * kConsumerWarps) & ~1);
+  const int rpc_down = min(kStageBytes / max(inter, 1), 4);
+  if (rpc_down < 1 || (2 * per(inter) + rpc_gu - 1) / rpc_gu > kStages ||
+      (per(hidden) + rpc_down - 1) / rpc_down > kStages) {
+    return false;
+  }
   return hidden % 64 == 0 && hidden <= kMaxHidden && inter % 16 == 0 && inter <= kMaxInter &&
          per(hidden) <= kMaxOwnRows && per(q_rows) <= kMaxRows && 2 * per(inter) <= kMaxRows &&
          per(vocab) <= kMaxOutRows && inter <= kStageBytes && decode_step_smem_bytes() <= 227 * 1024;
