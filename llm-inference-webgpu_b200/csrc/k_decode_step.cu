@@ -483,10 +483,11 @@ __device__ __forceinline__ void walk_rows(const StepParams& p, StepSmem& sm, con
   }
 }
 
-// Segments whose stages all fit the ring at once (gate/up, down) are taken
-// whole: wait for every stage, spread the rows over the warps, free every
-// stage at the end (a warp's rows then run as one batch of independent dot
-// products instead of one ring stage at a time).
+// The down segment (a few rows of K = intermediate, in at most kStages
+// stages) is taken whole: wait for every stage, run its rows as one batch of
+// independent dot products with one CTA reduction, free every stage at the
+// end. (Taking the gate/up segment whole measured slower than its chunk walk:
+// its later stages are still landing when the phase starts.)
 __device__ __forceinline__ int seg_stages(const Seg& sg) { return (sg.r1 - sg.r0 + sg.rpc - 1) / sg.rpc; }
 __device__ __forceinline__ void seg_wait(const StepParams& p, StepSmem& sm, Walk& w, int nst) {
   for (int k = 0; k < nst; k++) {
@@ -982,13 +983,9 @@ int decode_step_attn_chunk() { return kAttnChunk; }
 bool decode_step_supported(int hidden, int inter, int q_rows, int vocab, int ctas) {
   if (ctas < 1) return false;
   auto per = [ctas](int rows) { return (rows + ctas - 1) / ctas; };
-  // the gate/up and down segments are taken whole: their stages must fit the ring
-  const int rpc_gu = max(2, min(kStageBytes / max(hidden, 1), 4 * kConsumerWarps) & ~1);
+  // the down segment is taken whole: its stages must fit the ring
   const int rpc_down = min(kStageBytes / max(inter, 1), 4);
-  if (rpc_down < 1 || (2 * per(inter) + rpc_gu - 1) / rpc_gu > kStages ||
-      (per(hidden) + rpc_down - 1) / rpc_down > kStages) {
-    return false;
-  }
+  if (rpc_down < 1 || (per(hidden) + rpc_down - 1) / rpc_down > kStages) return false;
   return hidden % 64 == 0 && hidden <= kMaxHidden && inter % 16 == 0 && inter <= kMaxInter &&
          per(hidden) <= kMaxOwnRows && per(q_rows) <= kMaxRows && 2 * per(inter) <= kMaxRows &&
          per(vocab) <= kMaxOutRows && inter <= kStageBytes && decode_step_smem_bytes() <= 227 * 1024;
