@@ -308,6 +308,27 @@ b2a_status b2a_attention_decode_partial_layers(b2a_ctx* ctx, b2a_kvcache* cache,
  * in ascending part order, into out [batch][num_heads][head_dim] (out_dtype). */
 b2a_status b2a_lse_combine(b2a_ctx* ctx, const float* partials, int num_parts, int batch,
                            int num_heads, int head_dim, void* out, b2a_dtype out_dtype, int flags);
+/* Split-KV decode over NCCL in one call (the per-layer decode dispatch of
+ * src/gpu/model.js:323-346 with each rank holding a contiguous slice of every
+ * sequence's positions; the reference itself runs on one device): this rank's
+ * partials (b2a_attention_decode_partial_layers, written into its slot of a
+ * per-context [world][batch][num_layers][num_heads][head_dim + 4] buffer), an
+ * in-place ncclAllGather of the slots on the context's stream through the
+ * caller's communicator `nccl_comm` (an ncclComm_t of `world` ranks in which
+ * this process is `rank`), then b2a_lse_combine of the world slots in
+ * ascending rank order into out [batch][num_layers][num_heads][head_dim]
+ * (out_dtype; the same bits on every rank). Every rank passes the same q and
+ * q_positions; k_new/v_new are appended and attended by rank world - 1 only
+ * (the slice that ends the sequences) and ignored elsewhere. Device pointers
+ * only (flags B2A_DEVICE). NCCL is loaded at the first call (libnccl.so.2,
+ * the instance the process has loaded when there is one); B2A_ENCCL when it
+ * cannot be loaded or the all-gather fails. Every rank must make the call,
+ * the same number of times, in the same order as its other collectives. */
+b2a_status b2a_split_kv_decode_nccl(b2a_ctx* ctx, b2a_kvcache* cache, const b2a_rope* rope, int layer_begin,
+                                    int num_layers, int num_heads, const void* q, const void* k_new,
+                                    const void* v_new, b2a_dtype in_dtype, const int32_t* q_positions,
+                                    void* nccl_comm, int world, int rank, void* out, b2a_dtype out_dtype,
+                                    int flags);
 
 /* ---- projections either side of attention: int8 weights, per-row scales -----
  * The Qwen2.5 layer's q/k/v and output projections (src/cpu/model.js:98-101,

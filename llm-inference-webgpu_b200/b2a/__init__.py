@@ -7,7 +7,7 @@ src/gpu/model.js) over libb2a.so. There is no CPU fallback: without the built
 library, or without a CUDA device, calls raise.
 """
 from ._lib import B2AError, BusyError, RangeError, load, lib_path  # noqa: F401
-from .attention import (appendRope, attentionDecode, attentionDecodeAsync, attentionPrefill, attentionPrefillBatch, decodePartial, decodeSplit,  # noqa: F401
+from .attention import (appendRope, attentionDecode, attentionDecodeAsync, attentionPrefill, attentionPrefillBatch, decodePartial, decodeSplit, decodeSplitNccl,  # noqa: F401
                         default_context, groupedAttention, kvHeadFor, linearInt8, lseCombine, qkvInt8,
                         quantizeInt8PerChannel, ropeFrequencies, ropeTables)
 from .model import Model, ModelConfig  # noqa: F401

@@ -68,6 +68,8 @@ SIGNATURES = {
     "b2a_attention_decode_partial": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i]),
     "b2a_attention_decode_partial_layers": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i]),
     "b2a_lse_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _i, _i]),
+    "b2a_split_kv_decode_nccl": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp, _i,
+                                      _i]),
     "b2a_quantize_int8_per_channel": (_i, [_vp, _i, _i, _vp, _vp]),
     "b2a_linear_int8": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp, _i, _i]),
     "b2a_qkv_int8": (_i, [_vp, _vp, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i]),

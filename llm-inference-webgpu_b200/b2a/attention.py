@@ -179,6 +179,26 @@ def decodeSplit(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q,
     del keep
 
 
+def decodeSplitNccl(ctx: Context, cache: GpuKVCache, rope: RopeTable, layer: int, q, k_new, v_new, q_positions,
+                    comm, world: int, rank: int, out, numHeads: int, dtype: str | None = None,
+                    out_dtype: str | None = None, numLayers: int = 1) -> None:
+    """One split-KV decode step over NCCL (b2a_split_kv_decode_nccl): this rank's
+    partials, an in-place ncclAllGather through `comm` (an ncclComm_t, as an int
+    address or an object with a `.value`), the combine in rank order into out
+    [batch, numLayers, numHeads, headDim]. Device tensors only; k_new/v_new are
+    used by rank world - 1 only."""
+    qa, ka, va = _arg(q, dtype), _arg(k_new, dtype), _arg(v_new, dtype)
+    oa = _arg(out, out_dtype, writable=True)
+    in_dt = _same_dtype(qa, ka, va)
+    where = _where(qa, ka, va, oa)
+    pos_ptr, keep = _positions(ctx, q_positions, where)
+    handle = getattr(comm, "value", comm)
+    check(load().b2a_split_kv_decode_nccl(ctx.handle, cache.handle, rope.handle, layer, numLayers, numHeads, qa.ptr,
+                                          ka.ptr if ka else None, va.ptr if va else None, DTYPES[in_dt], pos_ptr,
+                                          handle, world, rank, oa.ptr, DTYPES[oa.dtype], where))
+    del keep
+
+
 def lseCombine(ctx: Context, partials, numParts: int, batch: int, numHeads: int, headDim: int, out,
                out_dtype: str | None = None) -> None:
     """Merge [numParts, batch, numHeads, headDim+4] partials in ascending part order."""

@@ -24,6 +24,7 @@ libb2a.so and torch.distributed's NCCL all-gather.
 """
 from __future__ import annotations
 
+import ctypes
 import heapq
 from typing import Callable, Sequence
 
@@ -111,6 +112,82 @@ def cuda_split_kv(ctx, cache, rope, layer: int, num_heads: int, rank: int, world
         A.lseCombine(ctx, stacked, world, rows, num_heads, head_dim, out)
 
     return SplitKVDecode(rank, world, partial_fn, nccl_gather_fn(group), combine_fn)
+
+
+class NcclComm:
+    """An NCCL communicator made through libnccl.so.2 itself (ctypes), for the
+    one-call NCCL split-KV decode (b2a_split_kv_decode_nccl): one rank makes
+    `unique_id()`, the others receive it over any channel, and every rank opens
+    NcclComm(uid, world, rank) with its GPU current. `single()` makes a
+    communicator of one rank. The library loaded is the process's own
+    libnccl.so.2 (torch's, once torch has loaded it)."""
+
+    ID_BYTES = 128
+
+    class _Id(ctypes.Structure):
+        _fields_ = [("internal", ctypes.c_char * 128)]
+
+    @staticmethod
+    def _lib():
+        return ctypes.CDLL("libnccl.so.2")
+
+    @classmethod
+    def unique_id(cls) -> bytes:
+        uid = cls._Id()
+        r = cls._lib().ncclGetUniqueId(ctypes.byref(uid))
+        if r != 0:
+            raise RuntimeError(f"ncclGetUniqueId failed ({r})")
+        return ctypes.string_at(ctypes.addressof(uid), cls.ID_BYTES)
+
+    def __init__(self, uid: bytes | None, world: int, rank: int, _comm=None):
+        self.world, self.rank = world, rank
+        self._handle = ctypes.c_void_p()
+        if _comm is not None:
+            self._handle = _comm
+            return
+        if uid is None or len(uid) != self.ID_BYTES:
+            raise ValueError("an NCCL unique id of 128 bytes")
+        u = self._Id()
+        ctypes.memmove(ctypes.addressof(u), uid, self.ID_BYTES)
+        r = self._lib().ncclCommInitRank(ctypes.byref(self._handle), world, u, rank)
+        if r != 0:
+            raise RuntimeError(f"ncclCommInitRank failed ({r})")
+
+    @classmethod
+    def single(cls, device: int = 0) -> "NcclComm":
+        comm = ctypes.c_void_p()
+        devs = (ctypes.c_int * 1)(device)
+        r = cls._lib().ncclCommInitAll(ctypes.byref(comm), 1, devs)
+        if r != 0:
+            raise RuntimeError(f"ncclCommInitAll failed ({r})")
+        return cls(None, 1, 0, _comm=comm)
+
+    @property
+    def value(self) -> int:
+        return self._handle.value
+
+    def close(self) -> None:
+        if self._handle.value:
+            self._lib().ncclCommDestroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+
+class NcclSplitKV:
+    """Split-KV decode with the all-gather over NCCL in one library call per step
+    (b2a_split_kv_decode_nccl): the C-ABI form of `cuda_split_kv`, for hosts that
+    hold an NCCL communicator but no torch.distributed process group."""
+
+    def __init__(self, ctx, cache, rope, layer: int, num_heads: int, comm: NcclComm, num_layers: int = 1,
+                 dtype: str | None = None):
+        self.ctx, self.cache, self.rope, self.layer = ctx, cache, rope, layer
+        self.num_heads, self.comm, self.num_layers, self.dtype = num_heads, comm, num_layers, dtype
+
+    def step(self, q, k_new, v_new, positions, out):
+        from . import attention as A
+        A.decodeSplitNccl(self.ctx, self.cache, self.rope, self.layer, q, k_new, v_new, positions, self.comm,
+                          self.comm.world, self.comm.rank, out, self.num_heads, dtype=self.dtype,
+                          numLayers=self.num_layers)
+        return out
 
 
 def gather_handles(handle: bytes, world: int, group=None) -> bytes:

@@ -829,6 +829,7 @@ b2a_status b2a_destroy(b2a_ctx* ctx) {
     if (ctx->async_free[i]) cudaEventDestroy(ctx->async_free[i]);
   }
   if (ctx->d_scratch) cudaFree(ctx->d_scratch);
+  nccl_split_release(ctx);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
   if (ctx->d_positions) cudaFree(ctx->d_positions);

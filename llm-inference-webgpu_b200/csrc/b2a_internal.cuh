@@ -380,6 +380,8 @@ bool st_widen(const std::string& dt, const void* src, size_t n, float* dst);
 bool ctx_acquire(b2a_ctx* ctx);
 void ctx_release(b2a_ctx* ctx);
 b2a_status busy_fail(b2a_ctx* ctx);
+// frees the context's NCCL gather buffer (b2a_split_kv_decode_nccl)
+void nccl_split_release(b2a_ctx* ctx);
 // waits for the stream, then reads and clears the device error word
 b2a_status stream_sync_check(b2a_ctx* ctx);
 

@@ -58,6 +58,13 @@ def multilayer(ctx, dev, rank, world, failures):
     local = torch.empty(batch, layers, H, D + 4, device=dev)
     out_nccl = torch.empty(batch, layers, H, D, device=dev)
     nccl.step(q, kn, vn, pos, local, out_nccl)
+    # the same step through one C-ABI call over this test's own NCCL communicator
+    uid = bd.gather_handles(bd.NcclComm.unique_id(), world)[:bd.NcclComm.ID_BYTES]
+    comm = bd.NcclComm(uid, world, rank)
+    out_capi = torch.empty(batch, layers, H, D, device=dev)
+    capi = bd.NcclSplitKV(ctx, cache, rope, 0, H, comm, num_layers=layers)
+    for _ in range(2):
+        capi.step(q, kn, vn, pos, out_capi)
     full = b2a.GpuKVCache(ctx, b2a.CacheConfig(layers, KVH, D, H), total + 1, batch=batch, dtype="f16")
     fill(full, kfull, vfull)
     out_full = torch.empty(batch, layers, H, D, device=dev)
@@ -66,10 +73,16 @@ def multilayer(ctx, dev, rank, world, failures):
     torch.cuda.synchronize(dev)
     d_peer = (out_peer - out_full).abs().max().item()
     d_nccl = (out_nccl - out_full).abs().max().item()
+    d_capi = (out_capi - out_full).abs().max().item()
     if not d_peer <= 2e-3:
         failures.append(f"3-layer peer exchange off by {d_peer}")
     if not d_nccl <= 2e-3:
         failures.append(f"3-layer nccl path off by {d_nccl}")
+    if not d_capi <= 2e-3:
+        failures.append(f"3-layer C-ABI nccl call off by {d_capi}")
+    if not torch.equal(out_capi, out_nccl):
+        failures.append("C-ABI nccl call and the torch.distributed nccl path differ")
+    comm.close()
     peer.close()
     return d_peer, d_nccl
 

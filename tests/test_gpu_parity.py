@@ -440,6 +440,48 @@ def test_split_kv_partials_combine_to_full_decode(ctx, rope, oracle):
         assert_parity(out[b].reshape(-1), ref, "f32", f"split seq {b}")
 
 
+def test_split_kv_nccl_call_single_rank(ctx, rope, oracle):
+    """b2a_split_kv_decode_nccl through a one-rank NCCL communicator: the partials,
+    the in-place ncclAllGather and the combine in one call, over two layers; two
+    steps in a row (new q/k/v each), checked against the oracle, with the appended
+    rows bit for bit."""
+    import torch
+    from b2a import dist
+    dev = torch.device("cuda", 0)
+    batch, L, layers = 3, 1500, 2
+    c = b2a.GpuKVCache(ctx, cfg(layers), L + 1, batch=batch, dtype="f16")
+    hk, hv = _fill_cache(ctx, c, oracle, [L] * batch, layers, "f16", 700)
+    comm = dist.NcclComm.single(0)
+    try:
+        split = dist.NcclSplitKV(ctx, c, rope, 0, H, comm, num_layers=layers)
+        pos = torch.full((batch,), L, dtype=torch.int32, device=dev)
+        for step in range(2):
+            q = oracle.round_to(oracle.normal_array(batch * layers * H * D, 40 + step), "f16")
+            kn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 50 + step), "f16")
+            vn = oracle.round_to(oracle.normal_array(batch * layers * KVH * D, 60 + step), "f16")
+            qt = torch.as_tensor(q).to(dev).half().view(batch, layers, H, D)
+            kt = torch.as_tensor(kn).to(dev).half().view(batch, layers, KVH, D)
+            vt = torch.as_tensor(vn).to(dev).half().view(batch, layers, KVH, D)
+            out = torch.empty(batch, layers, H, D, device=dev)
+            torch.cuda.synchronize(dev)
+            split.step(qt, kt, vt, pos, out)
+            ctx.synchronize()
+            got = out.cpu().numpy()
+            q4, k4, v4 = (q.reshape(batch, layers, H, D), kn.reshape(batch, layers, KVH, D),
+                          vn.reshape(batch, layers, KVH, D))
+            for b in range(batch):
+                for layer in range(layers):
+                    ref, kr, vr = _oracle_decode(oracle, q4[b, layer], k4[b, layer], v4[b, layer], hk[b, layer],
+                                                 hv[b, layer], L, "f16")
+                    assert_parity(got[b, layer].reshape(-1), ref, "f32", f"step {step} seq {b} layer {layer}")
+                    gk, gv = c.read(layer, L + 1, seq=b)
+                    assert np.array_equal(gk[:, L], oracle.to_bits(kr, "f16"))
+                    assert np.array_equal(gv[:, L], oracle.to_bits(vr, "f16"))
+    finally:
+        comm.close()
+        c.close()
+
+
 def test_split_exchange_single_rank_matches_decode(ctx, rope, oracle):
     """The in-kernel exchange path with one rank: the group partials go through
     the exchange buffer and flags of this GPU only, and the output equals the
