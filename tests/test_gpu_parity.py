@@ -477,6 +477,13 @@ def test_split_kv_nccl_call_single_rank(ctx, rope, oracle):
                     gk, gv = c.read(layer, L + 1, seq=b)
                     assert np.array_equal(gk[:, L], oracle.to_bits(kr, "f16"))
                     assert np.array_equal(gv[:, L], oracle.to_bits(vr, "f16"))
+        # argument errors come back before any device work
+        with pytest.raises(b2a.B2AError):   # host arrays: the call takes device pointers only
+            b2a.decodeSplitNccl(ctx, c, rope, 0, q.reshape(batch, layers, H, D), None, None, np.full(batch, L, np.int32),
+                                comm, 1, 0, np.empty((batch, layers, H, D), np.float32), H, numLayers=layers,
+                                dtype="f16")
+        with pytest.raises(b2a.B2AError):   # a rank outside the world
+            b2a.decodeSplitNccl(ctx, c, rope, 0, qt, None, None, pos, comm, 1, 1, out, H, numLayers=layers)
     finally:
         comm.close()
         c.close()
