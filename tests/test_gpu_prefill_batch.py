@@ -111,3 +111,68 @@ def test_batched_prefill_checks_every_sequence(ctx, rope, oracle):
     with pytest.raises(b2a.B2AError, match="out of range"):
         b2a.attentionPrefillBatch(ctx, c, rope, 1, q, k, k, o, 8, H, 2, 3, dtype="f16", out_dtype="f32")
     c.close()
+
+
+@pytest.mark.parametrize("in_dtype", ["f16", "bf16"])
+def test_batched_prefill_more_units_than_sms(ctx, rope, oracle, monkeypatch, in_dtype):
+    """24 sequences of 200 new tokens at ragged cache lengths: 384 CTAs of the
+    two-tile kernel (query tile, sequence, head pair), more than one wave on
+    the SMs, with partial last tiles in every sequence. The result must carry
+    the same bits as one call per sequence (16 CTAs each) and match the oracle;
+    the 16-bit output must be the f32 output rounded."""
+    monkeypatch.setenv("B2A_PREFILL_TILES", "2")
+    count, nseq = 200, 24
+    pasts = [(37 * i) % 301 for i in range(nseq)]
+    cap = max(pasts) + count
+    cfg = b2a.CacheConfig(numLayers=1, numKVHeads=KVH, headDim=D, numHeads=H)
+    cb = b2a.GpuKVCache(ctx, cfg, cap, batch=nseq, dtype="f16")
+    cs = b2a.GpuKVCache(ctx, cfg, cap, batch=nseq, dtype="f16")
+    hk, hv = {}, {}
+    for b, L in enumerate(pasts):
+        if L:
+            kk = oracle.normal_array(L * KVH * D, 700 + b)
+            vv = oracle.normal_array(L * KVH * D, 800 + b)
+            for c in (cb, cs):
+                c.writeAt(0, 0, kk, vv, L, seq=b)
+            hk[b], hv[b] = oracle.round_to(kk, "f16"), oracle.round_to(vv, "f16")
+    cb.setLengths(pasts)
+    cs.setLengths(pasts)
+    q = oracle.round_to(oracle.normal_array(nseq * count * H * D, 91), in_dtype).reshape(nseq, count, H * D)
+    k = oracle.round_to(oracle.normal_array(nseq * count * KVH * D, 92), in_dtype).reshape(nseq, count, KVH * D)
+    v = oracle.round_to(oracle.normal_array(nseq * count * KVH * D, 93), in_dtype).reshape(nseq, count, KVH * D)
+    bits = lambda x: oracle.to_bits(x, in_dtype)  # noqa: E731
+    ob = np.empty((nseq, count, H * D), np.float32)
+    b2a.attentionPrefillBatch(ctx, cb, rope, 0, bits(q), bits(k), bits(v), ob, count, H, 0, nseq, dtype=in_dtype,
+                              out_dtype="f32")
+    os_ = np.empty_like(ob)
+    for i in range(nseq):
+        b2a.attentionPrefill(ctx, cs, rope, 0, bits(q[i]), bits(k[i]), bits(v[i]), os_[i], count, H, seq=i,
+                             dtype=in_dtype, out_dtype="f32")
+    for i in range(nseq):
+        assert np.array_equal(ob[i], os_[i]), f"sequence {i} (past {pasts[i]}): batched and single calls differ"
+    # 16-bit output (rows past each sequence's tokens left alone): the same
+    # values as the f32 output, rounded to nearest even
+    cb2 = b2a.GpuKVCache(ctx, cfg, cap, batch=nseq, dtype="f16")
+    for b, L in enumerate(pasts):
+        if L:
+            cb2.writeAt(0, 0, oracle.normal_array(L * KVH * D, 700 + b), oracle.normal_array(L * KVH * D, 800 + b), L,
+                        seq=b)
+    cb2.setLengths(pasts)
+    o16 = np.zeros((nseq, count, H * D), np.uint16)
+    b2a.attentionPrefillBatch(ctx, cb2, rope, 0, bits(q), bits(k), bits(v), o16, count, H, 0, nseq, dtype=in_dtype,
+                              out_dtype="bf16")
+    want = oracle.to_bits(ob.reshape(-1), "bf16").reshape(o16.shape)
+    bad = np.argwhere(o16 != want)
+    assert len(bad) == 0, f"bf16 output differs from the rounded f32 output at {len(bad)} places, first {bad[:4]}"
+    cb2.close()
+    for i in (0, 1, nseq - 1):
+        past = pasts[i]
+        qr = oracle.rope_rows(q[i], range(past, past + count), D, THETA).reshape(-1)
+        kr = oracle.round_to(oracle.rope_rows(k[i], range(past, past + count), D, THETA), "f16")
+        keys = np.concatenate([hk[i].reshape(past, KVH * D), kr]) if past else kr
+        vals = np.concatenate([hv[i].reshape(past, KVH * D), oracle.round_to(v[i], "f16")]) if past else \
+            oracle.round_to(v[i], "f16")
+        ref = oracle.grouped_attention(qr, keys.reshape(-1), vals.reshape(-1), count, past, H, KVH, D)
+        assert_parity(ob[i].reshape(-1), ref, "f32", f"{in_dtype} batched prefill over many units, sequence {i}")
+    cb.close()
+    cs.close()
