@@ -170,6 +170,22 @@ bool encode_pool_map(CUtensorMap* map, void* base, uint64_t rows, b2a_dtype dtyp
   return r == CUDA_SUCCESS;
 }
 
+// A prefill call's rotated f16 queries [rows][heads * 64] as a 2D tensor;
+// each load is one head's 128-row query tile, 128-byte swizzled as the
+// tensor-core MMAs read it.
+bool encode_query_map(CUtensorMap* map, void* q_rot, uint64_t rows, int heads) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr || rows >= (1ull << 32)) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(heads) * 64, rows};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(heads) * 128};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q_rot, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Carves device staging for host-pointer calls: each `add` reserves an
 // aligned slice of ctx->d_stage.
 struct Stage {
@@ -829,6 +845,7 @@ b2a_status b2a_destroy(b2a_ctx* ctx) {
     if (ctx->async_free[i]) cudaEventDestroy(ctx->async_free[i]);
   }
   if (ctx->d_scratch) cudaFree(ctx->d_scratch);
+  if (ctx->d_qrot) cudaFree(ctx->d_qrot);
   nccl_split_release(ctx);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_err) cudaFreeHost(ctx->h_err);
@@ -1623,8 +1640,40 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
   p.k_new = k;
   p.v_new = v;
   p.horizon_extra = 1;
+  if (c->has_tmaps) {
+    p.tmap_k = &c->tmap_k;
+    p.tmap_v = &c->tmap_v;
+  }
+  // the tensor-core kernels (f16 cache) take their query tiles by TMA from
+  // RoPE(q) rows that the append kernel writes
+  CUtensorMap qmap;
+  if (c->dtype == B2A_F16 && c->head_dim == 64 && c->has_tmaps) {
+    const size_t rows = static_cast<size_t>(nseq) * count;
+    if ((s = ensure_buffer(&ctx->d_qrot, &ctx->d_qrot_bytes, rows * num_heads * 64 * sizeof(uint16_t),
+                           "allocating rotated queries")) != B2A_OK) {
+      return s;
+    }
+    if (encode_query_map(&qmap, ctx->d_qrot, rows, num_heads)) {
+      p.q_rot = static_cast<uint16_t*>(ctx->d_qrot);
+      p.tmap_q = &qmap;
+    }
+  }
+  AttnParams attn = p;   // as the attention kernels see it: the new rows are in the cache
+  attn.k_new = nullptr;
+  attn.v_new = nullptr;
+  const bool pair = prefill_pair_supported(attn) && prefill_tiles_per_cta(ctx, count, num_heads * nseq) == 2;
+  // The one-tile kernel takes them too once its CTAs need more than one wave
+  // on the SMs: the later CTAs then find their queries ready. In a single
+  // wave its own staging runs under the append kernel, which the rotated rows
+  // would instead put in front of every CTA's first MMA.
+  const int64_t tc_ctas = static_cast<int64_t>(num_heads) * nseq * ((count + 127) / 128);
+  if (!pair && !(prefill_tc_supported(attn) && c->dtype == B2A_F16 && tc_ctas > ctx->sm_count)) {
+    p.q_rot = nullptr;
+    p.tmap_q = nullptr;
+  }
   // RoPE(K) + append first (src/cpu/model.js:116 writes before attending), then
-  // causal attention over past+count with RoPE(Q) fused into the Q load.
+  // causal attention over past+count, with RoPE(Q) done by the append kernel
+  // (tensor-core kernels, f16 cache) or fused into the Q load (the others).
   cudaError_t e;
   {
     KernelTimer kt(ctx, K_ROPE_APPEND);
@@ -1633,11 +1682,7 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
   if (e != cudaSuccess) return cuda_fail(e, "launching the rope append");
   p.k_new = nullptr;
   p.v_new = nullptr;
-  if (c->has_tmaps) {
-    p.tmap_k = &c->tmap_k;
-    p.tmap_v = &c->tmap_v;
-  }
-  if (prefill_pair_supported(p) && prefill_tiles_per_cta(ctx, count, num_heads * nseq) == 2) {
+  if (pair) {
     // tensor-core causal attention, two heads' 128-query tiles per CTA (f16 cache)
     {
       KernelTimer kt(ctx, K_PREFILL_PAIR);

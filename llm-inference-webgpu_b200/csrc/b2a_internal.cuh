@@ -25,6 +25,9 @@ struct b2a_ctx {
   // split-KV partials, grown on demand
   void* d_scratch = nullptr;
   size_t d_scratch_bytes = 0;
+  // rotated f16 queries of a tensor-core prefill call, grown on demand
+  void* d_qrot = nullptr;
+  size_t d_qrot_bytes = 0;
   int32_t* d_err = nullptr;             // device error word (bounded waits, bounds checks)
   int32_t* h_err = nullptr;             // pinned host copy of it, read after a call's stream sync
   int32_t* d_counters = nullptr;        // fused split-KV merge counters, kept zeroed
@@ -158,6 +161,12 @@ struct AttnParams {
   int32_t* err;
   const void* tmap_k;         // host CUtensorMap* of the pools (tensor-core path), or null
   const void* tmap_v;
+  // Prefill with an f16 cache: the append kernel also writes RoPE(q) as f16
+  // rows [sequence][token][head][64] to q_rot (null: not asked for), and the
+  // tensor-core prefill loads its query tiles from there through tmap_q (a
+  // host CUtensorMap* over q_rot as [rows][heads * 64], 128-row boxes).
+  uint16_t* q_rot;
+  const void* tmap_q;
   // Fused split-KV merge (tensor-core path): when fuse_out is set, a group
   // whose keys fit one chunk writes its result straight to fuse_out, and the
   // last CTA of every other group merges that group's chunk partials, so no

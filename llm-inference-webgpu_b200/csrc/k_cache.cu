@@ -1,49 +1,152 @@
 // KV-cache kernels: fused RoPE(K) + round + append, raw writeAt, and the
 // device mirror of the per-sequence lengths.
+#include <climits>
+
 #include "b2a_internal.cuh"
 #include "k_util.cuh"
 
 namespace b2a {
 
+namespace {
+
+// Eight 16-bit or f32 elements of a row -> f32 (vector loads when 16-byte aligned).
+__device__ __forceinline__ void load8(const void* base, int64_t at, int dt, float (&x)[8]) {
+  if (dt != DT_F32 && (reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + at);
+    const uint16_t* hw = reinterpret_cast<const uint16_t*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+      x[e] = dt == DT_F16 ? __half2float(__ushort_as_half(hw[e])) : __bfloat162float(__ushort_as_bfloat16(hw[e]));
+  } else if (dt == DT_F32 && (reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+    const float4* f4 = reinterpret_cast<const float4*>(static_cast<const float*>(base) + at);
+    *reinterpret_cast<float4*>(&x[0]) = f4[0];
+    *reinterpret_cast<float4*>(&x[4]) = f4[1];
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; e++) x[e] = ld_as_f32(base, at + e, dt);
+  }
+}
+
+// Eight f32 values -> a row of the cache dtype, rounded as st_from_f32 rounds
+// (8-element rows of a 64-wide head are 16-byte aligned in the pools).
+__device__ __forceinline__ void store8(void* base, int64_t at, int dt, const float (&x)[8]) {
+  if (dt == DT_F32) {
+    float4* f4 = reinterpret_cast<float4*>(static_cast<float*>(base) + at);
+    f4[0] = make_float4(x[0], x[1], x[2], x[3]);
+    f4[1] = make_float4(x[4], x[5], x[6], x[7]);
+    return;
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const uint32_t lo = dt == DT_F16 ? f32_to_f16_bits(x[2 * e]) : f32_to_bf16_bits(x[2 * e]);
+    const uint32_t hi = dt == DT_F16 ? f32_to_f16_bits(x[2 * e + 1]) : f32_to_bf16_bits(x[2 * e + 1]);
+    w[e] = lo | (hi << 16);
+  }
+  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + at) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+}  // namespace
+
 // src/cpu/model.js:103-116 (rope-k at absolute position past+t, then
-// kv.writeAt), src/gpu/model.js:327-338 (ROPE on k, two copies). One thread
-// per rotation pair (t, kv head, j); the same thread stores both halves of V.
-__global__ void k_rope_append(AttnParams p, int seq_first, int count, int nseq) {
+// kv.writeAt), src/gpu/model.js:327-338 (ROPE on k, two copies), and, for the
+// two-tile tensor-core prefill, RoPE(q) (src/cpu/model.js:103-106) as f16
+// rows. Grid (blocks, sequences); one thread per 8 dims of one (token, head)
+// row, so eight neighbouring lanes cover a row (coalesced 16-byte accesses)
+// and lanes l and l ^ 4 hold the two halves of each rotation pair, swapped by
+// shuffle. Blocks [0, kv_blocks) rotate and append K and append V; blocks from
+// kv_blocks on (when p.q_rot is set) rotate the queries.
+// K: IEEE f64 from the f64 table, every product and sum rounded separately
+// (rope_pair_f64), then the cache dtype. Q: f32 from the f32 table, rounded
+// once to f16, x[d] c - x[d+32] s and x[d+32] c + x[d] s: the arithmetic the
+// prefill kernels' own query staging uses.
+__global__ void k_rope_append(AttnParams p, int seq_first, int count, int kv_blocks) {
   // a kernel launched after this one as a programmatic dependent may start its
   // prologue now; it waits for this grid before reading the cache
   asm volatile("griddepcontrol.launch_dependents;");
-  const int half = p.head_dim >> 1;
-  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * half;   // per sequence
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n * nseq;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int b = static_cast<int>(i / n);
-    const int64_t ib = i - b * n;
-    const int seq_idx = seq_first + b;
-    const int past = p.len[seq_idx];
-    const int j = static_cast<int>(ib % half);
-    const int g = static_cast<int>((ib / half) % p.kv_heads);
-    const int t = static_cast<int>(ib / (static_cast<int64_t>(half) * p.kv_heads));
-    const int pos = past + t;
-    const int64_t src = ((static_cast<int64_t>(b) * count + t) * p.kv_heads + g) * p.head_dim;
-    const int64_t dst = kv_elem(p, seq_idx, p.layer_begin, g, pos);
-    const double c = p.rope_cos[static_cast<int64_t>(pos) * half + j];
-    const double s = p.rope_sin[static_cast<int64_t>(pos) * half + j];
-    float lo, hi;
-    rope_pair_f64(ld_as_f32(p.k_new, src + j, p.in_dtype), ld_as_f32(p.k_new, src + j + half, p.in_dtype), c,
-                  s, lo, hi);
-    st_from_f32(p.kc_w, dst + j, p.cache_dtype, lo);
-    st_from_f32(p.kc_w, dst + j + half, p.cache_dtype, hi);
-    convert_elem(p.v_new, src + j, p.in_dtype, p.vc_w, dst + j, p.cache_dtype);
-    convert_elem(p.v_new, src + j + half, p.in_dtype, p.vc_w, dst + j + half, p.cache_dtype);
+  const int b = static_cast<int>(blockIdx.y);
+  const int seq_idx = seq_first + b;
+  const int past = p.len[seq_idx];
+  const bool kv = static_cast<int>(blockIdx.x) < kv_blocks;
+  const int heads = kv ? p.kv_heads : p.heads;
+  const int i = (kv ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) - kv_blocks) * blockDim.x +
+                threadIdx.x;
+  const bool live = i < count * heads * 8;
+  const int ii = live ? i : 0;   // a lane past the end computes row 0 for the shuffles, stores nothing
+  const int l = ii & 7;
+  const int row = ii >> 3;
+  const int t = row / heads;
+  const int h = row - t * heads;
+  const int pos = past + t;
+  const int64_t at = ((static_cast<int64_t>(b) * count + t) * heads + h) * p.head_dim + 8 * l;
+  const int j0 = 8 * (l & 3);                     // rotation index of the lane's first dim
+  float x[8], y[8];
+  load8(kv ? p.k_new : p.q, at, p.in_dtype, x);
+#pragma unroll
+  for (int e = 0; e < 8; e++) y[e] = __shfl_xor_sync(0xffffffffu, x[e], 4);
+  float o[8];
+  if (kv) {
+    // the lane's 8 table entries: 64 bytes at a 64-byte boundary of each table
+    const double2* c2 = reinterpret_cast<const double2*>(p.rope_cos + static_cast<int64_t>(pos) * (p.head_dim / 2) + j0);
+    const double2* s2 = reinterpret_cast<const double2*>(p.rope_sin + static_cast<int64_t>(pos) * (p.head_dim / 2) + j0);
+    double cr[8], sr[8];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const double2 cc = c2[e], ss = s2[e];
+      cr[2 * e] = cc.x;
+      cr[2 * e + 1] = cc.y;
+      sr[2 * e] = ss.x;
+      sr[2 * e + 1] = ss.y;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const double dx = static_cast<double>(x[e]), dy = static_cast<double>(y[e]);
+      // first half (l < 4): lo c - hi s; second half: hi c + lo s
+      o[e] = l < 4 ? __double2float_rn(__dsub_rn(__dmul_rn(dx, cr[e]), __dmul_rn(dy, sr[e])))
+                   : __double2float_rn(__dadd_rn(__dmul_rn(dx, cr[e]), __dmul_rn(dy, sr[e])));
+    }
+    const int64_t dst = kv_elem(p, seq_idx, p.layer_begin, h, pos) + 8 * l;
+    float vv[8];
+    load8(p.v_new, at, p.in_dtype, vv);
+    if (live) {
+      store8(p.kc_w, dst, p.cache_dtype, o);
+      if (p.in_dtype == p.cache_dtype && p.cache_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.v_new) & 15) == 0) {
+        // the same 16-bit dtype: the bits as given
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.vc_w) + dst) =
+            *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.v_new) + at);
+      } else {
+        store8(p.vc_w, dst, p.cache_dtype, vv);   // exact when the dtypes agree, else rounded as st_from_f32
+      }
+    }
+  } else {
+    const int64_t ra = static_cast<int64_t>(pos) * (p.head_dim / 2) + j0;
+    float c[8], sn[8];
+    *reinterpret_cast<float4*>(&c[0]) = *reinterpret_cast<const float4*>(p.rope_cos32 + ra);
+    *reinterpret_cast<float4*>(&c[4]) = *reinterpret_cast<const float4*>(p.rope_cos32 + ra + 4);
+    *reinterpret_cast<float4*>(&sn[0]) = *reinterpret_cast<const float4*>(p.rope_sin32 + ra);
+    *reinterpret_cast<float4*>(&sn[4]) = *reinterpret_cast<const float4*>(p.rope_sin32 + ra + 4);
+    const float sgn = l < 4 ? -1.f : 1.f;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const __half2 h2 = __floats2half2_rn(fmaf(x[e], c[e], sgn * (y[e] * sn[e])),
+                                           fmaf(x[e + 1], c[e + 1], sgn * (y[e + 1] * sn[e + 1])));
+      w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+    }
+    if (live) *reinterpret_cast<uint4*>(p.q_rot + at) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
 cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cudaStream_t st, int nseq) {
-  const int64_t n = static_cast<int64_t>(count) * p.kv_heads * (p.head_dim / 2) * nseq;
-  if (n == 0) return cudaSuccess;
+  if (count <= 0 || nseq <= 0) return cudaSuccess;
+  if (p.head_dim != 64 || nseq > 65535) return cudaErrorInvalidValue;
   const int threads = 256;
-  const int blocks = static_cast<int>((n + threads - 1) / threads < 4096 ? (n + threads - 1) / threads : 4096);
-  k_rope_append<<<blocks, threads, 0, st>>>(p, seq_idx, count, nseq);
+  const int64_t kv_rows8 = static_cast<int64_t>(count) * p.kv_heads * 8;
+  const int64_t q_rows8 = p.q_rot != nullptr ? static_cast<int64_t>(count) * p.heads * 8 : 0;
+  if (kv_rows8 > INT32_MAX - threads || q_rows8 > INT32_MAX - threads) return cudaErrorInvalidValue;
+  const int kv_blocks = static_cast<int>((kv_rows8 + threads - 1) / threads);
+  const int q_blocks = static_cast<int>((q_rows8 + threads - 1) / threads);
+  k_rope_append<<<dim3(kv_blocks + q_blocks, nseq), threads, 0, st>>>(p, seq_idx, count, kv_blocks);
   return cudaGetLastError();
 }
 

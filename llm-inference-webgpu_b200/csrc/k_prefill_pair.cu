@@ -5,9 +5,13 @@
 // (heads 2k and 2k+1 of the group; an odd group leaves one CTA per tile row
 // with a single head), so both see exactly the same keys and one K/V stream
 // feeds both. Twelve warps:
-//   warp 0      producer: K and V tiles (128 positions) of the rotated,
-//               appended cache into a 4-stage ring by 2D TMA (128-byte
-//               swizzle), after waiting on the append kernel's grid.
+//   warp 0      producer: after waiting on the append kernel's grid, the
+//               CTA's query tiles (RoPE(q) as f16, written by that kernel)
+//               and then K and V tiles (128 positions) of the rotated,
+//               appended cache into a 4-stage ring, all by 2D TMA (128-byte
+//               swizzle). Rows of a query tile past its sequence's tokens
+//               hold the next sequence's queries (or zeros past the last);
+//               their outputs are never stored.
 //   warp 1      allocates the 512 TMEM columns and issues every MMA:
 //                 S_w = Q_w . K_j^T    M=128 N=128 K=64  into S_w
 //                 O_w += P_w . V_j     M=128 N=64  K=128 (A = P_w from TMEM)
@@ -74,7 +78,7 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
 
 __global__ void __launch_bounds__(kThreads, 1)
     k_prefill_pair(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                   AttnParams p) {
+                   const __grid_constant__ CUtensorMap tmap_q, AttnParams p) {
   constexpr uint32_t kIdescS = idesc_f16(0, 0, kBM, kBN);
   constexpr uint32_t kIdescPV = idesc_f16(0, 1, kBM, kD);
 
@@ -88,7 +92,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 2;
-  uint64_t* q_ready = pv_done + 2;
+  uint64_t* q_ready = pv_done + 2;         // the CTA's query tiles are in Q_0 (and Q_1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -120,8 +124,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_free[w], 128);
       mbar_init(&p_full[w], 128);
       mbar_init(&pv_done[w], 1);
-      mbar_init(&q_ready[w], 128);
+
     }
+    mbar_init(q_ready, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -145,9 +150,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // the cache rows come from the preceding append kernel
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      // the append kernel stored the new rows through the generic proxy; the
-      // tensor loads below read them through the async proxy
+      // the append kernel stored the new rows and the rotated queries through
+      // the generic proxy; the tensor loads below read them through the async proxy
       asm volatile("fence.proxy.async.global;" ::: "memory");
+      // the query tiles: RoPE(q) as f16 rows, 128-byte swizzled as the MMAs read them
+      mbar_arrive_expect_tx(q_ready, static_cast<uint32_t>(ntile * kQBytes));
+      for (int w = 0; w < ntile; w++) {
+        tma_load_2d(smem_u32(smem + kOffQ + w * kQBytes), &tmap_q, q_ready, (h0 + w) * kD, sb * p.tokens + q0);
+      }
       for (int j = 0; j < n_kv; j++) {
         const int s = j % kStages;
         if (j >= kStages) mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, dead);
@@ -168,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // calls, so the warp stays converged); the elected lane issues and commits.
     {
       const uint32_t q_base = smem_u32(smem + kOffQ);
-      for (int w = 0; w < ntile; w++) mbar_wait(&q_ready[w], 0, p.err, dead);
+      mbar_wait(q_ready, 0, p.err, dead);
       auto issue_s = [&](int w, int j) {
         const uint32_t kt = ring + (j % kStages) * kStageBytes;
         const uint32_t qw = q_base + w * kQBytes;
@@ -224,67 +234,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = q0 + r;                          // token index within this call
     const int a = past + t;                        // absolute position
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    // stage RoPE(q) as f16 into Q_w, 128-byte-swizzled K-major rows; every
-    // global load of the row is issued before the first use. f32 rotation:
-    // its error (~2^-24) is far below the f16 rounding that follows.
-    {
-      float x[kD], cs[kD / 2], sn[kD / 2];
-      if (t < p.tokens) {
-        const int64_t qrow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;
-        const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos32 + static_cast<int64_t>(a) * (kD / 2));
-        const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin32 + static_cast<int64_t>(a) * (kD / 2));
-        if (p.in_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.q) & 15) == 0) {
-          uint4 u[8];   // one 16-byte load per 8 elements
-          const uint4* q4 = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + qrow);
-#pragma unroll
-          for (int i = 0; i < 8; i++) u[i] = q4[i];
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            reinterpret_cast<float4*>(cs)[i] = c4[i];
-            reinterpret_cast<float4*>(sn)[i] = s4[i];
-          }
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const uint16_t* hw = reinterpret_cast<const uint16_t*>(&u[i]);
-#pragma unroll
-            for (int e = 0; e < 8; e++)
-              x[8 * i + e] = p.in_dtype == DT_F16 ? __half2float(__ushort_as_half(hw[e]))
-                                                  : __bfloat162float(__ushort_as_bfloat16(hw[e]));
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < kD; e++) x[e] = ld_as_f32(p.q, qrow + e, p.in_dtype);
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            reinterpret_cast<float4*>(cs)[i] = c4[i];
-            reinterpret_cast<float4*>(sn)[i] = s4[i];
-          }
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < kD; e++) x[e] = 0.f;
-#pragma unroll
-        for (int e = 0; e < kD / 2; e++) cs[e] = sn[e] = 0.f;
-      }
-      unsigned char* row = smem + kOffQ + w * kQBytes + r * 128;
-#pragma unroll
-      for (int c = 0; c < 4; c++) {   // chunk c holds dims 8c..8c+7; chunk c+4 dims 32+8c..
-        uint4 v0, v1;
-        uint32_t* p0 = reinterpret_cast<uint32_t*>(&v0);
-        uint32_t* p1 = reinterpret_cast<uint32_t*>(&v1);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const int d = 8 * c + 2 * e;
-          p0[e] = pack_f16x2(fmaf(x[d], cs[d], -(x[d + 32] * sn[d])), fmaf(x[d + 1], cs[d + 1], -(x[d + 33] * sn[d + 1])));
-          p1[e] = pack_f16x2(fmaf(x[d + 32], cs[d], x[d] * sn[d]), fmaf(x[d + 33], cs[d + 1], x[d + 1] * sn[d + 1]));
-        }
-        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = v0;
-        *reinterpret_cast<uint4*>(row + (((c + 4) ^ (r & 7)) << 4)) = v1;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&q_ready[w]);
-    }
-
     const uint32_t scol = tmem + lane_addr + kColS + w * kBN;
     const uint32_t ocol = tmem + lane_addr + kColO + w * kD;
     const uint32_t pcol = tmem + lane_addr + kColP + w * (kBN / 2);
@@ -452,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 bool prefill_pair_supported(const AttnParams& p) {
   // grid (heads, batch, query tiles): y and z are limited to 65535
-  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.batch >= 1 && p.batch <= 65535 &&
+  return p.tmap_k != nullptr && p.tmap_v != nullptr && p.tmap_q != nullptr && p.batch >= 1 && p.batch <= 65535 &&
          (p.tokens + kBM - 1) / kBM <= 65535 && p.num_layers == 1 && p.head_dim == kD &&
          p.k_new == nullptr && p.cache_dtype == DT_F16 && p.group >= 1;
 }
@@ -484,7 +433,7 @@ cudaError_t launch_prefill_pair(const AttnParams& p, void* out, int out_dtype, c
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k_prefill_pair, *static_cast<const CUtensorMap*>(p.tmap_k),
-                            *static_cast<const CUtensorMap*>(p.tmap_v), q);
+                            *static_cast<const CUtensorMap*>(p.tmap_v), *static_cast<const CUtensorMap*>(p.tmap_q), q);
 }
 
 }  // namespace b2a

@@ -16,8 +16,11 @@
 //               raised lazily (only when a tile's max exceeds it by more than
 //               2^8), so O in TMEM is rescaled rarely. P is written back into
 //               the S buffer's columns (it aliases the consumed S).
-// RoPE(q) is applied while the softmax warps stage the Q tile into swizzled
-// shared memory (f32 rotation: the operand is rounded to 16 bits next).
+// RoPE(q): with an f16 cache the append kernel before this one writes the
+// rotated queries as f16 rows and the producer loads the Q tile by TMA (one
+// box, 128-byte swizzle); with a bf16 cache the softmax warps rotate and stage
+// the Q tile (and its residual) into swizzled shared memory themselves. Both
+// rotate in f32 and round the operand to 16 bits next.
 // The kernel is launched as a programmatic dependent of the RoPE(K) + append
 // kernel before it: everything up to the first K/V load (barriers, TMEM, the
 // Q tile) overlaps that kernel, and the producer waits on the grid dependency
@@ -90,8 +93,10 @@ __device__ __forceinline__ void split2_bf16(float a, float b, uint32_t& hi, uint
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     k_prefill_tc(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                 AttnParams p) {
+                 const __grid_constant__ CUtensorMap tmap_q, AttnParams p) {
   constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;
+  // the Q tile by TMA from the rotated rows (f16 cache, rows written)
+  const bool q_tma = !kSplit && p.q_rot != nullptr;
   constexpr int kAB = kSplit ? 1 : 0;
   constexpr uint32_t kIdescS = idesc_f16(kAB, 0, kBM, kBN);
   constexpr uint32_t kIdescPV = idesc_f16(kAB, 1, kBM, kD);
@@ -140,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_full[b], 128);
     }
     mbar_init(o_done, 1);
-    mbar_init(q_ready, 128);
+    mbar_init(q_ready, q_tma ? 1 : 128);
     mbar_init(o_final, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -160,9 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // the cache rows come from the preceding append kernel
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      // the append kernel stored the new rows through the generic proxy; the
-      // tensor loads below read them through the async proxy
+      // the append kernel stored the new rows (and the rotated queries) through
+      // the generic proxy; the tensor loads below read them through the async proxy
       asm volatile("fence.proxy.async.global;" ::: "memory");
+      if (q_tma) {
+        mbar_arrive_expect_tx(q_ready, kQBytes);
+        tma_load_2d(smem_u32(smem + kOffQHi), &tmap_q, q_ready, h * kD, sb * p.tokens + q0);
+      }
       for (int j = 0; j < n_kv; j++) {
         const int s = j % kStages;
         if (j >= kStages) mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.err, dead);
@@ -249,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // use so the thread pays one memory latency, not one per chunk. The
     // rotation runs in f32 from the f32 table: its error (~2^-24) is far below
     // the 16-bit rounding of the MMA operand that follows.
-    {
+    if (!q_tma) {
       float x[kD], cs[kD / 2], sn[kD / 2];
       if (t < p.tokens) {
         const int64_t qrow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;
@@ -513,8 +522,13 @@ cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cud
   cudaGetDevice(&dev);
   static bool attr_f16[64] = {}, attr_bf16[64] = {};
   const bool f16 = p.cache_dtype == DT_F16;
-  void (*kern)(const CUtensorMap, const CUtensorMap, AttnParams) =
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, AttnParams) =
       f16 ? k_prefill_tc<__half> : k_prefill_tc<__nv_bfloat16>;
+  // the rotated-query map travels with the rows it covers; absent (bf16
+  // cache, or the rows not written) the kernel stages its own Q tile
+  CUtensorMap mq = {};
+  if (f16 && p.q_rot != nullptr && p.tmap_q != nullptr) mq = *static_cast<const CUtensorMap*>(p.tmap_q);
+  else q.q_rot = nullptr;
   bool* attr = f16 ? attr_f16 : attr_bf16;
   if (dev < 64 && !attr[dev]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
@@ -531,7 +545,7 @@ cudaError_t launch_prefill_tc(const AttnParams& p, void* out, int out_dtype, cud
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *mk, *mv, q);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *mk, *mv, mq, q);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
