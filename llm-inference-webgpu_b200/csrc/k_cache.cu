@@ -48,19 +48,27 @@ __device__ __forceinline__ void store8(void* base, int64_t at, int dt, const flo
 
 }  // namespace
 
+// Query heads and KV heads one thread covers (the same 8 dims of one token in
+// each): the rotation-table entries are loaded once for all of them, and the
+// rows' loads are all in flight together.
+constexpr int kQGroup = 4;
+constexpr int kKVGroup = 1;
+
 // src/cpu/model.js:103-116 (rope-k at absolute position past+t, then
 // kv.writeAt), src/gpu/model.js:327-338 (ROPE on k, two copies), and, for the
-// two-tile tensor-core prefill, RoPE(q) (src/cpu/model.js:103-106) as f16
-// rows. Grid (blocks, sequences); one thread per 8 dims of one (token, head)
-// row, so eight neighbouring lanes cover a row (coalesced 16-byte accesses)
-// and lanes l and l ^ 4 hold the two halves of each rotation pair, swapped by
-// shuffle. Blocks [0, kv_blocks) rotate and append K and append V; blocks from
-// kv_blocks on (when p.q_rot is set) rotate the queries.
+// tensor-core prefill, RoPE(q) (src/cpu/model.js:103-106) as f16 rows.
+// Grid (blocks, sequences); a thread takes 8 dims (lane l: dims 8l..8l+7, 16
+// bytes of a 16-bit row) of one token in a group of heads, so eight
+// neighbouring lanes cover a row (coalesced 16-byte accesses) and lanes l and
+// l ^ 4 hold the two halves of each rotation pair, swapped by shuffle. Blocks
+// [0, kv_blocks) rotate and append K and append V (kKVGroup KV heads per
+// thread); blocks from kv_blocks on (when p.q_rot is set) rotate the queries
+// (kQGroup heads per thread).
 // K: IEEE f64 from the f64 table, every product and sum rounded separately
 // (rope_pair_f64), then the cache dtype. Q: f32 from the f32 table, rounded
 // once to f16, x[d] c - x[d+32] s and x[d+32] c + x[d] s: the arithmetic the
 // prefill kernels' own query staging uses.
-__global__ void k_rope_append(AttnParams p, int seq_first, int count, int kv_blocks) {
+__global__ void __launch_bounds__(256, 4) k_rope_append(AttnParams p, int seq_first, int count, int kv_blocks) {
   // a kernel launched after this one as a programmatic dependent may start its
   // prologue now; it waits for this grid before reading the cache
   asm volatile("griddepcontrol.launch_dependents;");
@@ -69,23 +77,32 @@ __global__ void k_rope_append(AttnParams p, int seq_first, int count, int kv_blo
   const int past = p.len[seq_idx];
   const bool kv = static_cast<int>(blockIdx.x) < kv_blocks;
   const int heads = kv ? p.kv_heads : p.heads;
+  const int group = kv ? kKVGroup : kQGroup;
+  const int groups = (heads + group - 1) / group;           // head groups per token
   const int i = (kv ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) - kv_blocks) * blockDim.x +
                 threadIdx.x;
-  const bool live = i < count * heads * 8;
-  const int ii = live ? i : 0;   // a lane past the end computes row 0 for the shuffles, stores nothing
+  const bool live = i < count * groups * 8;
+  const int ii = live ? i : 0;   // a lane past the end computes token 0 for the shuffles, stores nothing
   const int l = ii & 7;
-  const int row = ii >> 3;
-  const int t = row / heads;
-  const int h = row - t * heads;
+  const int slot = ii >> 3;
+  const int t = slot / groups;
+  const int h0 = (slot - t * groups) * group;
   const int pos = past + t;
-  const int64_t at = ((static_cast<int64_t>(b) * count + t) * heads + h) * p.head_dim + 8 * l;
-  const int j0 = 8 * (l & 3);                     // rotation index of the lane's first dim
-  float x[8], y[8];
-  load8(kv ? p.k_new : p.q, at, p.in_dtype, x);
-#pragma unroll
-  for (int e = 0; e < 8; e++) y[e] = __shfl_xor_sync(0xffffffffu, x[e], 4);
-  float o[8];
+  const int64_t row0 = (static_cast<int64_t>(b) * count + t) * heads;   // (sequence, token) row of head 0
+  const int j0 = 8 * (l & 3);                                          // rotation index of the lane's first dim
   if (kv) {
+    float x[kKVGroup][8], y[kKVGroup][8], vv[kKVGroup][8];
+    uint4 vraw[kKVGroup];
+    const bool vcopy = p.in_dtype == p.cache_dtype && p.cache_dtype != DT_F32 &&
+                       (reinterpret_cast<uintptr_t>(p.v_new) & 15) == 0;   // the same 16-bit dtype: bits as given
+#pragma unroll
+    for (int m = 0; m < kKVGroup; m++) {
+      const bool ok = live && h0 + m < heads;
+      const int64_t at = (row0 + (ok ? h0 + m : 0)) * p.head_dim + 8 * l;
+      load8(p.k_new, at, p.in_dtype, x[m]);
+      if (vcopy) vraw[m] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.v_new) + at);
+      else load8(p.v_new, at, p.in_dtype, vv[m]);
+    }
     // the lane's 8 table entries: 64 bytes at a 64-byte boundary of each table
     const double2* c2 = reinterpret_cast<const double2*>(p.rope_cos + static_cast<int64_t>(pos) * (p.head_dim / 2) + j0);
     const double2* s2 = reinterpret_cast<const double2*>(p.rope_sin + static_cast<int64_t>(pos) * (p.head_dim / 2) + j0);
@@ -99,26 +116,32 @@ __global__ void k_rope_append(AttnParams p, int seq_first, int count, int kv_blo
       sr[2 * e + 1] = ss.y;
     }
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-      const double dx = static_cast<double>(x[e]), dy = static_cast<double>(y[e]);
-      // first half (l < 4): lo c - hi s; second half: hi c + lo s
-      o[e] = l < 4 ? __double2float_rn(__dsub_rn(__dmul_rn(dx, cr[e]), __dmul_rn(dy, sr[e])))
-                   : __double2float_rn(__dadd_rn(__dmul_rn(dx, cr[e]), __dmul_rn(dy, sr[e])));
-    }
-    const int64_t dst = kv_elem(p, seq_idx, p.layer_begin, h, pos) + 8 * l;
-    float vv[8];
-    load8(p.v_new, at, p.in_dtype, vv);
-    if (live) {
-      store8(p.kc_w, dst, p.cache_dtype, o);
-      if (p.in_dtype == p.cache_dtype && p.cache_dtype != DT_F32 && (reinterpret_cast<uintptr_t>(p.v_new) & 15) == 0) {
-        // the same 16-bit dtype: the bits as given
-        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.vc_w) + dst) =
-            *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.v_new) + at);
-      } else {
-        store8(p.vc_w, dst, p.cache_dtype, vv);   // exact when the dtypes agree, else rounded as st_from_f32
+    for (int m = 0; m < kKVGroup; m++)
+#pragma unroll
+      for (int e = 0; e < 8; e++) y[m][e] = __shfl_xor_sync(0xffffffffu, x[m][e], 4);
+#pragma unroll
+    for (int m = 0; m < kKVGroup; m++) {
+      if (!live || h0 + m >= heads) continue;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const double dx = static_cast<double>(x[m][e]), dy = static_cast<double>(y[m][e]);
+        // first half (l < 4): lo c - hi s; second half: hi c + lo s
+        o[e] = l < 4 ? __double2float_rn(__dsub_rn(__dmul_rn(dx, cr[e]), __dmul_rn(dy, sr[e])))
+                     : __double2float_rn(__dadd_rn(__dmul_rn(dx, cr[e]), __dmul_rn(dy, sr[e])));
       }
+      const int64_t dst = kv_elem(p, seq_idx, p.layer_begin, h0 + m, pos) + 8 * l;
+      store8(p.kc_w, dst, p.cache_dtype, o);
+      if (vcopy) *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.vc_w) + dst) = vraw[m];
+      else store8(p.vc_w, dst, p.cache_dtype, vv[m]);   // exact when the dtypes agree, else rounded as st_from_f32
     }
   } else {
+    float x[kQGroup][8];
+#pragma unroll
+    for (int m = 0; m < kQGroup; m++) {
+      const bool ok = live && h0 + m < heads;
+      load8(p.q, (row0 + (ok ? h0 + m : 0)) * p.head_dim + 8 * l, p.in_dtype, x[m]);
+    }
     const int64_t ra = static_cast<int64_t>(pos) * (p.head_dim / 2) + j0;
     float c[8], sn[8];
     *reinterpret_cast<float4*>(&c[0]) = *reinterpret_cast<const float4*>(p.rope_cos32 + ra);
@@ -126,14 +149,21 @@ __global__ void k_rope_append(AttnParams p, int seq_first, int count, int kv_blo
     *reinterpret_cast<float4*>(&sn[0]) = *reinterpret_cast<const float4*>(p.rope_sin32 + ra);
     *reinterpret_cast<float4*>(&sn[4]) = *reinterpret_cast<const float4*>(p.rope_sin32 + ra + 4);
     const float sgn = l < 4 ? -1.f : 1.f;
-    uint32_t w[4];
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const __half2 h2 = __floats2half2_rn(fmaf(x[e], c[e], sgn * (y[e] * sn[e])),
-                                           fmaf(x[e + 1], c[e + 1], sgn * (y[e + 1] * sn[e + 1])));
-      w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+    for (int m = 0; m < kQGroup; m++) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float y0 = __shfl_xor_sync(0xffffffffu, x[m][e], 4);
+        const float y1 = __shfl_xor_sync(0xffffffffu, x[m][e + 1], 4);
+        const __half2 h2 = __floats2half2_rn(fmaf(x[m][e], c[e], sgn * (y0 * sn[e])),
+                                             fmaf(x[m][e + 1], c[e + 1], sgn * (y1 * sn[e + 1])));
+        w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      if (live && h0 + m < heads) {
+        *reinterpret_cast<uint4*>(p.q_rot + (row0 + h0 + m) * p.head_dim + 8 * l) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
     }
-    if (live) *reinterpret_cast<uint4*>(p.q_rot + at) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -141,11 +171,11 @@ cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cuda
   if (count <= 0 || nseq <= 0) return cudaSuccess;
   if (p.head_dim != 64 || nseq > 65535) return cudaErrorInvalidValue;
   const int threads = 256;
-  const int64_t kv_rows8 = static_cast<int64_t>(count) * p.kv_heads * 8;
-  const int64_t q_rows8 = p.q_rot != nullptr ? static_cast<int64_t>(count) * p.heads * 8 : 0;
-  if (kv_rows8 > INT32_MAX - threads || q_rows8 > INT32_MAX - threads) return cudaErrorInvalidValue;
-  const int kv_blocks = static_cast<int>((kv_rows8 + threads - 1) / threads);
-  const int q_blocks = static_cast<int>((q_rows8 + threads - 1) / threads);
+  const int64_t kv_lanes = static_cast<int64_t>(count) * ((p.kv_heads + kKVGroup - 1) / kKVGroup) * 8;
+  const int64_t q_lanes = p.q_rot != nullptr ? static_cast<int64_t>(count) * ((p.heads + kQGroup - 1) / kQGroup) * 8 : 0;
+  if (kv_lanes > INT32_MAX - threads || q_lanes > INT32_MAX - threads) return cudaErrorInvalidValue;
+  const int kv_blocks = static_cast<int>((kv_lanes + threads - 1) / threads);
+  const int q_blocks = static_cast<int>((q_lanes + threads - 1) / threads);
   k_rope_append<<<dim3(kv_blocks + q_blocks, nseq), threads, 0, st>>>(p, seq_idx, count, kv_blocks);
   return cudaGetLastError();
 }
