@@ -1644,10 +1644,21 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
     p.tmap_k = &c->tmap_k;
     p.tmap_v = &c->tmap_v;
   }
-  // the tensor-core kernels (f16 cache) take their query tiles by TMA from
-  // RoPE(q) rows that the append kernel writes
+  // The tensor-core kernels (f16 cache) take their query tiles by TMA from
+  // RoPE(q) rows that the append kernel writes: the two-tile kernel always,
+  // the one-tile kernel once its CTAs need more than one wave on the SMs (the
+  // later CTAs then find their queries ready; in a single wave its own
+  // staging runs under the append kernel, which the rotated rows would
+  // instead put in front of every CTA's first MMA).
   CUtensorMap qmap;
-  if (c->dtype == B2A_F16 && c->head_dim == 64 && c->has_tmaps) {
+  AttnParams attn = p;   // as the attention kernels see it: the new rows are in the cache
+  attn.k_new = nullptr;
+  attn.v_new = nullptr;
+  const bool rows_ok = c->dtype == B2A_F16 && c->head_dim == 64 && c->has_tmaps;
+  attn.tmap_q = rows_ok ? &qmap : nullptr;   // the map is encoded below, only if it is used
+  bool pair = prefill_pair_supported(attn) && prefill_tiles_per_cta(ctx, count, num_heads * nseq) == 2;
+  const int64_t tc_ctas = static_cast<int64_t>(num_heads) * nseq * ((count + 127) / 128);
+  if (pair || (rows_ok && prefill_tc_supported(attn) && tc_ctas > ctx->sm_count)) {
     const size_t rows = static_cast<size_t>(nseq) * count;
     if ((s = ensure_buffer(&ctx->d_qrot, &ctx->d_qrot_bytes, rows * num_heads * 64 * sizeof(uint16_t),
                            "allocating rotated queries")) != B2A_OK) {
@@ -1656,20 +1667,9 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
     if (encode_query_map(&qmap, ctx->d_qrot, rows, num_heads)) {
       p.q_rot = static_cast<uint16_t*>(ctx->d_qrot);
       p.tmap_q = &qmap;
+    } else {
+      pair = false;   // the one-tile kernel stages its own query tiles
     }
-  }
-  AttnParams attn = p;   // as the attention kernels see it: the new rows are in the cache
-  attn.k_new = nullptr;
-  attn.v_new = nullptr;
-  const bool pair = prefill_pair_supported(attn) && prefill_tiles_per_cta(ctx, count, num_heads * nseq) == 2;
-  // The one-tile kernel takes them too once its CTAs need more than one wave
-  // on the SMs: the later CTAs then find their queries ready. In a single
-  // wave its own staging runs under the append kernel, which the rotated rows
-  // would instead put in front of every CTA's first MMA.
-  const int64_t tc_ctas = static_cast<int64_t>(num_heads) * nseq * ((count + 127) / 128);
-  if (!pair && !(prefill_tc_supported(attn) && c->dtype == B2A_F16 && tc_ctas > ctx->sm_count)) {
-    p.q_rot = nullptr;
-    p.tmap_q = nullptr;
   }
   // RoPE(K) + append first (src/cpu/model.js:116 writes before attending), then
   // causal attention over past+count, with RoPE(Q) done by the append kernel
