@@ -57,36 +57,33 @@ constexpr int kKVGroup = 1;
 // src/cpu/model.js:103-116 (rope-k at absolute position past+t, then
 // kv.writeAt), src/gpu/model.js:327-338 (ROPE on k, two copies), and, for the
 // tensor-core prefill, RoPE(q) (src/cpu/model.js:103-106) as f16 rows.
-// Grid (blocks, sequences); a thread takes 8 dims (lane l: dims 8l..8l+7, 16
-// bytes of a 16-bit row) of one token in a group of heads, so eight
-// neighbouring lanes cover a row (coalesced 16-byte accesses) and lanes l and
-// l ^ 4 hold the two halves of each rotation pair, swapped by shuffle. Blocks
-// [0, kv_blocks) rotate and append K and append V (kKVGroup KV heads per
-// thread); blocks from kv_blocks on (when p.q_rot is set) rotate the queries
-// (kQGroup heads per thread).
+// Grid (token blocks, sequences, head groups); a thread takes 8 dims (lane l:
+// dims 8l..8l+7, 16 bytes of a 16-bit row) of one token in a group of heads,
+// so eight neighbouring lanes cover a row (coalesced 16-byte accesses) and
+// lanes l and l ^ 4 hold the two halves of each rotation pair, swapped by
+// shuffle. Groups z < kv_groups rotate and append K and append V (kKVGroup KV
+// heads per thread); the groups after them (when p.q_rot is set) rotate the
+// queries (kQGroup heads per thread).
 // K: IEEE f64 from the f64 table, every product and sum rounded separately
 // (rope_pair_f64), then the cache dtype. Q: f32 from the f32 table, rounded
 // once to f16, x[d] c - x[d+32] s and x[d+32] c + x[d] s: the arithmetic the
 // prefill kernels' own query staging uses.
-__global__ void __launch_bounds__(256, 4) k_rope_append(AttnParams p, int seq_first, int count, int kv_blocks) {
+__global__ void __launch_bounds__(256, 4) k_rope_append(AttnParams p, int seq_first, int count, int kv_groups) {
   // a kernel launched after this one as a programmatic dependent may start its
   // prologue now; it waits for this grid before reading the cache
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = static_cast<int>(blockIdx.y);
   const int seq_idx = seq_first + b;
   const int past = p.len[seq_idx];
-  const bool kv = static_cast<int>(blockIdx.x) < kv_blocks;
+  // grid z: the KV head groups, then the query head groups
+  const bool kv = static_cast<int>(blockIdx.z) < kv_groups;
   const int heads = kv ? p.kv_heads : p.heads;
-  const int group = kv ? kKVGroup : kQGroup;
-  const int groups = (heads + group - 1) / group;           // head groups per token
-  const int i = (kv ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) - kv_blocks) * blockDim.x +
-                threadIdx.x;
-  const bool live = i < count * groups * 8;
+  const int h0 = (kv ? static_cast<int>(blockIdx.z) : static_cast<int>(blockIdx.z) - kv_groups) * (kv ? kKVGroup : kQGroup);
+  const int i = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;   // 8 lanes per token
+  const bool live = i < count * 8;
   const int ii = live ? i : 0;   // a lane past the end computes token 0 for the shuffles, stores nothing
   const int l = ii & 7;
-  const int slot = ii >> 3;
-  const int t = slot / groups;
-  const int h0 = (slot - t * groups) * group;
+  const int t = ii >> 3;
   const int pos = past + t;
   const int64_t row0 = (static_cast<int64_t>(b) * count + t) * heads;   // (sequence, token) row of head 0
   const int j0 = 8 * (l & 3);                                          // rotation index of the lane's first dim
@@ -148,7 +145,12 @@ __global__ void __launch_bounds__(256, 4) k_rope_append(AttnParams p, int seq_fi
     *reinterpret_cast<float4*>(&c[4]) = *reinterpret_cast<const float4*>(p.rope_cos32 + ra + 4);
     *reinterpret_cast<float4*>(&sn[0]) = *reinterpret_cast<const float4*>(p.rope_sin32 + ra);
     *reinterpret_cast<float4*>(&sn[4]) = *reinterpret_cast<const float4*>(p.rope_sin32 + ra + 4);
-    const float sgn = l < 4 ? -1.f : 1.f;
+    // first half (l < 4): x c - y s, second half: x c + y s, as x c + y (-/+ s)
+    // (a sign flip is exact, so the product rounds as y s would)
+    if (l < 4) {
+#pragma unroll
+      for (int e = 0; e < 8; e++) sn[e] = -sn[e];
+    }
 #pragma unroll
     for (int m = 0; m < kQGroup; m++) {
       uint32_t w[4];
@@ -156,8 +158,7 @@ __global__ void __launch_bounds__(256, 4) k_rope_append(AttnParams p, int seq_fi
       for (int e = 0; e < 8; e += 2) {
         const float y0 = __shfl_xor_sync(0xffffffffu, x[m][e], 4);
         const float y1 = __shfl_xor_sync(0xffffffffu, x[m][e + 1], 4);
-        const __half2 h2 = __floats2half2_rn(fmaf(x[m][e], c[e], sgn * (y0 * sn[e])),
-                                             fmaf(x[m][e + 1], c[e + 1], sgn * (y1 * sn[e + 1])));
+        const __half2 h2 = __floats2half2_rn(fmaf(x[m][e], c[e], y0 * sn[e]), fmaf(x[m][e + 1], c[e + 1], y1 * sn[e + 1]));
         w[e >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
       }
       if (live && h0 + m < heads) {
@@ -171,12 +172,12 @@ cudaError_t launch_rope_append(const AttnParams& p, int seq_idx, int count, cuda
   if (count <= 0 || nseq <= 0) return cudaSuccess;
   if (p.head_dim != 64 || nseq > 65535) return cudaErrorInvalidValue;
   const int threads = 256;
-  const int64_t kv_lanes = static_cast<int64_t>(count) * ((p.kv_heads + kKVGroup - 1) / kKVGroup) * 8;
-  const int64_t q_lanes = p.q_rot != nullptr ? static_cast<int64_t>(count) * ((p.heads + kQGroup - 1) / kQGroup) * 8 : 0;
-  if (kv_lanes > INT32_MAX - threads || q_lanes > INT32_MAX - threads) return cudaErrorInvalidValue;
-  const int kv_blocks = static_cast<int>((kv_lanes + threads - 1) / threads);
-  const int q_blocks = static_cast<int>((q_lanes + threads - 1) / threads);
-  k_rope_append<<<dim3(kv_blocks + q_blocks, nseq), threads, 0, st>>>(p, seq_idx, count, kv_blocks);
+  const int64_t lanes = static_cast<int64_t>(count) * 8;   // per (sequence, head group)
+  if (lanes > INT32_MAX - threads) return cudaErrorInvalidValue;
+  const int kv_groups = (p.kv_heads + kKVGroup - 1) / kKVGroup;
+  const int q_groups = p.q_rot != nullptr ? (p.heads + kQGroup - 1) / kQGroup : 0;
+  const int blocks = static_cast<int>((lanes + threads - 1) / threads);
+  k_rope_append<<<dim3(blocks, nseq, kv_groups + q_groups), threads, 0, st>>>(p, seq_idx, count, kv_groups);
   return cudaGetLastError();
 }
 
