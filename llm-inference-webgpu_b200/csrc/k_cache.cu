@@ -51,7 +51,7 @@ __device__ __forceinline__ void store8(void* base, int64_t at, int dt, const flo
 // Query heads and KV heads one thread covers (the same 8 dims of one token in
 // each): the rotation-table entries are loaded once for all of them, and the
 // rows' loads are all in flight together.
-constexpr int kQGroup = 4;
+constexpr int kQGroup = 2;
 constexpr int kKVGroup = 1;
 
 // src/cpu/model.js:103-116 (rope-k at absolute position past+t, then
@@ -68,7 +68,7 @@ constexpr int kKVGroup = 1;
 // (rope_pair_f64), then the cache dtype. Q: f32 from the f32 table, rounded
 // once to f16, x[d] c - x[d+32] s and x[d+32] c + x[d] s: the arithmetic the
 // prefill kernels' own query staging uses.
-__global__ void __launch_bounds__(256, 4) k_rope_append(AttnParams p, int seq_first, int count, int kv_groups) {
+__global__ void __launch_bounds__(256, 5) k_rope_append(AttnParams p, int seq_first, int count, int kv_groups) {
   // a kernel launched after this one as a programmatic dependent may start its
   // prologue now; it waits for this grid before reading the cache
   asm volatile("griddepcontrol.launch_dependents;");
