@@ -60,6 +60,7 @@ constexpr int kColO = 256;                     // + 64 w
 constexpr int kColP = 384;                     // + 64 w
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units
+constexpr long long kTile1Delay = 800;         // cycles between the two tiles' first S (600-1000 measured alike)
 
 // smem layout (offsets from a 1024-aligned base)
 constexpr int kOffQ = 0;                       // + w * kQBytes
@@ -193,7 +194,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       mbar_wait(&kv_full[0], 0, p.err, dead);
       tc_fence_after();
-      for (int w = 0; w < ntile; w++) issue_s(w, 0);
+      // Tile 1's first S goes in kTile1Delay cycles after tile 0's, so the two
+      // tiles' first exponentials do not collide on the sub-partitions'
+      // exponential units; later steps keep that offset on their own (left to
+      // themselves the tiles start together and settle ~900 cycles apart only
+      // after a few steps). A fixed count of cycles: no wait on anything.
+      issue_s(0, 0);
+      if (ntile > 1) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < kTile1Delay) {
+        }
+        issue_s(1, 0);
+      }
       for (int j = 0; j < n_kv; j++) {
         const int s = j % kStages;
         if (j + 1 < n_kv) mbar_wait(&kv_full[(j + 1) % kStages], ((j + 1) / kStages) & 1, p.err, dead);
