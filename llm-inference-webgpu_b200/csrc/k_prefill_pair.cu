@@ -24,9 +24,11 @@
 //   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1: TMEM lane =
 //               query row, thread r owns row r. Two softmax warps per SM
 //               sub-partition share its exponential unit; with no hand-over
-//               between them the two tiles settle half a KV step apart, so
-//               one tile's TMEM traffic, row max and P store run under the
-//               other's exponentials.
+//               between them the two tiles settle about a third of a KV step
+//               apart (tile 1's first S starts a fixed 800 cycles after tile
+//               0's, so they do not start together), and one tile's TMEM
+//               traffic, row max and P store run under the other's
+//               exponentials.
 // TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
 // P_0 [384,448) P_1 [448,512) (P as packed f16 pairs, separate from S so the
 // next S can be written while P is still being produced or consumed).
