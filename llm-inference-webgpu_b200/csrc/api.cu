@@ -1645,11 +1645,8 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
     p.tmap_v = &c->tmap_v;
   }
   // The tensor-core kernels (f16 cache) take their query tiles by TMA from
-  // RoPE(q) rows that the append kernel writes: the two-tile kernel always,
-  // the one-tile kernel once its CTAs need more than one wave on the SMs (the
-  // later CTAs then find their queries ready; in a single wave its own
-  // staging runs under the append kernel, which the rotated rows would
-  // instead put in front of every CTA's first MMA).
+  // RoPE(q) rows that the append kernel writes (the one-tile kernel with a
+  // bf16 cache stages its own: it splits each query into two bf16 parts).
   CUtensorMap qmap;
   AttnParams attn = p;   // as the attention kernels see it: the new rows are in the cache
   attn.k_new = nullptr;
@@ -1657,8 +1654,7 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
   const bool rows_ok = c->dtype == B2A_F16 && c->head_dim == 64 && c->has_tmaps;
   attn.tmap_q = rows_ok ? &qmap : nullptr;   // the map is encoded below, only if it is used
   bool pair = prefill_pair_supported(attn) && prefill_tiles_per_cta(ctx, count, num_heads * nseq) == 2;
-  const int64_t tc_ctas = static_cast<int64_t>(num_heads) * nseq * ((count + 127) / 128);
-  if (pair || (rows_ok && prefill_tc_supported(attn) && tc_ctas > ctx->sm_count)) {
+  if (pair || (rows_ok && prefill_tc_supported(attn))) {
     const size_t rows = static_cast<size_t>(nseq) * count;
     if ((s = ensure_buffer(&ctx->d_qrot, &ctx->d_qrot_bytes, rows * num_heads * 64 * sizeof(uint16_t),
                            "allocating rotated queries")) != B2A_OK) {
