@@ -186,6 +186,26 @@ bool encode_query_map(CUtensorMap* map, void* q_rot, uint64_t rows, int heads) {
   return r == CUDA_SUCCESS;
 }
 
+// A prefill call's 16-bit output [sequences][tokens][heads * 64] as a 3D
+// tensor; each store is one head's 128-row tile of one sequence, 128-byte
+// swizzled, with the rows past the sequence's tokens clipped.
+bool encode_output_map(CUtensorMap* map, void* out, uint64_t nseq, uint64_t tokens, int heads, int out_dtype) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr || (out_dtype != B2A_F16 && out_dtype != B2A_BF16) || (reinterpret_cast<uintptr_t>(out) & 15) != 0 ||
+      tokens >= (1ull << 32) || nseq >= (1ull << 32)) {
+    return false;
+  }
+  const cuuint64_t row = static_cast<cuuint64_t>(heads) * 128;   // bytes
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(heads) * 64, tokens, nseq};
+  cuuint64_t strides[2] = {row, row * tokens};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, out_dtype == B2A_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out,
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Carves device staging for host-pointer calls: each `add` reserves an
 // aligned slice of ctx->d_stage.
 struct Stage {
@@ -1680,6 +1700,8 @@ b2a_status attn_prefill_device(b2a_ctx* ctx, b2a_kvcache* c, const b2a_rope* rop
   p.v_new = nullptr;
   if (pair) {
     // tensor-core causal attention, two heads' 128-query tiles per CTA (f16 cache)
+    CUtensorMap omap;
+    if (encode_output_map(&omap, dout, nseq, count, num_heads, static_cast<int>(out_dtype))) p.tmap_o = &omap;
     {
       KernelTimer kt(ctx, K_PREFILL_PAIR);
       e = launch_prefill_pair(p, dout, static_cast<int>(out_dtype), ctx->stream);

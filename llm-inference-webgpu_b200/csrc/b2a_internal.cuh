@@ -167,6 +167,9 @@ struct AttnParams {
   // host CUtensorMap* over q_rot as [rows][heads * 64], 128-row boxes).
   uint16_t* q_rot;
   const void* tmap_q;
+  // host CUtensorMap* of a prefill call's 16-bit output as [sequence][token]
+  // [heads * 64] (128-row boxes), or null: the epilogue then stores by thread
+  const void* tmap_o;
   // Fused split-KV merge (tensor-core path): when fuse_out is set, a group
   // whose keys fit one chunk writes its result straight to fuse_out, and the
   // last CTA of every other group merges that group's chunk partials, so no

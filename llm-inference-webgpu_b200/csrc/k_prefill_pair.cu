@@ -69,7 +69,7 @@ constexpr int kOffQ = 0;                       // + w * kQBytes
 constexpr int kOffRing = 2 * kQBytes;
 constexpr int kOffBars = kOffRing + kStages * kStageBytes;
 // kv_full[kStages], kv_empty[kStages], then per tile: s_full, s_free, p_full, pv_done, q_ready
-constexpr int kNumBars = 2 * kStages + 2 * 5;
+constexpr int kNumBars = 2 * kStages + 2 * 5 + 2;   // + out_full[tile]
 constexpr int kSmemTotal = kOffBars + kNumBars * 8 + 16 + 1024;
 
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
@@ -81,7 +81,8 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
 
 __global__ void __launch_bounds__(kThreads, 1)
     k_prefill_pair(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                   const __grid_constant__ CUtensorMap tmap_q, AttnParams p) {
+                   const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_o,
+                   AttnParams p, int tma_out) {
   constexpr uint32_t kIdescS = idesc_f16(0, 0, kBM, kBN);
   constexpr uint32_t kIdescPV = idesc_f16(0, 1, kBM, kD);
 
@@ -96,7 +97,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* q_ready = pv_done + 2;         // the CTA's query tiles are in Q_0 (and Q_1)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 2);
+  uint64_t* out_full = q_ready + 2;        // [tile]: the tile's output rows are in Q_w
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(out_full + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   bool dead = false;   // set once a bounded wait of this thread gave up
@@ -130,6 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     }
     mbar_init(q_ready, 1);
+    mbar_init(&out_full[0], 128);
+    mbar_init(&out_full[1], 128);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -366,7 +370,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_wait_ld();
     tmem_ld_fence(ov[0]);
     tmem_ld_fence(ov[1]);
-    if (t < p.tokens) {
+    if (tma_out) {
+      // 16-bit output: the tile's rows go into Q_w (its S MMAs are all done),
+      // 128-byte swizzled, and leave by one TMA store (rows past the
+      // sequence's tokens are clipped by the map); thread-per-row stores would
+      // touch 32 rows per warp instruction
+      const float inv = 1.f / l;
+      const int odt = p.nchunks;   // the output dtype travels in nchunks
+      unsigned char* orow = smem + kOffQ + w * kQBytes + r * 128;
+#pragma unroll
+      for (int x = 0; x < 8; x++) {
+        uint32_t wd[4];
+#pragma unroll
+        for (int y = 0; y < 4; y++) {
+          const int e = 8 * x + 2 * y;
+          const float f0 = __uint_as_float(ov[e >> 5][e & 31]) * inv;
+          const float f1 = __uint_as_float(ov[e >> 5][(e & 31) + 1]) * inv;
+          const uint32_t b0 = odt == DT_F16 ? f32_to_f16_bits(f0) : f32_to_bf16_bits(f0);
+          const uint32_t b1 = odt == DT_F16 ? f32_to_f16_bits(f1) : f32_to_bf16_bits(f1);
+          wd[y] = b0 | (b1 << 16);
+        }
+        *reinterpret_cast<uint4*>(orow + ((x ^ (r & 7)) << 4)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&out_full[w]);
+      if (r == 0) {
+        mbar_wait(&out_full[w], 0, p.err, dead);
+        if (!dead) {
+          asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                           reinterpret_cast<uint64_t>(&tmap_o)),
+                       "r"(smem_u32(smem + kOffQ + w * kQBytes)), "r"(h * kD), "r"(q0), "r"(sb)
+                       : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          // the shared rows must stay until the store has read them
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        }
+      }
+    } else if (t < p.tokens) {
       const float inv = 1.f / l;
       const int64_t orow = ((static_cast<int64_t>(sb) * p.tokens + t) * p.heads + h) * kD;
       void* out = p.partial;       // the output pointer travels in the partial slot for this kernel
@@ -446,8 +486,13 @@ cudaError_t launch_prefill_pair(const AttnParams& p, void* out, int out_dtype, c
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  // 16-bit output with a map: the epilogue's TMA store
+  const int tma_out = p.tmap_o != nullptr && (out_dtype == DT_F16 || out_dtype == DT_BF16) ? 1 : 0;
+  CUtensorMap omap = {};
+  if (tma_out) omap = *static_cast<const CUtensorMap*>(p.tmap_o);
   return cudaLaunchKernelEx(&cfg, k_prefill_pair, *static_cast<const CUtensorMap*>(p.tmap_k),
-                            *static_cast<const CUtensorMap*>(p.tmap_v), *static_cast<const CUtensorMap*>(p.tmap_q), q);
+                            *static_cast<const CUtensorMap*>(p.tmap_v), *static_cast<const CUtensorMap*>(p.tmap_q), omap,
+                            q, tma_out);
 }
 
 }  // namespace b2a
