@@ -176,3 +176,43 @@ def test_batched_prefill_more_units_than_sms(ctx, rope, oracle, monkeypatch, in_
         assert_parity(ob[i].reshape(-1), ref, "f32", f"{in_dtype} batched prefill over many units, sequence {i}")
     cb.close()
     cs.close()
+
+
+@pytest.mark.parametrize("tiles", ["1", "2"])
+def test_rotated_queries_from_unaligned_and_f32_rows(ctx, rope, oracle, monkeypatch, tiles):
+    """With an f16 cache the append kernel rotates the queries for the
+    tensor-core kernels: 16-byte-aligned 16-bit rows by vector loads, rows one
+    element off that alignment and f32 rows by other loads. The values are the
+    same bf16 numbers in all three, and the rotation rounds to f16 once either
+    way, so all three must give the same output bits (and the oracle's
+    attention within the tolerance)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    monkeypatch.setenv("B2A_PREFILL_TILES", tiles)
+    count = 300
+    cfg = b2a.CacheConfig(numLayers=1, numKVHeads=KVH, headDim=D, numHeads=H)
+    q = oracle.round_to(oracle.normal_array(count * H * D, 121), "bf16").reshape(count, H * D)
+    k = oracle.round_to(oracle.normal_array(count * KVH * D, 122), "bf16").reshape(count, KVH * D)
+    v = oracle.round_to(oracle.normal_array(count * KVH * D, 123), "bf16").reshape(count, KVH * D)
+
+    def dev_rows(a, tdt, offset):
+        flat = torch.zeros(a.size + offset, dtype=tdt, device=dev)
+        flat[offset:] = torch.as_tensor(a.reshape(-1).astype(np.float32)).to(tdt).to(dev)
+        return flat[offset:].view(a.shape)
+
+    outs = []
+    for tdt, offset in ((torch.bfloat16, 0), (torch.bfloat16, 1), (torch.float32, 0)):
+        c = b2a.GpuKVCache(ctx, cfg, count, batch=1, dtype="f16")
+        qt, kt, vt = dev_rows(q, tdt, offset), dev_rows(k, tdt, offset), dev_rows(v, tdt, offset)
+        assert (qt.data_ptr() % 16 == 0) == (offset == 0)
+        out = torch.empty(count, H * D, device=dev)
+        b2a.attentionPrefill(ctx, c, rope, 0, qt, kt, vt, out, count, H)
+        torch.cuda.synchronize(dev)
+        outs.append(out.cpu().numpy())
+        c.close()
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32)), "unaligned 16-bit rows differ"
+    assert np.array_equal(outs[0].view(np.uint32), outs[2].view(np.uint32)), "f32 rows differ"
+    qr = oracle.rope_rows(q, range(count), D, THETA).reshape(-1)
+    kr = oracle.round_to(oracle.rope_rows(k, range(count), D, THETA), "f16")
+    ref = oracle.grouped_attention(qr, kr.reshape(-1), oracle.round_to(v, "f16").reshape(-1), count, 0, H, KVH, D)
+    assert_parity(outs[0].reshape(-1), ref, "f32", f"prefill with rotated queries, {tiles} tile(s) per CTA")
