@@ -22,9 +22,10 @@
 // the Q tile (and its residual) into swizzled shared memory themselves. Both
 // rotate in f32 and round the operand to 16 bits next.
 // The kernel is launched as a programmatic dependent of the RoPE(K) + append
-// kernel before it: everything up to the first K/V load (barriers, TMEM, the
-// Q tile) overlaps that kernel, and the producer waits on the grid dependency
-// before its first TMA load of the cache.
+// kernel before it: barriers, TMEM allocation (and, with a bf16 cache, the Q
+// staging) overlap that kernel, and the producer waits on the grid dependency
+// before its first TMA load (the rotated Q tile with an f16 cache, then the
+// cache).
 // With a bf16 cache the rotated query and P are each split into a bf16 high
 // part and a bf16 residual (two MMAs each): a single bf16 rounding of either
 // puts the output about 5e-3 off the f32 reference, the split keeps it ~1e-6.
